@@ -1,0 +1,211 @@
+/*
+ * wiretorch_b200 — the C ABI of the B200 engine for wiretorch's conductance-based LIF
+ * simulation step.
+ *
+ * Every entry point takes plain device pointers and sizes (in the structures below) and
+ * a CUDA stream, enqueues its kernels on that stream and returns at once: 0 on success,
+ * a nonzero WT_ERR_* code if the arguments are inconsistent or a launch failed. None
+ * allocates memory (the caller passes every buffer, sized with wt_workspace_bytes) and
+ * none synchronises. Errors met by the kernels themselves — a grid barrier that timed
+ * out, an event list or fixed-point accumulator that overflowed — are written to the
+ * device word `err` of the workspace, which the caller reads after the stream has
+ * synchronised. wt_last_error() describes the last host-side failure of this thread.
+ *
+ * Layouts (row-major, contiguous): state v (B, N); conductances g (B, 2, S, N), i.e.
+ * per trial, component (rise, decay) and synapse channel, contiguous over neurons;
+ * refractory counters (B, N) int32; adaptation (B, N); presynaptic gating (B, R);
+ * input x (B, T, n_in); spikes (B, T, N) float32.
+ *
+ * The reference (rory-bedford/wiretorch) is pure Python with Triton kernels and binds
+ * no foreign functions; each entry point names the Python/Triton function of the
+ * reference whose work it replaces, and INTEGRATION.md shows the ctypes binding.
+ */
+#ifndef WIRETORCH_B200_H
+#define WIRETORCH_B200_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define WT_MAX_CHANNELS 8 /* synapse channels a neuron carries in the fast kernels */
+#define WT_CHUNK_EDGES 128 /* edges of one scatter work item */
+
+enum {
+    WT_OK = 0,
+    WT_ERR_ARGS = 1,        /* inconsistent sizes or missing buffers */
+    WT_ERR_LAUNCH = 2,      /* a kernel launch failed (see wt_last_error) */
+    WT_ERR_BARRIER = 3,     /* device: a grid barrier gave up waiting */
+    WT_ERR_EVENTS = 4,      /* device: an event list overflowed its capacity */
+    WT_ERR_FIXED_POINT = 5, /* device: a synaptic input exceeded the fixed-point range */
+    WT_ERR_UNSUPPORTED = 6, /* a combination the kernels do not implement */
+};
+
+/* Feature flags of a forward run (WtForward.flags). */
+enum {
+    WT_F_REFRACTORY = 1 << 0, /* n_ref / counter are used */
+    WT_F_MG_BLOCK = 1 << 1,   /* some channel has a voltage-dependent Mg block */
+    WT_F_ADAPT = 1 << 2,      /* adaptation conductance */
+    WT_F_SAMPLE = 1 << 3,     /* escape-noise spikes: noise < sigmoid(k (v - theta)) */
+    WT_F_GATED = 1 << 4,      /* presynaptic gating (short-term plasticity, saturation) */
+    WT_F_SAVE = 1 << 5,       /* save what the backward pass needs */
+    WT_F_TRACK = 1 << 6,      /* per-step v, currents, conductances */
+    WT_F_PROB = 1 << 7,       /* escape-noise probabilities output */
+    WT_F_SAVE_INPUT = 1 << 8, /* save each step's synaptic input X (learnt decay/jump) */
+};
+
+/* The network as the kernels see it (built once per network and per call from the
+ * reference's Drive and Physiology; see wiretorch_b200/plan.py). */
+typedef struct {
+    int32_t B, N, n_in;  /* trials, neurons, input columns */
+    int32_t S, C;        /* synapse channels carried per neuron, input channels */
+    /* per neuron (N) */
+    const float *theta, *U_reset, *E_L, *C_m, *beta;
+    const int32_t *n_ref;                       /* WT_F_REFRACTORY */
+    const float *adapt, *adapt_decay, *E_adapt; /* WT_F_ADAPT */
+    /* per channel (S): decays and jumps of the rise (r) and decay (d) components */
+    float decay_r[WT_MAX_CHANNELS], decay_d[WT_MAX_CHANNELS];
+    float jump_r[WT_MAX_CHANNELS], jump_d[WT_MAX_CHANNELS];
+    float E_syn[WT_MAX_CHANNELS], g_clip[WT_MAX_CHANNELS];
+    float mg_a[WT_MAX_CHANNELS], mg_lc[WT_MAX_CHANNELS]; /* block: sigmoid(mg_a v - mg_lc) */
+    int32_t input_of[WT_MAX_CHANNELS]; /* input channel feeding each channel, -1: none */
+    float fx_inv[WT_MAX_CHANNELS];     /* per input channel: 2^-s of its fixed point */
+    float dt, surr_scale;
+    /* connectivity: sources are the N neurons then the n_in input columns; each source
+     * owns slots (one per pathway it belongs to), each slot chunks of at most
+     * WT_CHUNK_EDGES edges of its CSR row (a chunk is one work item) */
+    const int32_t *src_slot;    /* (N + n_in + 1) */
+    const int32_t *slot_chunk;  /* (n_slots + 1) */
+    const int64_t *chunk_begin; /* (n_chunks): first edge */
+    const int32_t *chunk_len;   /* (n_chunks): edges, at most WT_CHUNK_EDGES */
+    const uint32_t *edge_col;   /* (E): target | input channel << 27 */
+    const float *edge_w;        /* (E): folded weight, times 2^s of its channel */
+    int32_t n_slots, n_chunks;
+    /* presynaptic gating (WT_F_GATED): per slot its gate (-1: none) and row */
+    const int32_t *slot_gate, *slot_row;
+    const float *gate_params;   /* (n_gates, 5): c, d, U, d_D, d_F */
+    const int32_t *gate_cols;   /* (n_gates, 4): u column (-1: no STP), n rows,
+                                   saturation column (-1: none), saved-factor column */
+    int32_t R, R_f;             /* gating columns, saved-factor columns */
+} WtNet;
+
+/* Buffers of one forward run of T steps (outputs indexed by step t0 + t of a chunk of
+ * T_total steps, so a chunk may be run in several launches). */
+typedef struct {
+    int32_t T, T_total, t0, flags;
+    float *v, *g;               /* state, updated in place */
+    int32_t *counter;           /* WT_F_REFRACTORY */
+    float *g_a;                 /* WT_F_ADAPT */
+    float *gating;              /* WT_F_GATED: (B, R) */
+    const float *x;             /* (B, T_total, n_in) */
+    const float *noise;         /* WT_F_SAMPLE: (B, T_total, N) uniform */
+    float *spikes;              /* (B, T_total, N) */
+    float *prob;                /* WT_F_PROB */
+    /* WT_F_SAVE: v entering each step (B, T, N); summed conductances (B, T, S, N);
+     * spike and refractory bits (B, T, ceil(N / 32)); adaptation (B, T, N); gating
+     * factors (B, T, R_f); WT_F_SAVE_INPUT: input (B, T, C, N) */
+    float *v_saved, *G_saved;
+    uint32_t *spike_bits, *held_bits;
+    float *a_saved, *f_saved, *X_saved;
+    /* WT_F_TRACK: trial track_b (-1: all) — v (Bt, T_total, N), currents
+     * (Bt, T_total, N, S + 1), conductances (Bt, T_total, N, 2, S), adaptation */
+    float *track_v, *track_I, *track_g, *track_a;
+    int32_t track_b;
+} WtForward;
+
+/* Scratch memory of a forward run; all of it device memory the caller allocated. */
+typedef struct {
+    unsigned long long *X;      /* (2, C, B, N) fixed-point input accumulators */
+    uint32_t *ev_item;          /* (2, ev_cap) event items: trial * n_chunks + chunk */
+    float *ev_amp;              /* (2, ev_cap) */
+    uint32_t *ev_count;         /* (T + 1) */
+    uint32_t *barrier;          /* (64) */
+    int32_t *err;               /* (1): a device error code, 0 if none */
+    int64_t ev_cap;
+} WtWorkspace;
+
+/* Bytes of each workspace buffer for a run of T steps (X, ev_item, ev_amp, ev_count,
+ * barrier, err), written to bytes[0..5]. */
+int wt_workspace_bytes(const WtNet *net, int32_t T, int64_t bytes[6]);
+
+/* Fold the per-edge weights: edge_w[e] = w[e] * scale[k(e), col(e)] * jf[k(e), c(e)] *
+ * 2^s(c(e)) for every edge of every chunk, from the raw weights w and the pathway of each
+ * chunk. Replaces the per-call kernel scale of the reference's Drive
+ * (network_simulators/network.py:816-854 `_drive`, conductance/dynamics.py:95-100
+ * `jumps`). */
+int wt_fold_weights(const WtNet *net, const float *w_raw, const int32_t *chunk_path,
+                    const float *scale /* (K, N) */, const float *jf /* (K, C) */,
+                    const float *fx_scale /* (C) */, float *edge_w_out, void *stream);
+
+/* Simulate T steps: one persistent kernel. Replaces the reference's per-step launches
+ * of `compact_spikes` + `recurrent_step` (network_simulators/kernels.py:132-204,
+ * conductance/kernels.py:571-700, driven by conductance/engine.py:306-355 `_recurrent`)
+ * and its feedforward scan `scan_forward` (conductance/kernels.py:158-289, driven by
+ * conductance/engine.py:285-303 `_scan`). */
+int wt_forward(const WtNet *net, const WtForward *run, const WtWorkspace *ws, void *stream);
+
+/* Gradients wanted by a backward pass (WtBackward.wants): the physiology, in the order
+ * of the reference's PHYSIOLOGY (conductance/engine.py:190-193). */
+enum {
+    WT_W_THETA = 1 << 0, WT_W_RESET = 1 << 1, WT_W_E_L = 1 << 2, WT_W_C_M = 1 << 3,
+    WT_W_BETA = 1 << 4, WT_W_E_SYN = 1 << 5, WT_W_DECAY = 1 << 6, WT_W_JUMP = 1 << 7,
+    WT_W_ADAPT = 1 << 8, WT_W_ADAPT_DECAY = 1 << 9, WT_W_E_ADAPT = 1 << 10,
+};
+
+/* One reverse scan over the T steps of a forward run saved with WT_F_SAVE (flags as
+ * that run's). Per (trial, neuron): the adjoint of each input channel at every step,
+ * Q (B, T, C, N) — dL/dX, what a unit of input of that channel at that step is worth —
+ * and per-(trial, neuron) partial sums of the physiology gradients wanted: theta,
+ * U_reset, E_L, C_m, beta, adapt, adapt_decay, E_adapt (B, N) each; E_syn (B, S, N);
+ * decay and jump (B, 2, S, N). grad_spikes (B, T, N) is dL/d(spike), grad_prob
+ * dL/d(probability) with WT_F_PROB. g_init (B, 2, S, N), the conductances entering the
+ * run, and the saved input X (WT_F_SAVE_INPUT) are read for decay and jump. */
+typedef struct {
+    int32_t T, flags, wants;
+    const float *grad_spikes, *grad_prob;
+    const float *v_saved, *G_saved, *a_saved, *X_saved, *g_init;
+    const uint32_t *spike_bits, *held_bits;
+    float *Q;
+    float *g_theta, *g_reset, *g_E_L, *g_C_m, *g_beta, *g_E_syn, *g_decay, *g_jump;
+    float *g_adapt, *g_adapt_decay, *g_E_adapt;
+} WtBackward;
+
+/* Gradients carried along the connectome's edges, from the adjoints Q of a reverse scan:
+ * for every event of the run (a recurrent spike, from the saved spike bits, or a
+ * non-zero input x) and every edge e of its slot (pathway k, target n, input channel c),
+ * with a = the event's value times its gating factor:
+ *   g_scale[k, n] += a * w[e] * jf[k, c] * Q[b, t, c, n]      (B-summed, float64)
+ *   g_w[e]        += a * scale[k, n] * jf[k, c] * Q[b, t, c, n] (float64)
+ * and, for every input column i, trial and step, whether or not it fired,
+ *   g_x[b, t, i] = sum over i's slots of f * sum_e w[e] scale[k, n] jf[k, c] Q[b, t, c, n]. */
+typedef struct {
+    int32_t T;
+    const uint32_t *spike_bits;  /* (B, T, ceil(N / 32)) */
+    const float *x, *f_saved, *Q;
+    const float *w_raw, *scale, *jf;
+    const int32_t *chunk_path;
+    double *g_scale;             /* (K, N) or NULL */
+    double *g_w;                 /* (E) or NULL */
+    float *g_x;                  /* (B, T, n_in) or NULL */
+} WtEdgeGrads;
+
+/* The reverse scan. Replaces `scan_backward` (conductance/kernels.py:382-568, driven by
+ * conductance/engine.py:358-383 `_backward`). */
+int wt_backward(const WtNet *net, const WtBackward *bwd, void *stream);
+
+/* The edge gradients. Replaces the scale partials of `scan_backward`, the weight
+ * gradient `weight_gradient` (network_simulators/engine.py:327-350) and the input
+ * gradient of `_SparseActivations.backward` (network_simulators/engine.py:96-116). */
+int wt_edge_grads(const WtNet *net, const WtEdgeGrads *eg, void *stream);
+
+/* Reading back: a static description of the last host-side error on this thread. */
+const char *wt_last_error(void);
+
+/* The version of this ABI. */
+int wt_abi_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

@@ -151,8 +151,8 @@ class Network:
                      "decay", "jump", "adapt", "adapt_decay", "E_adapt", "mg_c", "mg_a"):  # fmt: skip
             setattr(net, name, _ptr(arr(name), _f))
         net.n_ref = _ptr(arr("n_ref", np.int32), _i32)
-        net.dt = float(_np(p.dt))
-        net.surr_scale = float(_np(p.surr_scale))
+        net.dt = float(np.asarray(_np(p.dt)).reshape(-1)[0])
+        net.surr_scale = float(np.asarray(_np(p.surr_scale)).reshape(-1)[0])
         net.sample = int(p.spike_mode == "sample")
         net.R = R
         self.net = net

@@ -1,0 +1,75 @@
+"""The lockstep comparison of the engine with the oracle, shared by the GPU tests and
+``__graft_entry__.smoke``.
+
+The oracle runs the whole input, recording its state every ``window`` steps; the engine
+restarts from each recorded state and runs the window. Spikes must match exactly, except
+a neuron whose voltage entering the step was within ``margin`` mV of threshold (either
+outcome is a legitimate rounding of the same equations; that trial's window is then
+excused); voltages and conductances must match to the tolerances given. This is the
+reference suite's own definition of "the same simulator" (its tests/test_lockstep.py).
+"""
+
+from __future__ import annotations
+
+import numpy as np
+import torch
+
+
+def oracle_windows(net, x, v, g, kw, window):
+    """The oracle's free run in windows: per-window entering states and outputs."""
+    states = {"v": [], "g": [], **{k: [] for k in kw}}
+    spikes, v_track = [], []
+    v = v.detach().cpu().numpy()
+    g = g.detach().cpu().numpy()
+    kw = {k: val.detach().cpu().numpy() for k, val in kw.items()}
+    x = x.detach().cpu().numpy()
+    for start in range(0, x.shape[1], window):
+        for key, value in (("v", v), ("g", g), *kw.items()):
+            states[key].append(np.array(value))
+        out = net.simulate(x[:, start : start + window], v, g, **kw)
+        spikes.append(out["spikes"])
+        v_track.append(out["v_track"])
+        v, g = out["v"], out["g"]
+        kw = {k: (out[k] if out[k] is not None else kw[k]) for k in kw}
+    for key, value in (("v", v), ("g", g), *kw.items()):
+        states[key].append(np.array(value))
+    return states, np.concatenate(spikes, 1), np.concatenate(v_track, 1)
+
+
+def compare(engine_sim, net, drive, p, x, v, g, kw, window=10, margin=1e-3, v_atol=2e-4,
+            g_rtol=1e-5, g_atol=1e-6):  # fmt: skip
+    """Lockstep of ``engine_sim(v, g, x_window, kw) -> Run`` against the oracle.
+
+    Returns ``(excused, trial_windows, worst_dv, worst_dg)``; raises AssertionError on a
+    flip away from threshold or a trace outside tolerance."""
+    states, spikes, v_track = oracle_windows(net, x, v, g, kw, window)
+    theta = p.theta.detach().cpu().numpy()
+    dev = x.device
+    B = x.shape[0]
+    excused, worst_dv, worst_dg = 0, 0.0, 0.0
+    for w, start in enumerate(range(0, x.shape[1], window)):
+        stop = start + window
+        t = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(dev)  # noqa: E731
+        kw_w = {k: t(states[k][w]) for k in kw}
+        run = engine_sim(t(states["v"][w]), t(states["g"][w]), x[:, start:stop], kw_w)
+        got = run.output.detach().cpu().numpy() > 0.5
+        ok = np.ones(B, bool)
+        diff = got != spikes[:, start:stop]
+        if diff.any():
+            v_enter = np.concatenate([states["v"][w][:, None], v_track[:, start : stop - 1]], 1)
+            for b, tt, n in zip(*np.nonzero(diff)):
+                if ok[b]:
+                    m = abs(v_enter[b, tt, n] - theta[n])
+                    assert m < margin, f"window {w} step {start + tt} trial {b} neuron {n}: flip {m:.2e} mV from threshold"
+                    ok[b] = False
+                    excused += 1
+        vt = run.tracked["v"].detach().cpu().numpy()
+        dv = np.abs(vt[ok] - v_track[ok, start:stop]).max(initial=0.0)
+        assert dv <= v_atol, f"window {w}: voltage differs by {dv:.2e} mV"
+        gk = run.syn.detach().cpu().numpy()
+        ref = states["g"][w + 1]
+        err = np.abs(gk[ok] - ref[ok]) - (g_atol + g_rtol * np.abs(ref[ok]))
+        assert err.max(initial=-1.0) <= 0, f"window {w}: conductances differ by {np.abs(gk[ok]-ref[ok]).max():.2e}"
+        worst_dv = max(worst_dv, float(dv))
+        worst_dg = max(worst_dg, float(np.abs(gk[ok] - ref[ok]).max(initial=0.0)))
+    return excused, B * (x.shape[1] // window), worst_dv, worst_dg

@@ -1,0 +1,114 @@
+"""The engine's host-side tables (``wiretorch_b200.plan``) describe the reference's drive.
+
+Built on the CPU from the golden cases' ``Drive``s, the slots, chunks and folded edges
+must reproduce, for any set of active sources, every channel's input exactly as the
+reference computes it: ``sum_k made_k * scale_k * (pre_k @ W_k)`` per synapse type
+(``conductance/dynamics.py:95-100, 204-208``). No GPU involved: the chunks are walked
+in Python.
+"""
+
+import numpy as np
+import pytest
+import torch
+
+import golden_io
+from wiretorch_b200 import plan as P
+from wiretorch_b200._lib import CHUNK_EDGES
+
+
+def _walk(plan, pre_rec, pre_ff):
+    """Input channels of one trial from the plan's tables: (C, N) float64."""
+    t = plan.tensors
+    N = plan.N
+    X = np.zeros((plan.ch.C, N))
+    src_slot = t["src_slot"].numpy()
+    slot_chunk = t["slot_chunk"].numpy()
+    begin, length = t["chunk_begin"].numpy(), t["chunk_len"].numpy()
+    cols = t["edge_col"].numpy().astype(np.int64) & 0xFFFFFFFF
+    w = t["edge_w"].numpy().astype(np.float64)
+    values = np.concatenate([pre_rec, pre_ff])
+    for j in np.nonzero(values)[0]:
+        for slot in range(src_slot[j], src_slot[j + 1]):
+            for chunk in range(slot_chunk[slot], slot_chunk[slot + 1]):
+                assert 0 < length[chunk] <= CHUNK_EDGES
+                e = slice(begin[chunk], begin[chunk] + length[chunk])
+                np.add.at(X, (cols[e] >> 27, cols[e] & 0x7FFFFFF), values[j] * w[e])
+    return X / np.asarray(plan.fx_scale.double())[:, None]
+
+
+def _reference_input(drive, p, pre_rec, pre_ff):
+    """Per synapse type s: sum_k made[k, s] * jump_d[s] * scale_k * (pre_k @ W_k)."""
+    made = drive.made.numpy()
+    scale = drive.scale.double().numpy()
+    jd = p.jump[1].double().numpy()
+    N, S = scale.shape[1], made.shape[1]
+    out = np.zeros((S, N))
+    paths = [(r, W, pre_rec) for r, W in drive.recurrent]
+    paths += [(r, W, pre_ff) for r, W in drive.feedforward]
+    for k, (rows, W, pre) in enumerate(paths):
+        a = pre[rows.numpy()] @ W.double().numpy()
+        for s in range(S):
+            if made[k, s]:
+                out[s] += jd[s] * scale[k] * a
+    return out
+
+
+@pytest.mark.parametrize("pool", [False, True])
+@pytest.mark.parametrize("name", ["recurrent_scaling_factors", "feedforward_learnt_weights",
+                                  "recurrent_stp", "recurrent_saturation"])  # fmt: skip
+def test_plan_reproduces_the_drive(name, pool):
+    drive, p, d, meta = golden_io.load(name)
+    n_in = d["in.x"].shape[2]
+    plan = P.build(drive, p, 2, n_in, "cpu", pool=pool)
+    P.fold(plan, drive.scale)
+    rng = np.random.default_rng(0)
+    N = plan.N
+    pre_rec = (rng.random(N) < 0.2).astype(np.float64)
+    pre_ff = rng.random(n_in) * (rng.random(n_in) < 0.3)
+    X = _walk(plan, pre_rec, pre_ff)
+    expected = _reference_input(drive, p, pre_rec, pre_ff)
+    ch = plan.ch
+    for c, members in enumerate(ch.member):
+        total = sum(expected[s] for s in members)
+        if ch.input_of[c] < 0:
+            assert np.abs(total).max() == 0
+            continue
+        # channel c's decay component receives jump_d * X
+        got = ch.jump_d[c] * X[ch.input_of[c]]
+        np.testing.assert_allclose(got, total, rtol=1e-6, atol=1e-9)
+
+
+def test_pooling_merges_identical_types():
+    """Two source cell types whose synapse types share every dynamic parameter pool
+    into one channel; distinct ones stay apart."""
+    drive, p, d, meta = golden_io.load("recurrent_frozen")
+    exact = P.build(drive, p, 2, d["in.x"].shape[2], "cpu", pool=False)
+    assert exact.ch.Sp == drive.made.shape[1]
+    pooled = P.build(drive, p, 2, d["in.x"].shape[2], "cpu", pool=True)
+    assert pooled.ch.Sp <= exact.ch.Sp
+    for members in pooled.ch.member:
+        keys = {(float(p.decay[0, s]), float(p.decay[1, s]), float(p.E_syn[s])) for s in members}
+        assert len(keys) == 1
+
+
+def test_chunks_split_long_rows():
+    """A source with more than CHUNK_EDGES targets gets several chunks, each at most
+    CHUNK_EDGES long, covering its row once."""
+    from wiretorch_b200.types import Drive, Physiology
+
+    N = 700
+    W = torch.zeros(3, N)
+    W[0] = 1.0
+    W[1, :5] = 2.0
+    drive = Drive(made=torch.ones(1, 1, dtype=torch.bool), scale=torch.ones(1, N),
+                  recurrent=[(torch.tensor([0, 3, 9]), W)])  # fmt: skip
+    one = torch.ones(N)
+    p = Physiology(theta=one, U_reset=one, E_L=one, C_m=one, beta=one * 0.5,
+                   E_syn=torch.zeros(1), g_clip=torch.full((1,), float("inf")),
+                   decay=torch.full((2, 1), 0.5), jump=torch.tensor([[-1.0], [1.0]]),
+                   dt=torch.tensor(1.0), surr_scale=torch.tensor(1.0))  # fmt: skip
+    plan = P.build(drive, p, 1, 0, "cpu")
+    t = plan.tensors
+    assert plan.n_chunks == -(-N // CHUNK_EDGES) + 1
+    lens = t["chunk_len"][t["slot_chunk"][0] : t["slot_chunk"][1]]
+    assert int(lens.sum()) == N and int(lens.max()) <= CHUNK_EDGES

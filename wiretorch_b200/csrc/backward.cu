@@ -1,0 +1,370 @@
+// The backward pass when gradients do not flow through the recurrent spikes (the
+// reference's default for conductance-based networks): the recurrent input is then input
+// like any other, every (trial, neuron) is independent, and the adjoint of the whole run
+// is one reverse scan per (trial, neuron) — the adjoint of conductance/dynamics.py's
+// time step, as the reference's scan_backward (conductance/kernels.py:382-568) computes
+// it. Then wt_edge_grads carries each step's input adjoint Q back along the edges to
+// the kernel scales, the weights and the input.
+//
+// Reverse step t, with lv = dL/dv after the step, l_r, l_d = dL/dg after it:
+//   Q_c      = sum over channels fed by c of  jump_r l_r + jump_d l_d     (dL/dX_t)
+//   membrane adjoint of v' = (v - phi J)(1 - r) + U r  (exponential Euler, r = reset)
+//     gives dL/dv and dL/dG of each clipped, Mg-blocked conductance, and the
+//     physiology terms; then the spike's surrogate term is added to dL/dv.
+//   l_r = decay_r l_r + dL/dG ;  l_d = decay_d l_d + dL/dG
+// The decays' gradient sum_t l_t g_t needs no saved conductances per component: with
+// H_{t-1} = l_t + decay H_t it is sum_t jump X_t H_t + g_init H_{-1}.
+#include "common.cuh"
+
+namespace wt {
+namespace {
+
+struct BwdTables {
+    float dr[WT_MAX_CHANNELS], dd[WT_MAX_CHANNELS], jr[WT_MAX_CHANNELS], jd[WT_MAX_CHANNELS];
+    float E[WT_MAX_CHANNELS], clip[WT_MAX_CHANNELS], mga[WT_MAX_CHANNELS], mglc[WT_MAX_CHANNELS];
+    int in[WT_MAX_CHANNELS];
+};
+
+template <int S, bool SYN>
+__global__ void __launch_bounds__(kBlock) backward_kernel(const WtNet net, const WtBackward bw) {
+    __shared__ BwdTables tab;
+    if (threadIdx.x < WT_MAX_CHANNELS) {
+        const int c = threadIdx.x;
+        tab.dr[c] = net.decay_r[c];
+        tab.dd[c] = net.decay_d[c];
+        tab.jr[c] = net.jump_r[c];
+        tab.jd[c] = net.jump_d[c];
+        tab.E[c] = net.E_syn[c];
+        tab.clip[c] = net.g_clip[c];
+        tab.mga[c] = net.mg_a[c];
+        tab.mglc[c] = net.mg_lc[c];
+        tab.in[c] = net.input_of[c];
+    }
+    __syncthreads();
+    const int N = net.N, C = net.C, T = bw.T;
+    const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= (long long)net.B * N) return;
+    const int b = (int)(i / N), n = (int)(i % N);
+    const int flags = bw.flags, wants = bw.wants;
+    const bool REF = flags & WT_F_REFRACTORY, MG = flags & WT_F_MG_BLOCK, ADAPT = flags & WT_F_ADAPT;
+    const bool SAMPLE = flags & WT_F_SAMPLE, PROB = flags & WT_F_PROB;
+    const int words = (N + 31) >> 5;
+    const float dt = net.dt, k = net.surr_scale;
+
+    const float theta = net.theta[n], E_L = net.E_L[n], Cm = net.C_m[n], beta = net.beta[n];
+    const float rate = -log1pf(beta - 1.0f) / dt;
+    const float g_L = Cm * rate, inv_C = 1.0f / Cm;
+    const float a_decay = ADAPT ? net.adapt_decay[n] : 0.0f;
+    const float E_a = ADAPT ? net.E_adapt[n] : 0.0f;
+
+    float dv = 0.0f, la = 0.0f;
+    float lr[S], ld[S];
+    float acc_E[SYN ? S : 1], acc_dr[SYN ? S : 1], acc_dd[SYN ? S : 1], acc_jr[SYN ? S : 1],
+        acc_jd[SYN ? S : 1], H_r[SYN ? S : 1], H_d[SYN ? S : 1];
+#pragma unroll
+    for (int c = 0; c < S; c++) lr[c] = ld[c] = 0.0f;
+    if (SYN) {
+#pragma unroll
+        for (int c = 0; c < S; c++) acc_E[c] = acc_dr[c] = acc_dd[c] = acc_jr[c] = acc_jd[c] = H_r[c] = H_d[c] = 0.0f;
+    }
+    float acc_theta = 0.0f, acc_reset = 0.0f, acc_E_L = 0.0f, acc_C_m = 0.0f, acc_beta = 0.0f;
+    float acc_adapt = 0.0f, acc_adapt_decay = 0.0f, acc_E_a = 0.0f;
+
+    for (int t = T - 1; t >= 0; t--) {
+        const size_t o = ((size_t)b * T + t) * N + n;
+        const float v = bw.v_saved[o];
+        const size_t wd = ((size_t)b * T + t) * words + (n >> 5);
+        const float s = (bw.spike_bits[wd] >> (n & 31)) & 1u ? 1.0f : 0.0f;
+        const float held = (REF && ((bw.held_bits[wd] >> (n & 31)) & 1u)) ? 1.0f : 0.0f;
+        const float r = fmaxf(s, held);
+        float G[S];
+        const float *Gs = bw.G_saved + ((size_t)b * T + t) * S * N + n;
+#pragma unroll
+        for (int c = 0; c < S; c++) G[c] = Gs[(size_t)c * N];
+
+        // The input of step t entered the state step t + 1 saw: its adjoint.
+        float *Qt = bw.Q + ((size_t)b * T + t) * C * N + n;
+        for (int c = 0; c < C; c++) {
+            float q = 0.0f;
+#pragma unroll
+            for (int j = 0; j < S; j++)
+                if (tab.in[j] == c) q = q + (tab.jr[j] * lr[j] + tab.jd[j] * ld[j]);
+            Qt[(size_t)c * N] = q;
+        }
+        if (SYN && (wants & (WT_W_DECAY | WT_W_JUMP))) {
+            const float *Xt = bw.X_saved + ((size_t)b * T + t) * C * N + n;
+#pragma unroll
+            for (int c = 0; c < S; c++) {
+                const float base = tab.in[c] >= 0 ? Xt[(size_t)tab.in[c] * N] : 0.0f;
+                if (wants & WT_W_JUMP) {
+                    acc_jr[c] += lr[c] * base;
+                    acc_jd[c] += ld[c] * base;
+                }
+                if (wants & WT_W_DECAY) {
+                    acc_dr[c] += tab.jr[c] * base * H_r[c];
+                    acc_dd[c] += tab.jd[c] * base * H_d[c];
+                    H_r[c] = lr[c] + tab.dr[c] * H_r[c];
+                    H_d[c] = ld[c] + tab.dd[c] * H_d[c];
+                }
+            }
+        }
+        float g_a = 0.0f;
+        if (ADAPT) {
+            g_a = bw.a_saved[o];
+            if (wants & WT_W_ADAPT) acc_adapt += la * s;
+            if (wants & WT_W_ADAPT_DECAY) acc_adapt_decay += la * g_a;
+        }
+
+        // Membrane adjoint.
+        float Gc[S], Bm[S], clampg[S], Ge[S];
+        float Ssum = 0.0f, EG = 0.0f;
+#pragma unroll
+        for (int c = 0; c < S; c++) {
+            Gc[c] = fminf(fmaxf(G[c], 0.0f), tab.clip[c]);
+            float cg = G[c] < tab.clip[c] ? 1.0f : (G[c] == tab.clip[c] ? 0.5f : 0.0f);
+            clampg[c] = G[c] >= 0.0f ? cg : 0.0f;
+            Bm[c] = MG ? sigmoid(tab.mga[c] * v - tab.mglc[c]) : 1.0f;
+            Ge[c] = MG ? Gc[c] * Bm[c] : Gc[c];
+            Ssum = Ssum + Ge[c];
+            EG = EG + Ge[c] * tab.E[c];
+        }
+        const float gx = dv * (1.0f - r);
+        float J = g_L * (v - E_L) + v * Ssum - EG;
+        if (ADAPT) {
+            Ssum = Ssum + g_a;
+            J = J + g_a * (v - E_a);
+        }
+        const float em = expm1f(-dt * (rate + Ssum * inv_C));
+        const float inv_g = 1.0f / (g_L + Ssum);
+        const float a = 1.0f + em, phi = -em * inv_g;
+        const float phi_S = (a * dt * inv_C - phi) * inv_g;
+        const float k0 = -gx * (phi_S * J + phi * v), k1 = gx * phi;
+        float dv_in = gx * a;
+        float dG[S];
+#pragma unroll
+        for (int c = 0; c < S; c++) {
+            const float dGe = k0 + k1 * tab.E[c];
+            if (MG) {
+                dv_in += dGe * Gc[c] * tab.mga[c] * Bm[c] * (1.0f - Bm[c]);
+                dG[c] = dGe * Bm[c] * clampg[c];
+            } else {
+                dG[c] = dGe * clampg[c];
+            }
+            if (SYN && (wants & WT_W_E_SYN)) acc_E[c] += gx * phi * Ge[c];
+        }
+        if (wants & WT_W_RESET) acc_reset += dv * r;
+        if (wants & WT_W_E_L) acc_E_L += gx * phi * g_L;
+        if (wants & WT_W_C_M) {
+            const float dphi = -(a * dt * Ssum * inv_C * inv_C + phi * g_L * inv_C) * inv_g;
+            acc_C_m -= gx * (dphi * J + phi * (v - E_L) * g_L * inv_C);
+        }
+        if (wants & WT_W_BETA) {
+            const float dg_L = -Cm / (beta * dt);
+            const float dphi = -(a / beta + phi * dg_L) * inv_g;
+            acc_beta -= gx * (dphi * J + phi * (v - E_L) * dg_L);
+        }
+        if (ADAPT) {
+            const float d_ga = k0 + k1 * E_a;
+            if (wants & WT_W_E_ADAPT) acc_E_a += gx * phi * g_a;
+            la = la * a_decay + d_ga;
+        }
+        // The spike (surrogate) and probability of step t, both of v - theta.
+        const float xv = v - theta;
+        const float gs = bw.grad_spikes[o];
+        float g_x;
+        if (SAMPLE) {
+            const float p = sigmoid(k * xv);
+            g_x = gs * k * p * (1.0f - p);
+        } else {
+            const float d = k * fabsf(xv) + 1.0f;
+            g_x = gs / (d * d);
+        }
+        if (PROB && bw.grad_prob) {
+            const float p = sigmoid(k * xv);
+            g_x += bw.grad_prob[o] * k * p * (1.0f - p);
+        }
+        if (REF) g_x *= 1.0f - held;
+        dv = dv_in + g_x;
+        acc_theta -= g_x;
+#pragma unroll
+        for (int c = 0; c < S; c++) {
+            lr[c] = lr[c] * tab.dr[c] + dG[c];
+            ld[c] = ld[c] * tab.dd[c] + dG[c];
+        }
+    }
+
+    const size_t bn = (size_t)b * N + n;
+    if (wants & WT_W_THETA) bw.g_theta[bn] = acc_theta;
+    if (wants & WT_W_RESET) bw.g_reset[bn] = acc_reset;
+    if (wants & WT_W_E_L) bw.g_E_L[bn] = acc_E_L;
+    if (wants & WT_W_C_M) bw.g_C_m[bn] = acc_C_m;
+    if (wants & WT_W_BETA) bw.g_beta[bn] = acc_beta;
+    if (wants & WT_W_ADAPT) bw.g_adapt[bn] = acc_adapt;
+    if (wants & WT_W_ADAPT_DECAY) bw.g_adapt_decay[bn] = acc_adapt_decay;
+    if (wants & WT_W_E_ADAPT) bw.g_E_adapt[bn] = acc_E_a;
+    if (SYN) {
+        const float *gi = bw.g_init + (size_t)b * 2 * S * N + n;
+#pragma unroll
+        for (int c = 0; c < S; c++) {
+            if (wants & WT_W_E_SYN) bw.g_E_syn[((size_t)b * S + c) * N + n] = acc_E[c];
+            if (wants & WT_W_JUMP) {
+                bw.g_jump[((size_t)b * 2 * S + c) * N + n] = acc_jr[c];
+                bw.g_jump[((size_t)b * 2 * S + S + c) * N + n] = acc_jd[c];
+            }
+            if (wants & WT_W_DECAY) {
+                bw.g_decay[((size_t)b * 2 * S + c) * N + n] = acc_dr[c] + gi[(size_t)c * N] * H_r[c];
+                bw.g_decay[((size_t)b * 2 * S + S + c) * N + n] = acc_dd[c] + gi[(size_t)(S + c) * N] * H_d[c];
+            }
+        }
+    }
+}
+
+// One warp per (trial, step, word of 32 sources): every set source's slots and chunks,
+// the whole warp over each chunk's edges.
+__global__ void edge_grads_kernel(const WtNet net, const WtEdgeGrads eg, int rec_words, int in_words) {
+    const int lane = threadIdx.x & 31;
+    const long long warp = ((long long)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const long long nwarps = ((long long)gridDim.x * blockDim.x) >> 5;
+    const int N = net.N, C = net.C, T = eg.T, n_in = net.n_in;
+    const long long per_bt = rec_words + in_words;
+    const long long total = (long long)net.B * T * per_bt;
+    for (long long w = warp; w < total; w += nwarps) {
+        const int bt = (int)(w / per_bt);
+        const int word = (int)(w % per_bt);
+        const int b = bt / T, t = bt % T;
+        unsigned mask;
+        float value;
+        int j;
+        if (word < rec_words) {
+            mask = eg.spike_bits[(size_t)bt * rec_words + word];
+            j = word * 32 + lane;
+            value = 1.0f;
+        } else {
+            const int c = (word - rec_words) * 32 + lane;
+            const float xv = c < n_in ? eg.x[(size_t)bt * n_in + c] : 0.0f;
+            mask = __ballot_sync(kFull, xv != 0.0f);
+            j = N + c;
+            value = xv;
+        }
+        const float *Qbt = eg.Q + (size_t)bt * C * N;
+        while (mask) {
+            const int l = __ffs(mask) - 1;
+            mask &= mask - 1;
+            const int src = __shfl_sync(kFull, j, l);
+            const float val = __shfl_sync(kFull, value, l);
+            for (int slot = net.src_slot[src]; slot < net.src_slot[src + 1]; slot++) {
+                float amp = val;
+                if (net.slot_gate) {
+                    const int gate = net.slot_gate[slot];
+                    if (gate >= 0)
+                        amp = val * eg.f_saved[(size_t)bt * net.R_f + net.gate_cols[4 * gate + 3] + net.slot_row[slot]];
+                }
+                for (int ch = net.slot_chunk[slot]; ch < net.slot_chunk[slot + 1]; ch++) {
+                    const long long e0 = net.chunk_begin[ch];
+                    const int len = net.chunk_len[ch];
+                    const int kp = eg.chunk_path[ch];
+                    for (int q = lane; q < len; q += 32) {
+                        const uint32_t pc = net.edge_col[e0 + q];
+                        const int n = pc & 0x7ffffffu, c = pc >> 27;
+                        const float Qv = Qbt[(size_t)c * N + n];
+                        if (Qv == 0.0f) continue;
+                        const float jfv = eg.jf[(size_t)kp * C + c];
+                        if (eg.g_scale)
+                            atomicAdd(eg.g_scale + (size_t)kp * N + n,
+                                      (double)amp * (double)eg.w_raw[e0 + q] * (double)jfv * (double)Qv);
+                        if (eg.g_w)
+                            atomicAdd(eg.g_w + e0 + q,
+                                      (double)amp * (double)eg.scale[(size_t)kp * N + n] * (double)jfv * (double)Qv);
+                    }
+                }
+            }
+        }
+    }
+}
+
+// One warp per (trial, step, input column): the input's gradient, fired or not.
+__global__ void input_grads_kernel(const WtNet net, const WtEdgeGrads eg) {
+    const int lane = threadIdx.x & 31;
+    const long long warp = ((long long)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const long long nwarps = ((long long)gridDim.x * blockDim.x) >> 5;
+    const int N = net.N, C = net.C, n_in = net.n_in;
+    const long long total = (long long)net.B * eg.T * n_in;
+    for (long long w = warp; w < total; w += nwarps) {
+        const long long bt = w / n_in;
+        const int c_in = (int)(w % n_in);
+        const int src = N + c_in;
+        const float *Qbt = eg.Q + (size_t)bt * C * N;
+        float acc = 0.0f;
+        for (int slot = net.src_slot[src]; slot < net.src_slot[src + 1]; slot++) {
+            float f = 1.0f;
+            if (net.slot_gate) {
+                const int gate = net.slot_gate[slot];
+                if (gate >= 0) f = eg.f_saved[(size_t)bt * net.R_f + net.gate_cols[4 * gate + 3] + net.slot_row[slot]];
+            }
+            float part = 0.0f;
+            for (int ch = net.slot_chunk[slot]; ch < net.slot_chunk[slot + 1]; ch++) {
+                const long long e0 = net.chunk_begin[ch];
+                const int len = net.chunk_len[ch];
+                const int kp = eg.chunk_path[ch];
+                for (int q = lane; q < len; q += 32) {
+                    const uint32_t pc = net.edge_col[e0 + q];
+                    const int n = pc & 0x7ffffffu, c = pc >> 27;
+                    part += eg.w_raw[e0 + q] * eg.scale[(size_t)kp * N + n] * eg.jf[(size_t)kp * C + c] *
+                            Qbt[(size_t)c * N + n];
+                }
+            }
+            acc += f * part;
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(kFull, acc, o);
+        if (lane == 0) eg.g_x[w] = acc;
+    }
+}
+
+template <int S>
+cudaError_t launch_bwd_s(const WtNet &net, const WtBackward &bw, cudaStream_t st) {
+    const long long items = (long long)net.B * net.N;
+    const int blocks = (int)((items + kBlock - 1) / kBlock);
+    if (bw.wants & (WT_W_E_SYN | WT_W_DECAY | WT_W_JUMP))
+        backward_kernel<S, true><<<blocks, kBlock, 0, st>>>(net, bw);
+    else
+        backward_kernel<S, false><<<blocks, kBlock, 0, st>>>(net, bw);
+    return cudaGetLastError();
+}
+
+}  // namespace
+
+cudaError_t launch_backward(const WtNet &net, const WtBackward &bw, cudaStream_t st) {
+    switch (net.S) {
+        case 1: return launch_bwd_s<1>(net, bw, st);
+        case 2: return launch_bwd_s<2>(net, bw, st);
+        case 3: return launch_bwd_s<3>(net, bw, st);
+        case 4: return launch_bwd_s<4>(net, bw, st);
+        case 5: return launch_bwd_s<5>(net, bw, st);
+        case 6: return launch_bwd_s<6>(net, bw, st);
+        case 7: return launch_bwd_s<7>(net, bw, st);
+        case 8: return launch_bwd_s<8>(net, bw, st);
+        default: return cudaErrorInvalidValue;
+    }
+}
+
+cudaError_t launch_edge_grads(const WtNet &net, const WtEdgeGrads &eg, cudaStream_t st) {
+    const int rec_words = (net.N + 31) >> 5, in_words = (net.n_in + 31) >> 5;
+    if (eg.g_scale || eg.g_w) {
+        const long long warps = (long long)net.B * eg.T * (rec_words + in_words);
+        long long blocks = (warps + 7) / 8;
+        if (blocks > 148 * 64) blocks = 148 * 64;
+        if (blocks > 0) edge_grads_kernel<<<(int)blocks, 256, 0, st>>>(net, eg, rec_words, in_words);
+        cudaError_t e = cudaGetLastError();
+        if (e != cudaSuccess) return e;
+    }
+    if (eg.g_x && net.n_in > 0) {
+        const long long warps = (long long)net.B * eg.T * net.n_in;
+        long long blocks = (warps + 7) / 8;
+        if (blocks > 148 * 64) blocks = 148 * 64;
+        input_grads_kernel<<<(int)blocks, 256, 0, st>>>(net, eg);
+    }
+    return cudaGetLastError();
+}
+
+}  // namespace wt

@@ -1,0 +1,157 @@
+// The extern "C" entry points of include/wiretorch_b200.h: argument checks, workspace
+// sizes, and the launches. Nothing here allocates or synchronises.
+#include <cstdio>
+#include <cstring>
+
+#include "common.cuh"
+
+namespace wt {
+cudaError_t launch_forward_s(const WtNet &net, const WtForward &run, const WtWorkspace &ws,
+                             cudaStream_t st, int grid_cap);
+cudaError_t launch_backward(const WtNet &net, const WtBackward &bw, cudaStream_t st);
+cudaError_t launch_edge_grads(const WtNet &net, const WtEdgeGrads &eg, cudaStream_t st);
+cudaError_t launch_fold(const WtNet &net, const float *w_raw, const int32_t *chunk_path, const float *scale,
+                        const float *jf, const float *fx_scale, float *out, cudaStream_t st);
+}
+
+namespace {
+thread_local char g_error[512] = "";
+
+int fail(int code, const char *fmt, const char *detail = "") {
+    std::snprintf(g_error, sizeof g_error, fmt, detail);
+    return code;
+}
+
+int launch_status(cudaError_t e, const char *what) {
+    if (e == cudaSuccess) return WT_OK;
+    std::snprintf(g_error, sizeof g_error, "%s: %s", what, cudaGetErrorString(e));
+    return WT_ERR_LAUNCH;
+}
+
+// Grid blocks worth launching for `items` work items of the persistent kernel (0: as
+// many as can be resident); fewer blocks make the grid barrier cheaper on small nets.
+int grid_cap_for(long long items) {
+    const long long per_block = (long long)wt::kBlock * 2;
+    long long blocks = (items + per_block - 1) / per_block;
+    return blocks < 1 ? 1 : (blocks > (1 << 20) ? 0 : (int)blocks);
+}
+
+int check_net(const WtNet *n) {
+    if (!n) return fail(WT_ERR_ARGS, "net is null%s");
+    if (n->B <= 0 || n->N <= 0 || n->n_in < 0) return fail(WT_ERR_ARGS, "bad sizes%s");
+    if (n->S < 1 || n->S > WT_MAX_CHANNELS) return fail(WT_ERR_UNSUPPORTED, "S must be in 1..8%s");
+    if (n->C < 1 || n->C > WT_MAX_CHANNELS) return fail(WT_ERR_UNSUPPORTED, "C must be in 1..8%s");
+    if (n->N >= (1 << 27)) return fail(WT_ERR_UNSUPPORTED, "N must be below 2^27%s");
+    if ((unsigned long long)n->B * (unsigned long long)(n->n_chunks > 0 ? n->n_chunks : 1) >= (1ull << 32))
+        return fail(WT_ERR_UNSUPPORTED, "trials x chunks must be below 2^32%s");
+    if (!n->theta || !n->U_reset || !n->E_L || !n->C_m || !n->beta)
+        return fail(WT_ERR_ARGS, "missing neuron tables%s");
+    if (!n->src_slot || !n->slot_chunk || (n->n_chunks && (!n->chunk_begin || !n->chunk_len)))
+        return fail(WT_ERR_ARGS, "missing connectivity%s");
+    return WT_OK;
+}
+}  // namespace
+
+extern "C" {
+
+const char *wt_last_error(void) { return g_error; }
+
+int wt_abi_version(void) { return 1; }
+
+int wt_workspace_bytes(const WtNet *net, int32_t T, int64_t bytes[6]) {
+    int rc = check_net(net);
+    if (rc) return rc;
+    const long long BN = (long long)net->B * net->N;
+    const long long cap = (long long)net->B * (net->n_chunks > 0 ? net->n_chunks : 1);
+    bytes[0] = 2LL * net->C * BN * 8;   // X
+    bytes[1] = 2LL * cap * 4;           // ev_item
+    bytes[2] = 2LL * cap * 4;           // ev_amp
+    bytes[3] = ((long long)T + 1) * 4;  // ev_count
+    bytes[4] = 64 * 4;                  // barrier
+    bytes[5] = 4;                       // err
+    return WT_OK;
+}
+
+int wt_fold_weights(const WtNet *net, const float *w_raw, const int32_t *chunk_path, const float *scale,
+                    const float *jf, const float *fx_scale, float *edge_w_out, void *stream) {
+    int rc = check_net(net);
+    if (rc) return rc;
+    if (net->n_chunks && (!w_raw || !chunk_path || !scale || !jf || !fx_scale || !edge_w_out || !net->edge_col))
+        return fail(WT_ERR_ARGS, "missing fold buffers%s");
+    return launch_status(wt::launch_fold(*net, w_raw, chunk_path, scale, jf, fx_scale, edge_w_out,
+                                         (cudaStream_t)stream),
+                         "fold");
+}
+
+int wt_forward(const WtNet *net, const WtForward *run, const WtWorkspace *ws, void *stream) {
+    int rc = check_net(net);
+    if (rc) return rc;
+    if (!run || !ws) return fail(WT_ERR_ARGS, "run or workspace is null%s");
+    if (run->T < 0 || run->t0 < 0 || run->t0 + run->T > run->T_total)
+        return fail(WT_ERR_ARGS, "steps out of range%s");
+    if (!run->v || !run->g || !run->spikes || (net->n_in && !run->x))
+        return fail(WT_ERR_ARGS, "missing state or output%s");
+    const int f = run->flags;
+    if ((f & WT_F_REFRACTORY) && (!run->counter || !net->n_ref)) return fail(WT_ERR_ARGS, "refractory buffers%s");
+    if ((f & WT_F_ADAPT) && (!run->g_a || !net->adapt || !net->adapt_decay || !net->E_adapt))
+        return fail(WT_ERR_ARGS, "adaptation buffers%s");
+    if ((f & WT_F_SAMPLE) && !run->noise) return fail(WT_ERR_ARGS, "noise buffer%s");
+    if ((f & WT_F_GATED) && (!run->gating || !net->slot_gate || !net->slot_row || !net->gate_params ||
+                             !net->gate_cols))
+        return fail(WT_ERR_ARGS, "gating buffers%s");
+    if ((f & WT_F_SAVE) && (!run->v_saved || !run->G_saved || !run->spike_bits ||
+                            ((f & WT_F_REFRACTORY) && !run->held_bits) ||
+                            ((f & WT_F_ADAPT) && !run->a_saved) || ((f & WT_F_GATED) && !run->f_saved)))
+        return fail(WT_ERR_ARGS, "saved-tensor buffers%s");
+    if ((f & WT_F_SAVE_INPUT) && !run->X_saved) return fail(WT_ERR_ARGS, "saved-input buffer%s");
+    if ((f & WT_F_PROB) && !run->prob) return fail(WT_ERR_ARGS, "probability buffer%s");
+    if ((f & WT_F_TRACK) && (!run->track_v || !run->track_I || !run->track_g ||
+                             ((f & WT_F_ADAPT) && !run->track_a)))
+        return fail(WT_ERR_ARGS, "tracking buffers%s");
+    if (!ws->X || !ws->ev_item || !ws->ev_amp || !ws->ev_count || !ws->barrier || !ws->err)
+        return fail(WT_ERR_ARGS, "workspace buffers%s");
+    if (ws->ev_cap < (long long)net->B * net->n_chunks) return fail(WT_ERR_ARGS, "event capacity too small%s");
+    if (run->T == 0) return WT_OK;
+    cudaStream_t st = (cudaStream_t)stream;
+    cudaError_t e = cudaMemsetAsync(ws->barrier, 0, 64 * 4, st);
+    if (e != cudaSuccess) return launch_status(e, "barrier reset");
+    const long long Np = (net->N + 31) & ~31, Ip = (net->n_in + 31) & ~31;
+    const long long items = (long long)net->B * (Np > Ip ? Np : Ip);
+    return launch_status(wt::launch_forward_s(*net, *run, *ws, st, grid_cap_for(items)), "forward");
+}
+
+int wt_backward(const WtNet *net, const WtBackward *bw, void *stream) {
+    int rc = check_net(net);
+    if (rc) return rc;
+    if (!bw || bw->T < 0) return fail(WT_ERR_ARGS, "bad backward arguments%s");
+    if (!bw->grad_spikes || !bw->v_saved || !bw->G_saved || !bw->spike_bits || !bw->Q)
+        return fail(WT_ERR_ARGS, "missing saved tensors%s");
+    const int f = bw->flags, w = bw->wants;
+    if ((f & WT_F_REFRACTORY) && !bw->held_bits) return fail(WT_ERR_ARGS, "missing refractory bits%s");
+    if ((f & WT_F_ADAPT) && (!bw->a_saved || !net->adapt_decay || !net->E_adapt))
+        return fail(WT_ERR_ARGS, "missing adaptation%s");
+    if ((w & (WT_W_DECAY | WT_W_JUMP)) && !bw->X_saved) return fail(WT_ERR_ARGS, "missing saved input%s");
+    if ((w & WT_W_DECAY) && !bw->g_init) return fail(WT_ERR_ARGS, "missing initial conductances%s");
+    float *const outs[11] = {bw->g_theta, bw->g_reset, bw->g_E_L, bw->g_C_m, bw->g_beta, bw->g_E_syn,
+                             bw->g_decay, bw->g_jump, bw->g_adapt, bw->g_adapt_decay, bw->g_E_adapt};
+    for (int i = 0; i < 11; i++)
+        if ((w >> i & 1) && !outs[i]) return fail(WT_ERR_ARGS, "missing gradient output%s");
+    if (bw->T == 0) return WT_OK;
+    return launch_status(wt::launch_backward(*net, *bw, (cudaStream_t)stream), "backward");
+}
+
+int wt_edge_grads(const WtNet *net, const WtEdgeGrads *eg, void *stream) {
+    int rc = check_net(net);
+    if (rc) return rc;
+    if (!eg || eg->T < 0 || !eg->Q || !eg->chunk_path || !eg->jf) return fail(WT_ERR_ARGS, "bad edge arguments%s");
+    if ((eg->g_scale || eg->g_w) && (!eg->spike_bits || (net->n_in && !eg->x)))
+        return fail(WT_ERR_ARGS, "missing events%s");
+    if (eg->g_scale && !eg->w_raw) return fail(WT_ERR_ARGS, "missing raw weights%s");
+    if ((eg->g_w || eg->g_x) && !eg->scale) return fail(WT_ERR_ARGS, "missing scale%s");
+    if (eg->g_x && !eg->w_raw) return fail(WT_ERR_ARGS, "missing raw weights%s");
+    if (net->slot_gate && !eg->f_saved) return fail(WT_ERR_ARGS, "missing gating factors%s");
+    if (eg->T == 0) return WT_OK;
+    return launch_status(wt::launch_edge_grads(*net, *eg, (cudaStream_t)stream), "edge gradients");
+}
+
+}  // extern "C"
