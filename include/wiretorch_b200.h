@@ -82,6 +82,7 @@ typedef struct {
     const uint32_t *edge_col;   /* (E): target | input channel << 27 */
     const float *edge_w;        /* (E): folded weight, times 2^s of its channel */
     int32_t n_slots, n_chunks;
+    int32_t n_rec_chunks;       /* chunks of the neurons' slots (they come first) */
     /* presynaptic gating (WT_F_GATED): per slot its gate (-1: none) and row */
     const int32_t *slot_gate, *slot_row;
     const float *gate_params;   /* (n_gates, 5): c, d, U, d_D, d_F */
@@ -123,6 +124,7 @@ typedef struct {
     uint32_t *barrier;          /* (64) */
     int32_t *err;               /* (1): a device error code, 0 if none */
     int64_t ev_cap;
+    unsigned long long *edges;  /* (2) or NULL: edges traversed (recurrent, input) */
 } WtWorkspace;
 
 /* Bytes of each workspace buffer for a run of T steps (X, ev_item, ev_amp, ev_count,
@@ -198,6 +200,37 @@ int wt_backward(const WtNet *net, const WtBackward *bwd, void *stream);
  * gradient `weight_gradient` (network_simulators/engine.py:327-350) and the input
  * gradient of `_SparseActivations.backward` (network_simulators/engine.py:96-116). */
 int wt_edge_grads(const WtNet *net, const WtEdgeGrads *eg, void *stream);
+
+/* The double-exponential filter of the spike-train losses, over (B, T, N) trains:
+ * rise_t = a_rise rise_{t-1} + x_t, smooth_t = a_decay smooth_{t-1} + rise_t, the carried
+ * state entering undecayed at t = 0. x is read with element strides (a t-stride of 0
+ * filters a train constant in time). */
+typedef struct {
+    int32_t B, T, N;
+    const float *x;
+    int64_t x_bstride, x_tstride;
+    const float *carry_rise, *carry_smooth;  /* (B, N), or NULL for zero */
+    float a_rise, a_decay;
+    float *rise, *smooth;                    /* (B, T, N), either may be NULL */
+    float *last_rise, *last_smooth;          /* (B, N), either may be NULL */
+} WtFilterArgs;
+
+/* The filter's adjoint: dL/dx from dL/dsmooth times grad_scale (no gradient flows into
+ * the carried state or through rise). */
+typedef struct {
+    int32_t B, T, N;
+    const float *grad_smooth;
+    float grad_scale;
+    float a_rise, a_decay;
+    float *grad_x;
+} WtFilterGradArgs;
+
+/* Replaces `_filter_forward` (training_utils/filtering.py:103-120) and the CPU Toeplitz
+ * path of `double_exponential` (filtering.py:28-73). */
+int wt_filter_forward(const WtFilterArgs *f, void *stream);
+
+/* Replaces `_filter_backward` (training_utils/filtering.py:123-135). */
+int wt_filter_backward(const WtFilterGradArgs *f, void *stream);
 
 /* Reading back: a static description of the last host-side error on this thread. */
 const char *wt_last_error(void);

@@ -1,0 +1,68 @@
+"""The loss filter's kernels against its definition (wiretorch's
+``tests/test_losses.py:28-55``): ``y[t] = sum_{k <= t} exp(-k dt / tau) x[t - k] +
+carried exp(-t dt / tau)``, rise then decay, the state carried from chunk to chunk and no
+gradient across chunks. Both kernel variants run: the per-column scan (many trains) and
+the warp-shuffle parallel scan over time (few trains)."""
+
+import numpy as np
+import pytest
+import torch
+
+from wiretorch_b200 import filtering
+
+pytestmark = pytest.mark.gpu
+
+TAU_RISE, TAU_DECAY, DT = 10.0, 100.0, 1.0
+
+
+def exponential_filter(x, tau, carried):
+    T = x.shape[1]
+    k = torch.exp(-torch.arange(T, dtype=torch.float64, device=x.device) * DT / tau)
+    lag = torch.arange(T, device=x.device)
+    lag = lag[:, None] - lag[None, :]
+    M = torch.where(lag >= 0, k[lag.clamp(min=0)], torch.zeros((), dtype=torch.float64, device=x.device))
+    y = torch.einsum("ts,bsn->btn", M, x.double())
+    return y if carried is None else y + carried.double() * k[None, :, None]
+
+
+@pytest.mark.parametrize("B,N,T", [(2, 7, 300), (64, 2000, 120)], ids=["parallel-T", "per-column"])
+def test_filter_matches_definition_across_chunks(B, N, T):
+    rng = np.random.default_rng(0)
+    x = torch.from_numpy((rng.random((B, 3 * T, N)) < 0.05).astype(np.float32)).cuda()
+    x.requires_grad_(True)
+    t = torch.arange(T, dtype=torch.float32, device="cuda") * DT
+    kr, kd = torch.exp(-t / TAU_RISE), torch.exp(-t / TAU_DECAY)
+    rise = smooth = None
+    ref_r = ref_s = None
+    R = torch.from_numpy(rng.normal(size=(B, T, N)).astype(np.float32)).cuda()
+    for c in range(3):
+        xc = x[:, c * T : (c + 1) * T]
+        r, s = filtering.double_exponential(xc, kr, kd, rise, smooth)
+        er = exponential_filter(xc.detach(), TAU_RISE, ref_r)
+        es = exponential_filter(er, TAU_DECAY, ref_s)
+        torch.testing.assert_close(s.double(), es, rtol=1e-4, atol=1e-4)
+        torch.testing.assert_close(r.double(), er, rtol=1e-4, atol=1e-4)
+        # gradient of sum(s R) w.r.t. this chunk's input: the transposed filters
+        (g,) = torch.autograd.grad((s * R).sum(), xc)
+        x64 = xc.detach().double().requires_grad_(True)
+        e64 = exponential_filter(exponential_filter(x64, TAU_RISE, None), TAU_DECAY, None)
+        (g64,) = torch.autograd.grad((e64 * R.double()).sum(), x64)
+        torch.testing.assert_close(g.double(), g64, rtol=1e-4, atol=1e-3)
+        rise, smooth = r[:, -1:].detach(), s[:, -1:].detach()
+        ref_r, ref_s = er[:, -1:], es[:, -1:]
+
+
+def test_van_rossum_rate_loss_matches_definition():
+    rng = np.random.default_rng(1)
+    B, T, N = 4, 200, 300
+    out = torch.from_numpy((rng.random((B, T, N)) < 0.02).astype(np.float32)).cuda().requires_grad_(True)
+    rate = torch.from_numpy(rng.uniform(0.0, 0.05, (B, 1, N)).astype(np.float32)).cuda()
+    loss_fn = filtering.VanRossumRateLoss(TAU_RISE, TAU_DECAY, DT, T)
+    loss = loss_fn(rate.expand(B, T, N), output_spikes=out)
+    es_out = exponential_filter(exponential_filter(out.double(), TAU_RISE, None), TAU_DECAY, None)
+    es_tgt = exponential_filter(exponential_filter(rate.expand(B, T, N), TAU_RISE, None), TAU_DECAY, None)
+    expected = ((es_out - es_tgt) ** 2).mean()
+    torch.testing.assert_close(loss.double(), expected, rtol=1e-4, atol=1e-7)
+    (g,) = torch.autograd.grad(loss, out)
+    (g64,) = torch.autograd.grad(expected, out)
+    torch.testing.assert_close(g.double(), g64.double(), rtol=1e-3, atol=1e-7)

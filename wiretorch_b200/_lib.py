@@ -44,7 +44,7 @@ class WtNet(C.Structure):
         ("dt", C.c_float), ("surr_scale", C.c_float),
         ("src_slot", P), ("slot_chunk", P), ("chunk_begin", P), ("chunk_len", P),
         ("edge_col", P), ("edge_w", P),
-        ("n_slots", C.c_int32), ("n_chunks", C.c_int32),
+        ("n_slots", C.c_int32), ("n_chunks", C.c_int32), ("n_rec_chunks", C.c_int32),
         ("slot_gate", P), ("slot_row", P), ("gate_params", P), ("gate_cols", P),
         ("R", C.c_int32), ("R_f", C.c_int32),
     ]  # fmt: skip
@@ -65,7 +65,7 @@ class WtForward(C.Structure):
 class WtWorkspace(C.Structure):
     _fields_ = [
         ("X", P), ("ev_item", P), ("ev_amp", P), ("ev_count", P), ("barrier", P),
-        ("err", P), ("ev_cap", C.c_int64),
+        ("err", P), ("ev_cap", C.c_int64), ("edges", P),
     ]  # fmt: skip
 
 
@@ -83,9 +83,48 @@ def lib() -> C.CDLL:
             )
         _lib = C.CDLL(str(LIB))
         _lib.wt_last_error.restype = C.c_char_p
-        for name in ("wt_forward", "wt_fold_weights", "wt_workspace_bytes", "wt_abi_version"):
+        for name in ("wt_forward", "wt_fold_weights", "wt_workspace_bytes", "wt_abi_version",
+                     "wt_backward", "wt_edge_grads", "wt_filter_forward", "wt_filter_backward"):
             getattr(_lib, name).restype = C.c_int
     return _lib
+
+
+#: Kernels this process has launched through the library (for the benchmark's count).
+LAUNCHES = 0
+
+
+def count_launches(n: int) -> None:
+    global LAUNCHES
+    LAUNCHES += n
+
+
+#: When a dict, each launch through the library records CUDA events around itself on
+#: the current stream under its kernel's name: ``{name: [(start, end), ...]}``.
+TIMER = None
+
+
+class timed:
+    """Context manager: events around a launch (only while ``TIMER`` is a dict)."""
+
+    def __init__(self, name: str):
+        self.name = name
+
+    def __enter__(self):
+        if TIMER is not None:
+            import torch
+
+            self.start = torch.cuda.Event(enable_timing=True)
+            self.start.record()
+        return self
+
+    def __exit__(self, *exc):
+        if TIMER is not None:
+            import torch
+
+            end = torch.cuda.Event(enable_timing=True)
+            end.record()
+            TIMER.setdefault(self.name, []).append((self.start, end))
+        return False
 
 
 def check(rc: int, what: str) -> None:

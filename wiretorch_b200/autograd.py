@@ -145,7 +145,10 @@ class _Simulate(torch.autograd.Function):
                 partial[name] = torch.empty(shapes.get(name, (B, N)), device=device)
                 setattr(bw, field, partial[name].data_ptr())
         stream = _lib.C.c_void_p(_lib.stream_of(device))
-        _lib.check(_lib.lib().wt_backward(_lib.C.byref(net), _lib.C.byref(bw), stream), "wt_backward")
+        with _lib.timed("wt_backward"):
+            rc = _lib.lib().wt_backward(_lib.C.byref(net), _lib.C.byref(bw), stream)
+        _lib.check(rc, "wt_backward")
+        _lib.count_launches(1)
 
         n_weights = ctx.n_weights
         need_scale = ctx.needs_input_grad[1]
@@ -174,8 +177,10 @@ class _Simulate(torch.autograd.Function):
             if need_x:
                 g_x = torch.empty(x.shape, device=device)
                 eg.g_x = g_x.data_ptr()
-            _lib.check(_lib.lib().wt_edge_grads(_lib.C.byref(net), _lib.C.byref(eg), stream),
-                       "wt_edge_grads")  # fmt: skip
+            with _lib.timed("wt_edge_grads"):
+                rc = _lib.lib().wt_edge_grads(_lib.C.byref(net), _lib.C.byref(eg), stream)
+            _lib.check(rc, "wt_edge_grads")
+            _lib.count_launches(int(need_scale or need_w) + int(need_x))
 
         grads_w = [None] * n_weights
         if need_w:

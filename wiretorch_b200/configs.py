@@ -1,0 +1,226 @@
+"""Seeded synthetic networks of the benchmark configurations, built as wiretorch's
+networks hand them to their engine: a ``Drive`` (weights as ``SparseRows``), a
+``Physiology`` and the state at rest.
+
+The configurations (the benchmark specification's five) leave some physiology open; the
+values chosen here are fixed once and named in each builder (leak conductance, input
+weights), chosen so that neurons fire at a few to a few tens of Hz. Synapses with
+``tau_rise = 0`` are single exponentials: ``conductance_kernel`` gives them jumps
+``(-g_bar, +g_bar)`` and a rise decay of 0, so an input reaches the membrane one step
+after it arrives (as in the reference).
+
+Connectivity is generated with torch on the given device from a seeded generator (the
+same seed gives the same network on the same kind of device). Cell types occupy
+contiguous index ranges.
+"""
+
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass, field
+
+import numpy as np
+import torch
+
+from wiretorch_b200.types import Drive, Physiology, SparseRows
+
+
+@dataclass
+class Config:
+    """A built configuration: the engine's inputs plus what the benchmark needs."""
+
+    name: str
+    drive: Drive
+    p: Physiology
+    B: int
+    T: int
+    N: int
+    n_in: int
+    rates_in: torch.Tensor  # (n_in,) Hz of the Poisson inputs
+    types: torch.Tensor  # (N,) cell type of each neuron
+    n_types: int
+    out_degree: torch.Tensor  # (N + n_in,) edges of each source (recurrent + input)
+    extra: dict = field(default_factory=dict)
+
+    def state(self):
+        """``(v, g, kw)`` at rest: voltages at reset, conductances zero."""
+        dev = self.drive.scale.device
+        S = self.p.E_syn.shape[0]
+        v = self.p.U_reset.expand(self.B, self.N).clone()
+        g = torch.zeros((self.B, 2, S, self.N), device=dev).permute(0, 3, 1, 2)
+        kw = {"refractory": torch.zeros((self.B, self.N), dtype=torch.int32, device=dev)}
+        if self.p.adapt is not None:
+            kw["adaptation"] = torch.zeros((self.B, self.N), device=dev)
+        return v, g, kw
+
+    def inputs(self, T=None, seed=1, generator_device=None):
+        """Poisson input spikes ``(B, T, n_in)`` float32 (seeded)."""
+        T = self.T if T is None else T
+        dev = self.drive.scale.device
+        gen = torch.Generator(device=dev).manual_seed(seed)
+        p = (self.rates_in * float(self.p.dt) / 1000.0).to(dev)
+        return (torch.rand((self.B, T, self.n_in), generator=gen, device=dev) < p).float()
+
+
+def _kernel(tau_rise, tau_decay, g_bar):
+    """``conductance_kernel`` (conductance/synapses.py:70-87): jumps of the rise and decay
+    components per unit input, the difference of exponentials peaking at ``g_bar``."""
+    r = tau_rise / tau_decay
+    peak = torch.where(r > 0, r ** (r / (1 - r)) - r ** (1 / (1 - r)), torch.ones_like(r))
+    return torch.stack([-g_bar, g_bar]) / peak
+
+
+def _csr_from_edges(src, dst, w, n_rows, n_targets):
+    order = torch.argsort(src * n_targets + dst)
+    src, dst, w = src[order], dst[order], w[order]
+    row_ptr = torch.zeros(n_rows + 1, dtype=torch.int64, device=src.device)
+    row_ptr[1:] = torch.cumsum(torch.bincount(src, minlength=n_rows), 0)
+    return SparseRows(row_ptr, dst.to(torch.int32), w.float().contiguous(), n_targets)
+
+
+def _block_edges(gen, rows, cols, p, device):
+    """Bernoulli(p) edges between index ranges ``rows`` and ``cols`` (half-open pairs)."""
+    r0, r1 = rows
+    c0, c1 = cols
+    nr, nc = r1 - r0, c1 - c0
+    if nr == 0 or nc == 0 or p <= 0:
+        e = torch.zeros(0, dtype=torch.int64, device=device)
+        return e, e
+    mask = torch.rand((nr, nc), generator=gen, device=device) < p
+    nz = mask.nonzero()
+    return nz[:, 0] + r0, nz[:, 1] + c0
+
+
+def _physiology(N, types_e, dt, S_params, device, tau_mem=20.0, theta=-50.0, U_reset=-65.0,
+                E_L=-70.0, g_L=10.0, tau_ref=2.0):  # fmt: skip
+    """Per-neuron tables (all neurons alike) and per-synapse tables from ``S_params``:
+    list of (tau_rise, tau_decay, E_syn, g_bar)."""
+    f = lambda v: torch.tensor(v, dtype=torch.float32, device=device)  # noqa: E731
+    dtt = f(dt)
+    tr = f([s[0] for s in S_params])
+    td = f([s[1] for s in S_params])
+    gb = f([s[3] for s in S_params])
+    decay_r = torch.where(tr > 0, torch.exp(-dtt / tr.clamp(min=1e-30)), torch.zeros_like(tr))
+    ones = torch.ones(N, device=device)
+    return Physiology(
+        theta=ones * theta, U_reset=ones * U_reset, E_L=ones * E_L,
+        C_m=ones * (tau_mem * g_L), beta=torch.exp(-dtt / (ones * tau_mem)),
+        E_syn=f([s[2] for s in S_params]),
+        g_clip=torch.full((len(S_params),), float("inf"), device=device),
+        decay=torch.stack([decay_r, torch.exp(-dtt / td)]),
+        jump=_kernel(tr, td, gb), dt=dtt, surr_scale=f(10.0),
+        n_ref=torch.full((N,), int(round(tau_ref / dt)), dtype=torch.int32, device=device),
+    )  # fmt: skip
+
+
+def c1(B=8, T=1000, seed=0, device="cuda", w_in=15.0, g_L=10.0):
+    """Conductance LIF, N=1000 (800 E / 200 I), Erdos-Renyi p=0.1, log-normal weights
+    (mu=-1, sigma=1, nS) signed by presynaptic type, tau_m=20 ms, E_L=-70, V_th=-50,
+    V_reset=-65 mV, refractory 2 ms, E_exc=0 / E_inh=-80 mV, tau_syn 5 / 10 ms, dt=0.1 ms,
+    T=1000, batch 8, one independent 10 Hz Poisson input per neuron; forward only.
+    Chosen here: g_L = 10 nS, input weight 15 nS (rates of 2-3 Hz; with equal E and I
+    weight distributions the network runs away above ~18 nS)."""
+    dev = torch.device(device)
+    gen = torch.Generator(device=dev).manual_seed(seed)
+    N, NE = 1000, 800
+    src, dst = _block_edges(gen, (0, N), (0, N), 0.1, dev)
+    keep = src != dst
+    src, dst = src[keep], dst[keep]
+    w = torch.exp(-1.0 + torch.randn(src.numel(), generator=gen, device=dev))
+    e = src < NE
+    W_e = _csr_from_edges(src[e], dst[e], w[e], NE, N)
+    W_i = _csr_from_edges(src[~e] - NE, dst[~e], w[~e], N - NE, N)
+    ar = torch.arange(N, device=dev)
+    W_in = _csr_from_edges(ar, ar, torch.full((N,), w_in, device=dev), N, N)
+    # synapse types: 0 AMPA (E), 1 GABA (I), 2 AMPA (input)
+    S_params = [(0.0, 5.0, 0.0, 1.0), (0.0, 10.0, -80.0, 1.0), (0.0, 5.0, 0.0, 1.0)]
+    made = torch.eye(3, dtype=torch.bool, device=dev)
+    drive = Drive(made=made, scale=torch.ones(3, N, device=dev),
+                  recurrent=[(ar[:NE], W_e), (ar[NE:], W_i)],
+                  feedforward=[(ar, W_in)])  # fmt: skip
+    p = _physiology(N, None, 0.1, S_params, dev, g_L=g_L)
+    types = (ar >= NE).to(torch.int64)
+    out_deg = torch.cat([torch.bincount(src, minlength=N), torch.ones(N, dtype=torch.int64, device=dev)])
+    return Config("c1", drive, p, B, T, N, N, torch.full((N,), 10.0, device=dev), types, 2, out_deg)
+
+
+def c2(B=64, T=500, seed=0, device="cuda", n_in=2000, p_in=0.05, w_mu=-1.0, w_mu_i=0.6,
+       w_in_mu=-0.5, g_L=10.0, n_types=40, frac_e_types=0.75):  # fmt: skip
+    """N=20,000 neurons in 40 synthetic cell types (type sizes multinomial; 75% of the types
+    excitatory), per-type-pair connection probability ~U(0, 0.05), log-normal per-synapse
+    weights (sigma=1, nS; mu=w_mu from excitatory types, w_mu_i = w_mu + ln 5 from
+    inhibitory ones, so that inhibition balances the 3:1 excitatory majority), learnt
+    per-type-pair scale, dt=0.1 ms, T=500, batch 64,
+    Poisson inputs at 5-20 Hz (``n_in`` inputs, each reaching a neuron with probability
+    ``p_in``, log-normal weights mu=w_in_mu). Physiology as ``c1`` (g_L = 10 nS). At
+    these values the network fires at 10-15 Hz.
+
+    Every cell type makes its own synapse type, as the reference's synapse registry does
+    (one per source cell type and synapse name): 30 AMPA-like (tau 5 ms, E 0 mV), 10
+    GABA-like (tau 10 ms, E -80 mV), and the inputs' AMPA. ``extra["log_sf_shape"]``:
+    the learnt per-pair log scale, (41 source types, 40 target types)."""
+    dev = torch.device(device)
+    gen = torch.Generator(device=dev).manual_seed(seed)
+    rng = np.random.default_rng(seed)
+    N = 20000
+    sizes = rng.multinomial(N, np.full(n_types, 1.0 / n_types))
+    starts = np.concatenate([[0], np.cumsum(sizes)])
+    n_e_types = int(round(frac_e_types * n_types))
+    p_pair = rng.uniform(0.0, 0.05, (n_types, n_types))
+    rows_l, pathways = [], []
+    srcs, dsts = [], []
+    for a in range(n_types):
+        s_a, d_a = [], []
+        for b in range(n_types):
+            s, d = _block_edges(gen, (starts[a], starts[a + 1]), (starts[b], starts[b + 1]),
+                                float(p_pair[a, b]), dev)  # fmt: skip
+            s_a.append(s)
+            d_a.append(d)
+        s_a, d_a = torch.cat(s_a), torch.cat(d_a)
+        keep = s_a != d_a
+        srcs.append(s_a[keep])
+        dsts.append(d_a[keep])
+    out_deg = torch.zeros(N + n_in, dtype=torch.int64, device=dev)
+    for a in range(n_types):
+        s_a, d_a = srcs[a], dsts[a]
+        mu = w_mu if a < n_e_types else w_mu_i
+        w = torch.exp(mu + torch.randn(s_a.numel(), generator=gen, device=dev))
+        rows = torch.arange(starts[a], starts[a + 1], device=dev)
+        pathways.append((rows, _csr_from_edges(s_a - starts[a], d_a, w, int(sizes[a]), N)))
+        out_deg[starts[a] : starts[a + 1]] = torch.bincount(s_a - starts[a], minlength=int(sizes[a]))
+    s_in, d_in = _block_edges(gen, (0, n_in), (0, N), p_in, dev)
+    w_in = torch.exp(w_in_mu + torch.randn(s_in.numel(), generator=gen, device=dev))
+    W_in = _csr_from_edges(s_in, d_in, w_in, n_in, N)
+    out_deg[N:] = torch.bincount(s_in, minlength=n_in)
+    S = n_types + 1
+    S_params = [(0.0, 5.0, 0.0, 1.0) if a < n_e_types else (0.0, 10.0, -80.0, 1.0)
+                for a in range(n_types)] + [(0.0, 5.0, 0.0, 1.0)]  # fmt: skip
+    made = torch.eye(S, dtype=torch.bool, device=dev)
+    types = torch.repeat_interleave(torch.arange(n_types, device=dev),
+                                    torch.tensor(sizes, device=dev))  # fmt: skip
+    drive = Drive(made=made, scale=torch.ones(S, N, device=dev), recurrent=pathways,
+                  feedforward=[(torch.arange(n_in, device=dev), W_in)])  # fmt: skip
+    p = _physiology(N, None, 0.1, S_params, dev, g_L=g_L)
+    rates = torch.from_numpy(rng.uniform(5.0, 20.0, n_in).astype(np.float32)).to(dev)
+    cfg = Config("c2", drive, p, B, T, N, n_in, rates, types, n_types, out_deg)
+    cfg.extra["log_sf_shape"] = (S, n_types)
+    cfg.extra["target_rates"] = torch.from_numpy(
+        rng.uniform(1.0, 30.0, (B, N)).astype(np.float32)).to(dev)  # fmt: skip
+    return cfg
+
+
+def scale_from_log_sf(cfg: Config, log_sf: torch.Tensor) -> torch.Tensor:
+    """The kernel scale ``(K, N)`` of learnt per-pair log scales ``(K, n_types)``: each
+    pathway's factor for each target neuron's type (network.py:816-854 ``_drive``)."""
+    return torch.exp(log_sf)[:, cfg.types]
+
+
+def synaptic_events(cfg: Config, spikes: torch.Tensor, x: torch.Tensor | None = None) -> tuple[int, int]:
+    """``(recurrent, input)`` synaptic events of a run: every recurrent spike times its
+    neuron's out-degree, and every non-zero input times its input's out-degree."""
+    deg = cfg.out_degree.to(spikes.device).double()
+    rec = int((spikes.double().sum((0, 1)) * deg[: cfg.N]).sum())
+    inp = 0
+    if x is not None:
+        inp = int(((x != 0).double().sum((0, 1)) * deg[cfg.N :]).sum())
+    return rec, inp

@@ -10,6 +10,8 @@ cudaError_t launch_forward_s(const WtNet &net, const WtForward &run, const WtWor
                              cudaStream_t st, int grid_cap);
 cudaError_t launch_backward(const WtNet &net, const WtBackward &bw, cudaStream_t st);
 cudaError_t launch_edge_grads(const WtNet &net, const WtEdgeGrads &eg, cudaStream_t st);
+cudaError_t launch_filter(const WtFilterArgs &f, cudaStream_t st);
+cudaError_t launch_filter_grad(const WtFilterGradArgs &f, cudaStream_t st);
 cudaError_t launch_fold(const WtNet &net, const float *w_raw, const int32_t *chunk_path, const float *scale,
                         const float *jf, const float *fx_scale, float *out, cudaStream_t st);
 }
@@ -152,6 +154,18 @@ int wt_edge_grads(const WtNet *net, const WtEdgeGrads *eg, void *stream) {
     if (net->slot_gate && !eg->f_saved) return fail(WT_ERR_ARGS, "missing gating factors%s");
     if (eg->T == 0) return WT_OK;
     return launch_status(wt::launch_edge_grads(*net, *eg, (cudaStream_t)stream), "edge gradients");
+}
+
+int wt_filter_forward(const WtFilterArgs *f, void *stream) {
+    if (!f || f->B < 0 || f->T < 0 || f->N < 0 || (f->B && f->T && f->N && !f->x))
+        return fail(WT_ERR_ARGS, "bad filter arguments%s");
+    return launch_status(wt::launch_filter(*f, (cudaStream_t)stream), "filter");
+}
+
+int wt_filter_backward(const WtFilterGradArgs *f, void *stream) {
+    if (!f || f->B < 0 || f->T < 0 || f->N < 0 || (f->B && f->T && f->N && (!f->grad_smooth || !f->grad_x)))
+        return fail(WT_ERR_ARGS, "bad filter-gradient arguments%s");
+    return launch_status(wt::launch_filter_grad(*f, (cudaStream_t)stream), "filter gradient");
 }
 
 }  // extern "C"

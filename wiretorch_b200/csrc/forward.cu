@@ -367,6 +367,7 @@ __global__ void __launch_bounds__(kBlock) forward_kernel(const WtNet net, const 
                 const long long e0 = net.chunk_begin[chunk];
                 const int len = net.chunk_len[chunk];
                 unsigned long long *Xb = X + (size_t)b * N;
+                if (ws.edges && lane == 0) atomicAdd(ws.edges + (chunk >= (uint32_t)net.n_rec_chunks), (unsigned long long)len);
                 for (int q = lane; q < len; q += 32) {
                     const uint32_t pc = net.edge_col[e0 + q];
                     const float prod = net.edge_w[e0 + q] * amp;

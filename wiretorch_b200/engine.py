@@ -33,6 +33,10 @@ POOL_SYNAPSES = os.environ.get("WIRETORCH_POOL_SYNAPSES", "0") == "1"
 
 _PLANS: dict = {}
 
+#: If set to a (2,) int64 CUDA tensor, the forward kernel adds to it the edges it
+#: traverses (recurrent, input): the synaptic events of the run, counted on the device.
+EDGE_COUNTER = None
+
 
 def _key(drive, p, B, n_in, device, pool):
     pathways = list(drive.recurrent) + list(drive.feedforward)
@@ -108,6 +112,8 @@ def _workspace(plan, T, device):
     for name in ("X", "ev_item", "ev_amp", "ev_count", "barrier", "err"):
         setattr(w, name, ws[name].data_ptr())
     w.ev_cap = cap
+    if EDGE_COUNTER is not None:
+        w.edges = EDGE_COUNTER.data_ptr()
     return ws, w
 
 
@@ -192,9 +198,11 @@ def run_forward(plan, p, x, v, g, counter, g_a, gating, *, probabilities=False, 
     run.flags = flags
     ws, w = _workspace(plan, T, device)
     out["_ws"] = ws
-    rc = _lib.lib().wt_forward(_ctypes_ref(net), _ctypes_ref(run), _ctypes_ref(w),
-                               _lib.C.c_void_p(_lib.stream_of(device)))  # fmt: skip
+    with _lib.timed("wt_forward"):
+        rc = _lib.lib().wt_forward(_ctypes_ref(net), _ctypes_ref(run), _ctypes_ref(w),
+                                   _lib.C.c_void_p(_lib.stream_of(device)))  # fmt: skip
     _lib.check(rc, "wt_forward")
+    _lib.count_launches(1)
     if check:
         check_device(ws["err"], "wt_forward")
     return out

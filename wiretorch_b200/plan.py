@@ -181,6 +181,7 @@ class Plan:
     fx_exp: list = field(default_factory=list)
     n_slots: int = 0
     n_chunks: int = 0
+    n_rec_chunks: int = 0
     n_edges: int = 0
     R: int = 0
     R_f: int = 0
@@ -241,6 +242,7 @@ class Plan:
         n.chunk_begin, n.chunk_len = t["chunk_begin"].data_ptr(), t["chunk_len"].data_ptr()
         n.edge_col, n.edge_w = t["edge_col"].data_ptr(), t["edge_w"].data_ptr()
         n.n_slots, n.n_chunks = self.n_slots, self.n_chunks
+        n.n_rec_chunks = self.n_rec_chunks
         if self.gated:
             n.slot_gate, n.slot_row = t["slot_gate"].data_ptr(), t["slot_row"].data_ptr()
             n.gate_params, n.gate_cols = t["gate_params"].data_ptr(), t["gate_cols"].data_ptr()
@@ -341,6 +343,8 @@ def build(drive, p, B: int, n_in: int, device, pool: bool = False) -> Plan:
     slot_chunk = torch.zeros(plan.n_slots + 1, dtype=torch.int64, device=device)
     slot_chunk[1:] = torch.cumsum(per_slot, 0)
     plan.n_chunks = total
+    # the neurons' slots come first (sources are ordered neurons, then inputs)
+    plan.n_rec_chunks = int(slot_chunk[int(src_slot[N])])
     if total >= 2**31 or plan.n_edges >= 2**62:
         raise NotImplementedError("more than 2^31 chunks")
 
@@ -436,13 +440,15 @@ def fold(plan: Plan, scale: torch.Tensor, p=None) -> None:
     if "edge_w" not in t:
         t["edge_w"] = torch.empty_like(t["w_raw"])
     net = plan.net(p) if p is not None else plan.net_for_fold()
-    rc = _lib.lib().wt_fold_weights(
-        _lib.C.byref(net), _lib.C.c_void_p(t["w_raw"].data_ptr()),
-        _lib.C.c_void_p(t["chunk_path"].data_ptr()), _lib.C.c_void_p(scale.data_ptr()),
-        _lib.C.c_void_p(t["jf"].data_ptr()), _lib.C.c_void_p(plan.fx_scale.data_ptr()),
-        _lib.C.c_void_p(t["edge_w"].data_ptr()), _lib.C.c_void_p(_lib.stream_of(plan.device)),
-    )
+    with _lib.timed("wt_fold_weights"):
+        rc = _lib.lib().wt_fold_weights(
+            _lib.C.byref(net), _lib.C.c_void_p(t["w_raw"].data_ptr()),
+            _lib.C.c_void_p(t["chunk_path"].data_ptr()), _lib.C.c_void_p(scale.data_ptr()),
+            _lib.C.c_void_p(t["jf"].data_ptr()), _lib.C.c_void_p(plan.fx_scale.data_ptr()),
+            _lib.C.c_void_p(t["edge_w"].data_ptr()), _lib.C.c_void_p(_lib.stream_of(plan.device)),
+        )
     _lib.check(rc, "wt_fold_weights")
+    _lib.count_launches(1)
     plan.tensors["_scale"] = scale  # alive until the kernel has read it
 
 
