@@ -77,12 +77,14 @@ typedef struct {
      * WT_CHUNK_EDGES edges of its CSR row (a chunk is one work item) */
     const int32_t *src_slot;    /* (N + n_in + 1) */
     const int32_t *slot_chunk;  /* (n_slots + 1) */
-    const int64_t *chunk_begin; /* (n_chunks): first edge */
-    const int32_t *chunk_len;   /* (n_chunks): edges, at most WT_CHUNK_EDGES */
+    const int32_t *src_chunk;   /* (N + n_in + 1): each source's first chunk (a source's
+                                   chunks are contiguous: its slots' chunks in order) */
+    const int64_t *chunk_desc;  /* (n_chunks): first edge | edge count << 56 */
     const uint32_t *edge_col;   /* (E): target | input channel << 27 */
-    const float *edge_w;        /* (E): folded weight, times 2^s of its channel */
+    const uint64_t *edge_cw;    /* (E): edge_col | folded weight bits << 32, the weight
+                                   times 2^s of its channel (written by wt_fold_weights) */
     int32_t n_slots, n_chunks;
-    int32_t n_rec_chunks;       /* chunks of the neurons' slots (they come first) */
+    int64_t n_rec_edges;        /* edges of the neurons' pathways (they come first) */
     /* presynaptic gating (WT_F_GATED): per slot its gate (-1: none) and row */
     const int32_t *slot_gate, *slot_row;
     const float *gate_params;   /* (n_gates, 5): c, d, U, d_D, d_F */
@@ -115,11 +117,18 @@ typedef struct {
     int32_t track_b;
 } WtForward;
 
+/* One scatter work item: a chunk of a source's edges, for one trial. */
+typedef struct {
+    int64_t edge;               /* first edge */
+    uint32_t trial_len;         /* trial << 8 | edge count */
+    float amp;                  /* the spike's (or input's) value times its gating factor */
+} WtEvent;
+
 /* Scratch memory of a forward run; all of it device memory the caller allocated. */
 typedef struct {
-    unsigned long long *X;      /* (2, C, B, N) fixed-point input accumulators */
-    uint32_t *ev_item;          /* (2, ev_cap) event items: trial * n_chunks + chunk */
-    float *ev_amp;              /* (2, ev_cap) */
+    unsigned long long *X;      /* (2, C, B, Np) fixed-point input accumulators, Np = N rounded
+                                 * up to a multiple of 32; 16-byte aligned */
+    WtEvent *ev;                /* (2, ev_cap) events of two consecutive steps */
     uint32_t *ev_count;         /* (T + 1) */
     uint32_t *barrier;          /* (64) */
     int32_t *err;               /* (1): a device error code, 0 if none */
@@ -127,18 +136,18 @@ typedef struct {
     unsigned long long *edges;  /* (2) or NULL: edges traversed (recurrent, input) */
 } WtWorkspace;
 
-/* Bytes of each workspace buffer for a run of T steps (X, ev_item, ev_amp, ev_count,
- * barrier, err), written to bytes[0..5]. */
+/* Bytes of each workspace buffer for a run of T steps (X, ev, ev_count, barrier, err,
+ * edges), written to bytes[0..5]. */
 int wt_workspace_bytes(const WtNet *net, int32_t T, int64_t bytes[6]);
 
-/* Fold the per-edge weights: edge_w[e] = w[e] * scale[k(e), col(e)] * jf[k(e), c(e)] *
- * 2^s(c(e)) for every edge of every chunk, from the raw weights w and the pathway of each
- * chunk. Replaces the per-call kernel scale of the reference's Drive
+/* Fold the per-edge weights: the weight of edge_cw[e] = w[e] * scale[k(e), col(e)] *
+ * jf[k(e), c(e)] * 2^s(c(e)) for every edge of every chunk, from the raw weights w and the
+ * pathway of each chunk. Replaces the per-call kernel scale of the reference's Drive
  * (network_simulators/network.py:816-854 `_drive`, conductance/dynamics.py:95-100
  * `jumps`). */
 int wt_fold_weights(const WtNet *net, const float *w_raw, const int32_t *chunk_path,
                     const float *scale /* (K, N) */, const float *jf /* (K, C) */,
-                    const float *fx_scale /* (C) */, float *edge_w_out, void *stream);
+                    const float *fx_scale /* (C) */, uint64_t *edge_cw_out, void *stream);
 
 /* Simulate T steps: one persistent kernel. Replaces the reference's per-step launches
  * of `compact_spikes` + `recurrent_step` (network_simulators/kernels.py:132-204,

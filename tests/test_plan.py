@@ -23,9 +23,12 @@ def _walk(plan, pre_rec, pre_ff):
     X = np.zeros((plan.ch.C, N))
     src_slot = t["src_slot"].numpy()
     slot_chunk = t["slot_chunk"].numpy()
-    begin, length = t["chunk_begin"].numpy(), t["chunk_len"].numpy()
+    np.testing.assert_array_equal(t["src_chunk"].numpy(), slot_chunk[src_slot])
+    desc = t["chunk_desc"].numpy()
+    begin, length = desc & ((1 << 56) - 1), desc >> 56
     cols = t["edge_col"].numpy().astype(np.int64) & 0xFFFFFFFF
-    w = t["edge_w"].numpy().astype(np.float64)
+    w = P.edge_weights(plan).numpy().astype(np.float64)
+    assert (t["edge_cw"].numpy() & 0xFFFFFFFF == cols).all()
     values = np.concatenate([pre_rec, pre_ff])
     for j in np.nonzero(values)[0]:
         for slot in range(src_slot[j], src_slot[j + 1]):

@@ -13,6 +13,7 @@ from pathlib import Path
 LIB = Path(__file__).parent / "_lib" / "libwiretorch_b200.so"
 MAX_CHANNELS = 8
 CHUNK_EDGES = 128
+EVENT_BYTES = 16  # sizeof(WtEvent)
 
 OK, ERR_ARGS, ERR_LAUNCH, ERR_BARRIER, ERR_EVENTS, ERR_FIXED_POINT, ERR_UNSUPPORTED = range(7)
 ERRORS = {
@@ -42,9 +43,8 @@ class WtNet(C.Structure):
         ("E_syn", _f8), ("g_clip", _f8), ("mg_a", _f8), ("mg_lc", _f8),
         ("input_of", _i8), ("fx_inv", _f8),
         ("dt", C.c_float), ("surr_scale", C.c_float),
-        ("src_slot", P), ("slot_chunk", P), ("chunk_begin", P), ("chunk_len", P),
-        ("edge_col", P), ("edge_w", P),
-        ("n_slots", C.c_int32), ("n_chunks", C.c_int32), ("n_rec_chunks", C.c_int32),
+        ("src_slot", P), ("slot_chunk", P), ("src_chunk", P), ("chunk_desc", P), ("edge_col", P), ("edge_cw", P),
+        ("n_slots", C.c_int32), ("n_chunks", C.c_int32), ("n_rec_edges", C.c_int64),
         ("slot_gate", P), ("slot_row", P), ("gate_params", P), ("gate_cols", P),
         ("R", C.c_int32), ("R_f", C.c_int32),
     ]  # fmt: skip
@@ -64,7 +64,7 @@ class WtForward(C.Structure):
 
 class WtWorkspace(C.Structure):
     _fields_ = [
-        ("X", P), ("ev_item", P), ("ev_amp", P), ("ev_count", P), ("barrier", P),
+        ("X", P), ("ev", P), ("ev_count", P), ("barrier", P),
         ("err", P), ("ev_cap", C.c_int64), ("edges", P),
     ]  # fmt: skip
 

@@ -182,6 +182,7 @@ class _Simulate(torch.autograd.Function):
             _lib.check(rc, "wt_edge_grads")
             _lib.count_launches(int(need_scale or need_w) + int(need_x))
 
+        ctx.save = ctx.g_init = None  # release the saved run as soon as it is used
         grads_w = [None] * n_weights
         if need_w:
             grads_w = _dense_weight_grads(plan, cx.drive, weights, g_w, ctx.needs_input_grad[4:])
@@ -248,6 +249,10 @@ def simulate_with_grad(plan, v, g, x, drive, p, refractory, gating, adaptation,
     weights, _ = _unique_weights(drive)
     phys = [getattr(p, n) if getattr(p, n) is not None else torch.zeros(0) for n in PHYSIOLOGY]
     spikes, prob = _Simulate.apply(cx, drive.scale, x, len(weights), *weights, *phys)
+    # The outputs hold the autograd graph, which holds ``cx``: take ``out`` off it so that
+    # no reference cycle keeps a step's saved tensors alive after its backward pass.
+    out, cx.out = cx.out, None
     v_k, g_k, counter, g_a, gating_k = state
-    return engine._run(plan, cx.out, v_k, g_k, counter, g_a, gating_k, p, track, refractory,
+    cx.state = None
+    return engine._run(plan, out, v_k, g_k, counter, g_a, gating_k, p, track, refractory,
                        spikes=spikes, prob=prob if probabilities else None)  # fmt: skip

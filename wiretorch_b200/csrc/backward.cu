@@ -260,8 +260,9 @@ __global__ void edge_grads_kernel(const WtNet net, const WtEdgeGrads eg, int rec
                         amp = val * eg.f_saved[(size_t)bt * net.R_f + net.gate_cols[4 * gate + 3] + net.slot_row[slot]];
                 }
                 for (int ch = net.slot_chunk[slot]; ch < net.slot_chunk[slot + 1]; ch++) {
-                    const long long e0 = net.chunk_begin[ch];
-                    const int len = net.chunk_len[ch];
+                    const long long d = net.chunk_desc[ch];
+                    const long long e0 = d & ((1LL << 56) - 1);
+                    const int len = (int)((unsigned long long)d >> 56);
                     const int kp = eg.chunk_path[ch];
                     for (int q = lane; q < len; q += 32) {
                         const uint32_t pc = net.edge_col[e0 + q];
@@ -303,8 +304,9 @@ __global__ void input_grads_kernel(const WtNet net, const WtEdgeGrads eg) {
             }
             float part = 0.0f;
             for (int ch = net.slot_chunk[slot]; ch < net.slot_chunk[slot + 1]; ch++) {
-                const long long e0 = net.chunk_begin[ch];
-                const int len = net.chunk_len[ch];
+                const long long d = net.chunk_desc[ch];
+                const long long e0 = d & ((1LL << 56) - 1);
+                const int len = (int)((unsigned long long)d >> 56);
                 const int kp = eg.chunk_path[ch];
                 for (int q = lane; q < len; q += 32) {
                     const uint32_t pc = net.edge_col[e0 + q];

@@ -6,6 +6,7 @@
 #include "common.cuh"
 
 namespace wt {
+long long forward_x_row(int N);
 cudaError_t launch_forward_s(const WtNet &net, const WtForward &run, const WtWorkspace &ws,
                              cudaStream_t st, int grid_cap);
 cudaError_t launch_backward(const WtNet &net, const WtBackward &bw, cudaStream_t st);
@@ -13,7 +14,7 @@ cudaError_t launch_edge_grads(const WtNet &net, const WtEdgeGrads &eg, cudaStrea
 cudaError_t launch_filter(const WtFilterArgs &f, cudaStream_t st);
 cudaError_t launch_filter_grad(const WtFilterGradArgs &f, cudaStream_t st);
 cudaError_t launch_fold(const WtNet &net, const float *w_raw, const int32_t *chunk_path, const float *scale,
-                        const float *jf, const float *fx_scale, float *out, cudaStream_t st);
+                        const float *jf, const float *fx_scale, uint64_t *out, cudaStream_t st);
 }
 
 namespace {
@@ -30,14 +31,6 @@ int launch_status(cudaError_t e, const char *what) {
     return WT_ERR_LAUNCH;
 }
 
-// Grid blocks worth launching for `items` work items of the persistent kernel (0: as
-// many as can be resident); fewer blocks make the grid barrier cheaper on small nets.
-int grid_cap_for(long long items) {
-    const long long per_block = (long long)wt::kBlock * 2;
-    long long blocks = (items + per_block - 1) / per_block;
-    return blocks < 1 ? 1 : (blocks > (1 << 20) ? 0 : (int)blocks);
-}
-
 int check_net(const WtNet *n) {
     if (!n) return fail(WT_ERR_ARGS, "net is null%s");
     if (n->B <= 0 || n->N <= 0 || n->n_in < 0) return fail(WT_ERR_ARGS, "bad sizes%s");
@@ -48,7 +41,7 @@ int check_net(const WtNet *n) {
         return fail(WT_ERR_UNSUPPORTED, "trials x chunks must be below 2^32%s");
     if (!n->theta || !n->U_reset || !n->E_L || !n->C_m || !n->beta)
         return fail(WT_ERR_ARGS, "missing neuron tables%s");
-    if (!n->src_slot || !n->slot_chunk || (n->n_chunks && (!n->chunk_begin || !n->chunk_len)))
+    if (!n->src_slot || !n->slot_chunk || !n->src_chunk || (n->n_chunks && (!n->chunk_desc || !n->edge_col)))
         return fail(WT_ERR_ARGS, "missing connectivity%s");
     return WT_OK;
 }
@@ -63,24 +56,23 @@ int wt_abi_version(void) { return 1; }
 int wt_workspace_bytes(const WtNet *net, int32_t T, int64_t bytes[6]) {
     int rc = check_net(net);
     if (rc) return rc;
-    const long long BN = (long long)net->B * net->N;
     const long long cap = (long long)net->B * (net->n_chunks > 0 ? net->n_chunks : 1);
-    bytes[0] = 2LL * net->C * BN * 8;   // X
-    bytes[1] = 2LL * cap * 4;           // ev_item
-    bytes[2] = 2LL * cap * 4;           // ev_amp
-    bytes[3] = ((long long)T + 1) * 4;  // ev_count
-    bytes[4] = 64 * 4;                  // barrier
-    bytes[5] = 4;                       // err
+    bytes[0] = 2LL * net->C * net->B * wt::forward_x_row(net->N) * 8;  // X (rows padded to 32)
+    bytes[1] = 2LL * cap * (long long)sizeof(WtEvent);  // ev
+    bytes[2] = ((long long)T + 1) * 4;                // ev_count
+    bytes[3] = 64 * 4;                                // barrier
+    bytes[4] = 4;                                     // err
+    bytes[5] = 2 * 8;                                 // edges
     return WT_OK;
 }
 
 int wt_fold_weights(const WtNet *net, const float *w_raw, const int32_t *chunk_path, const float *scale,
-                    const float *jf, const float *fx_scale, float *edge_w_out, void *stream) {
+                    const float *jf, const float *fx_scale, uint64_t *edge_cw_out, void *stream) {
     int rc = check_net(net);
     if (rc) return rc;
-    if (net->n_chunks && (!w_raw || !chunk_path || !scale || !jf || !fx_scale || !edge_w_out || !net->edge_col))
+    if (net->n_chunks && (!w_raw || !chunk_path || !scale || !jf || !fx_scale || !edge_cw_out || !net->edge_col))
         return fail(WT_ERR_ARGS, "missing fold buffers%s");
-    return launch_status(wt::launch_fold(*net, w_raw, chunk_path, scale, jf, fx_scale, edge_w_out,
+    return launch_status(wt::launch_fold(*net, w_raw, chunk_path, scale, jf, fx_scale, edge_cw_out,
                                          (cudaStream_t)stream),
                          "fold");
 }
@@ -110,16 +102,17 @@ int wt_forward(const WtNet *net, const WtForward *run, const WtWorkspace *ws, vo
     if ((f & WT_F_TRACK) && (!run->track_v || !run->track_I || !run->track_g ||
                              ((f & WT_F_ADAPT) && !run->track_a)))
         return fail(WT_ERR_ARGS, "tracking buffers%s");
-    if (!ws->X || !ws->ev_item || !ws->ev_amp || !ws->ev_count || !ws->barrier || !ws->err)
+    if (net->n_chunks && !net->edge_cw) return fail(WT_ERR_ARGS, "missing folded edges%s");
+    if (!ws->X || !ws->ev || !ws->ev_count || !ws->barrier || !ws->err)
         return fail(WT_ERR_ARGS, "workspace buffers%s");
     if (ws->ev_cap < (long long)net->B * net->n_chunks) return fail(WT_ERR_ARGS, "event capacity too small%s");
+    if (((uintptr_t)ws->X & 15) || ((uintptr_t)ws->ev & 15))
+        return fail(WT_ERR_ARGS, "workspace X and ev must be 16-byte aligned%s");
     if (run->T == 0) return WT_OK;
     cudaStream_t st = (cudaStream_t)stream;
     cudaError_t e = cudaMemsetAsync(ws->barrier, 0, 64 * 4, st);
     if (e != cudaSuccess) return launch_status(e, "barrier reset");
-    const long long Np = (net->N + 31) & ~31, Ip = (net->n_in + 31) & ~31;
-    const long long items = (long long)net->B * (Np > Ip ? Np : Ip);
-    return launch_status(wt::launch_forward_s(*net, *run, *ws, st, grid_cap_for(items)), "forward");
+    return launch_status(wt::launch_forward_s(*net, *run, *ws, st, 0), "forward");
 }
 
 int wt_backward(const WtNet *net, const WtBackward *bw, void *stream) {

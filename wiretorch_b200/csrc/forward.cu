@@ -3,9 +3,26 @@
 // conductance/dynamics.py:146-237, which its Triton kernels scan_forward,
 // compact_spikes and recurrent_step implement on CUDA).
 //
+// Work is cut into warp items: 32 consecutive neurons of one trial. The items, ordered
+// neuron group by group and trial by trial within a group, are split into equal
+// contiguous runs, one per warp of the grid, for the whole launch; a warp keeps its
+// current group's constants in registers. When the warps' state fits in shared memory
+// ("resident") it is read from HBM once at the start and written back once at the end;
+// otherwise it streams through HBM every step. Every step, each warp stages its items'
+// inputs (and streamed state) through a ring of shared-memory slots with asynchronous
+// copies issued several items ahead, so that a warp keeps kilobytes of loads in flight
+// while it computes. A channel whose rise component does not decay (a single-exponential
+// synapse, tau_rise = 0) keeps no rise state: its rise is jump_r X of the previous step.
+//
 // Work per step t, over the whole grid, with one grid barrier between steps:
 //
-//   phase A (each (trial, neuron), coalesced over neurons):
+//   scatter (all warps): the events of step t — each a (trial, chunk of at most
+//     WT_CHUNK_EDGES edges of one source's CSR row) — into X_t, the per
+//     (input channel, trial, neuron) fixed-point accumulators: 64-bit integer
+//     reductions, so the sum, and every result, is independent of the order in
+//     which events land (bit-for-bit reproducible). The events were emitted during
+//     step t - 1, so the reductions are issued first and drain while the warps go on.
+//   update (every item of the warp, coalesced over neurons):
 //     g_t = decay g_{t-1} + jump X_{t-1}           (completes the previous step's input)
 //     s_t = H(v_t - theta) (1 - held)               (or escape noise)
 //     v_{t+1} = exponential-Euler membrane step, reset where s_t or held
@@ -16,27 +33,51 @@
 //     Input columns likewise emit x_{t+1}'s non-zero entries.
 //   Data that crosses blocks within the kernel (event lists, accumulators) is read
 //   with L2-only loads: an SM's L1 is not coherent with the other SMs' writes.
-//   phase B (all warps): scatter the events of step t — each a (trial, chunk of at
-//     most WT_CHUNK_EDGES edges of one source's CSR row) — into X_t, the per
-//     (input channel, trial, neuron) fixed-point accumulators: 64-bit integer
-//     reductions, so the sum, and every result, is independent of the order in
-//     which events land (bit-for-bit reproducible).
 //
 // A presynaptic pathway with gating (short-term plasticity, receptor saturation:
 // network.py:186-223) steps its state when its source's spike (or input) of the next
 // step is known, and scales the events by the factor.
+#include <algorithm>
+
 #include "common.cuh"
 
 namespace wt {
+
+// Geometry of a launch, chosen by the host (see geometry_for).
+struct Geometry {
+    long long W;                  // warp items: groups x B
+    int groups, Np;               // 32-neuron groups; accumulator row stride (N rounded up to 32)
+    int resident;                 // state in shared memory
+    int ks;                       // state words per item
+    int w_cnt, w_ga, w_gd, w_gr;  // word offsets: counter, adaptation, decay, rise
+    int max_items;                // most items of one warp
+    int D;                        // ring slots per warp (copies issued D items ahead)
+    int slot_rows, warp_rows;     // 128-byte rows of a ring slot, of a warp's shared memory
+};
+
 namespace {
 
-struct Tables {
-    // per-channel constants, copied to shared memory at launch
-    float dr[WT_MAX_CHANNELS], dd[WT_MAX_CHANNELS], jr[WT_MAX_CHANNELS], jd[WT_MAX_CHANNELS];
-    float E[WT_MAX_CHANNELS], clip[WT_MAX_CHANNELS], mga[WT_MAX_CHANNELS], mglc[WT_MAX_CHANNELS];
-    float fx_inv[WT_MAX_CHANNELS];
-    int in[WT_MAX_CHANNELS];
-};
+// Asynchronous global -> shared copies (cp.async), grouped per thread. The 16-byte form
+// reads through L2 only (data written by other SMs); the 4-byte form is used for data
+// this SM alone writes.
+__device__ __forceinline__ void cp_async16(void *dst, const void *src) {
+    const unsigned d = (unsigned)__cvta_generic_to_shared(dst);
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(d), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async4(void *dst, const void *src) {
+    const unsigned d = (unsigned)__cvta_generic_to_shared(dst);
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(d), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+// Waits until at most `pending` of this thread's groups are in flight.
+__device__ __forceinline__ void cp_async_wait(int pending) {
+    switch (pending) {
+        case 0: asm volatile("cp.async.wait_group 0;" ::: "memory"); break;
+        case 1: asm volatile("cp.async.wait_group 1;" ::: "memory"); break;
+        case 2: asm volatile("cp.async.wait_group 2;" ::: "memory"); break;
+        default: asm volatile("cp.async.wait_group 3;" ::: "memory"); break;
+    }
+}
 
 // Presynaptic gating of one slot for one trial (network.py:186-223): steps the state
 // with the source's spike (or input) `s` and returns the factor of its input.
@@ -114,13 +155,52 @@ __device__ void emit(const WtNet &net, const WtForward &run, const WtWorkspace &
         const bool fits = off + cnt <= ws.ev_cap;  // per lane; no early exit before the
         if (!fits && cnt) set_error(ws.err, WT_ERR_EVENTS);  // next round's collectives
         if (fits) {
-            uint32_t *items = ws.ev_item + (size_t)(step & 1) * ws.ev_cap;
-            float *amps = ws.ev_amp + (size_t)(step & 1) * ws.ev_cap;
-            const uint32_t key = (uint32_t)b * (uint32_t)net.n_chunks;
+            WtEvent *evs = ws.ev + (size_t)(step & 1) * ws.ev_cap;
             for (int q = 0; q < cnt; q++) {
-                items[off + q] = key + (uint32_t)(c0 + q);
-                amps[off + q] = amp;
+                const long long d = net.chunk_desc[c0 + q];
+                WtEvent e;
+                e.edge = d & ((1LL << 56) - 1);
+                e.trial_len = ((uint32_t)b << 8) | (uint32_t)((unsigned long long)d >> 56);
+                e.amp = amp;
+                evs[off + q] = e;
             }
+        }
+    }
+}
+
+// Emission of ungated sources: a source's chunks are contiguous (src_chunk), so the warp
+// reserves room for all its lanes' events with one atomic, then writes each spiking
+// lane's events with all 32 lanes. `on`: the lane's source j fires with `value`.
+__device__ __forceinline__ void emit_fast(const WtNet &net, const WtWorkspace &ws, int step, bool on, int b,
+                                          int j, float value, int lane) {
+    unsigned m = __ballot_sync(kFull, on);
+    if (!m) return;
+    int c0 = 0, cnt = 0;
+    if (on) {
+        c0 = net.src_chunk[j];
+        cnt = net.src_chunk[j + 1] - c0;
+    }
+    const int incl = warp_inclusive_sum(cnt, lane);
+    const int total = __shfl_sync(kFull, incl, 31);
+    if (total == 0) return;
+    unsigned base = 0;
+    if (lane == 31) base = atomicAdd(&ws.ev_count[step], (unsigned)total);
+    base = __shfl_sync(kFull, base, 31);
+    int4 *evs = reinterpret_cast<int4 *>(ws.ev + (size_t)(step & 1) * ws.ev_cap);
+    while (m) {
+        const int l = __ffs(m) - 1;
+        m &= m - 1;
+        const int lc0 = __shfl_sync(kFull, c0, l), lcnt = __shfl_sync(kFull, cnt, l);
+        const long long off = (long long)base + __shfl_sync(kFull, incl, l) - lcnt;
+        const int amp = __float_as_int(__shfl_sync(kFull, value, l));
+        for (int q = lane; q < lcnt; q += 32) {
+            if (off + q >= ws.ev_cap) {
+                set_error(ws.err, WT_ERR_EVENTS);
+                break;
+            }
+            const unsigned long long d = (unsigned long long)net.chunk_desc[lc0 + q];
+            evs[off + q] = make_int4((int)(unsigned)d, (int)(unsigned)((d >> 32) & 0xffffffu),
+                                     (int)(((unsigned)b << 8) | (unsigned)(d >> 56)), amp);
         }
     }
 }
@@ -139,110 +219,355 @@ __device__ __forceinline__ float spike_of(float v, float theta, int counter, flo
     return s;
 }
 
-template <int S>
-__global__ void __launch_bounds__(kBlock) forward_kernel(const WtNet net, const WtForward run,
-                                                        const WtWorkspace ws) {
-    __shared__ Tables tab;
-    if (threadIdx.x < WT_MAX_CHANNELS) {
-        const int c = threadIdx.x;
-        tab.dr[c] = net.decay_r[c];
-        tab.dd[c] = net.decay_d[c];
-        tab.jr[c] = net.jump_r[c];
-        tab.jd[c] = net.jump_d[c];
-        tab.E[c] = net.E_syn[c];
-        tab.clip[c] = net.g_clip[c];
-        tab.mga[c] = net.mg_a[c];
-        tab.mglc[c] = net.mg_lc[c];
-        tab.fx_inv[c] = net.fx_inv[c];
-        tab.in[c] = net.input_of[c];
-    }
-    __syncthreads();
+static_assert(WT_CHUNK_EDGES <= 128, "a chunk's edges take at most four per lane");
+constexpr int kWarps = 16;                // warps per block of the forward kernel
+constexpr int kThreads = kWarps * 32;     // one block per SM
+constexpr int kMaxRing = 4;               // deepest ring of staged items
 
-    const int B = net.B, N = net.N, n_in = net.n_in, C = net.C, T = run.T;
+// Feature bits of a specialised kernel: the refractory period and saving for the backward
+// pass known at compile time; everything else (adaptation, Mg block, escape noise,
+// gating, probabilities, tracking, saved input) in the generic variant, tested at run time.
+constexpr int kRef = 1, kSave = 2, kGeneric = 4;
+
+// A warp's position in its run of items: neuron group g, trial b, and the trial's row
+// offsets in the (B, N) state, the (B, Np) accumulators and the (B, T_total, N) outputs.
+struct Cursor {
+    int g, b;
+    size_t bN, bNp, bTN;
+    __device__ void next(int B, int N, int Np, size_t TN) {
+        if (++b == B) {
+            b = 0;
+            ++g;
+            bN = bNp = bTN = 0;
+        } else {
+            bN += N;
+            bNp += Np;
+            bTN += TN;
+        }
+    }
+};
+
+// A neuron's constants (conductance/dynamics.py:116-143): the leak's rate from its decay
+// beta, and g_L = C_m rate.
+struct NeuronConsts {
+    float theta, U_reset, E_L, Cm, rate, g_L, adapt, a_decay, E_a;
+    int n_ref;
+};
+
+template <int S, int FEAT>
+__global__ void __launch_bounds__(kThreads, 1) forward_kernel(const WtNet net, const WtForward run,
+                                                             const WtWorkspace ws, const Geometry geo) {
+    extern __shared__ __align__(16) float smem[];
+    constexpr bool GEN = FEAT & kGeneric;
     const int flags = run.flags;
-    const bool gated = flags & WT_F_GATED;
-    const int Np = (N + 31) & ~31, Ip = (n_in + 31) & ~31;  // padded: a warp = one word
-    const long long itemsN = (long long)B * Np, itemsI = (long long)B * Ip;
+    const bool REF = GEN ? (flags & WT_F_REFRACTORY) != 0 : (FEAT & kRef) != 0;
+    const bool SAVE = GEN ? (flags & WT_F_SAVE) != 0 : (FEAT & kSave) != 0;
+    const bool ADAPT = GEN && (flags & WT_F_ADAPT);
+    const bool MG = GEN && (flags & WT_F_MG_BLOCK);
+    const bool SAMPLE = GEN && (flags & WT_F_SAMPLE);
+    const bool gated = GEN && (flags & WT_F_GATED);
+    const bool PROB = GEN && (flags & WT_F_PROB);
+    const bool TRACK = GEN && (flags & WT_F_TRACK);
+    const bool SAVE_IN = GEN && (flags & WT_F_SAVE_INPUT);
+
+    const int B = net.B, N = net.N, n_in = net.n_in, C = net.C, T = run.T, Np = geo.Np;
+    const int Ip = (n_in + 31) & ~31;
+    const long long itemsI = (long long)B * Ip;
     const long long nthreads = (long long)gridDim.x * blockDim.x;
     const long long gtid = (long long)blockIdx.x * blockDim.x + threadIdx.x;
     const int lane = threadIdx.x & 31;
     const long long warp0 = gtid - lane;
     const long long gwarp = gtid >> 5, nwarps = nthreads >> 5;
-    const size_t BN = (size_t)B * N;
-    const int words = Np >> 5;
+    const size_t BNp = (size_t)B * Np;
+    const size_t TN = (size_t)run.T_total * N;  // one trial's (T, N) plane
+    const int words = (N + 31) >> 5;
     const float dt = net.dt, ksur = net.surr_scale;
+    const bool RES = geo.resident;
+    const int D = geo.D, ks = geo.ks, w_cnt = geo.w_cnt, w_ga = geo.w_ga, w_gd = geo.w_gd;
+    const int slot_words = geo.slot_rows * 32;
     GridBarrier bar(ws.barrier, gridDim.x);
 
-    // Phase 0: empty accumulators and event counts.
-    for (long long i = gtid; i < 2LL * C * (long long)BN; i += nthreads) ws.X[i] = 0ull;
+    // Per channel: the input channel feeding it, that input's fixed-point scale, and the
+    // state word of its rise component (-1: it does not decay and keeps none).
+    int in_c[S], rw[S];
+    float fx_c[S];
+    {
+        int r = 0;
+#pragma unroll
+        for (int c = 0; c < S; c++) {
+            in_c[c] = net.input_of[c];
+            fx_c[c] = in_c[c] >= 0 ? net.fx_inv[in_c[c]] : 0.0f;
+            rw[c] = net.decay_r[c] != 0.0f ? geo.w_gr + r++ : -1;
+        }
+    }
+
+    // This warp's items, and its shared memory: resident state [item][word][lane], then
+    // the ring of D slots, each [input channel int64 x 32][streamed state word x 32].
+    const long long lo = geo.W * gwarp / nwarps, hi = geo.W * (gwarp + 1) / nwarps;
+    const int nitems = (int)(hi - lo);
+    Cursor start;
+    start.g = (int)(lo / B);
+    start.b = (int)(lo % B);
+    start.bN = (size_t)start.b * N;
+    start.bNp = (size_t)start.b * Np;
+    start.bTN = (size_t)start.b * TN;
+    float *wsm = smem + (size_t)(threadIdx.x >> 5) * geo.warp_rows * 32;
+    float *ring = wsm + (RES ? (size_t)geo.max_items * ks * 32 : 0);
+    // a lane's 16-byte pieces of an item's accumulator rows: piece k = lane + 32 i covers
+    // channel k / 16, neurons 2 (k % 16) and 2 (k % 16) + 1 of the group
+    const size_t x_goff = (size_t)(lane >> 4) * BNp + (lane & 15) * 2;
+    const int x_soff = (lane >> 4) * 64 + (lane & 15) * 4;
+
+    auto consts_of = [&](int n) {
+        NeuronConsts k{};
+        k.Cm = 1.0f;
+        if (n < N) {
+            k.theta = net.theta[n];
+            k.U_reset = net.U_reset[n];
+            k.E_L = net.E_L[n];
+            k.Cm = net.C_m[n];
+            k.rate = -log1pf(net.beta[n] - 1.0f) / dt;
+            k.g_L = k.Cm * k.rate;
+            k.n_ref = REF ? net.n_ref[n] : 0;
+            if (ADAPT) {
+                k.adapt = net.adapt[n];
+                k.a_decay = net.adapt_decay[n];
+                k.E_a = net.E_adapt[n];
+            }
+        }
+        return k;
+    };
+    // Stage item j (at cursor q) into ring slot `wr`: the previous step's input of its C
+    // channels (when `with_x`), and its state when streamed. One copy group per call.
+    auto issue = [&](int j, const Cursor &q, int wr, const unsigned long long *Xsrc, bool with_x) {
+        if (j < nitems) {
+            float *slot = ring + wr * slot_words;
+            if (with_x) {
+                const unsigned long long *src = Xsrc + q.bNp + (size_t)q.g * 32 + x_goff;
+                float *dst = slot + x_soff;
+                for (int k = lane; k < C * 16; k += 32, src += 2 * BNp, dst += 128) cp_async16(dst, src);
+            }
+            const int n = q.g * 32 + lane;
+            if (!RES && n < N) {
+                const size_t o = q.bN + n;
+                const float *g_b = run.g + q.bN * 2 * S + n;
+                float *st = slot + 2 * C * 32 + lane;
+                cp_async4(st, run.v + o);
+                if (REF) cp_async4(st + w_cnt * 32, run.counter + o);
+                if (ADAPT) cp_async4(st + w_ga * 32, run.g_a + o);
+#pragma unroll
+                for (int c = 0; c < S; c++) {
+                    cp_async4(st + (w_gd + c) * 32, g_b + (size_t)(S + c) * N);
+                    if (rw[c] >= 0) cp_async4(st + rw[c] * 32, g_b + (size_t)c * N);
+                }
+            }
+        }
+        cp_async_commit();
+    };
+    auto emit_any = [&](int step, bool valid, int b, int j, float value) {
+        if (gated)
+            emit(net, run, ws, step, valid, b, j, value, true, lane);
+        else
+            emit_fast(net, ws, step, valid && value != 0.0f, b, j, value, lane);
+    };
+
+    // Phase 0: empty accumulators and event counts; resident state.
+    for (long long i = gtid; i < 2LL * C * (long long)BNp; i += nthreads) ws.X[i] = 0ull;
     for (long long i = gtid; i <= T; i += nthreads) ws.ev_count[i] = 0u;
+    if (RES) {
+        Cursor q = start;
+        float *rp = wsm + lane;
+        for (int j = 0; j < nitems; j++, q.next(B, N, Np, TN), rp += ks * 32) {
+            const int n = q.g * 32 + lane;
+            if (n >= N) continue;
+            const size_t o = q.bN + n;
+            const float *g_b = run.g + q.bN * 2 * S + n;
+            rp[0] = run.v[o];
+            if (REF) rp[w_cnt * 32] = __int_as_float(run.counter[o]);
+            if (ADAPT) rp[w_ga * 32] = run.g_a[o];
+#pragma unroll
+            for (int c = 0; c < S; c++) {
+                rp[(w_gd + c) * 32] = g_b[(size_t)(S + c) * N];
+                if (rw[c] >= 0) rp[rw[c] * 32] = g_b[(size_t)c * N];
+            }
+        }
+    }
     if (!bar.sync(ws.err)) return;
 
+    const int sflags = (REF ? WT_F_REFRACTORY : 0) | (SAMPLE ? WT_F_SAMPLE : 0);
     // Emit step 0's events: the spikes of the state entering the run, and x at t0.
-    for (long long base = warp0; base < itemsN; base += nthreads) {
-        const long long i = base + lane;
-        const int b = (int)(i / Np), n = (int)(i % Np);
-        const bool valid = n < N;
-        float s = 0.0f;
-        if (valid) {
-            const size_t o = (size_t)b * N + n;
-            float held;
-            const int cnt = (flags & WT_F_REFRACTORY) ? run.counter[o] : 0;
-            const float u = (flags & WT_F_SAMPLE) ? run.noise[((size_t)b * run.T_total + run.t0) * N + n] : 0.0f;
-            s = spike_of(run.v[o], net.theta[n], cnt, u, flags, ksur, held);
+    {
+        Cursor q = start;
+        int g_k = -1;
+        NeuronConsts k{};
+        const float *rp = wsm + lane;
+        for (int j = 0; j < nitems; j++, q.next(B, N, Np, TN), rp += ks * 32) {
+            const int n = q.g * 32 + lane;
+            const bool valid = n < N;
+            if (q.g != g_k) {
+                k = consts_of(n);
+                g_k = q.g;
+            }
+            float s = 0.0f;
+            if (valid) {
+                const size_t o = q.bN + n;
+                const float v = RES ? rp[0] : run.v[o];
+                const int cnt = REF ? (RES ? __float_as_int(rp[w_cnt * 32]) : run.counter[o]) : 0;
+                const float u01 = SAMPLE ? run.noise[q.bTN + (size_t)run.t0 * N + n] : 0.0f;
+                float held;
+                s = spike_of(v, k.theta, cnt, u01, sflags, ksur, held);
+            }
+            emit_any(0, valid, q.b, n, s);
         }
-        emit(net, run, ws, 0, valid, b, n, s, gated, lane);
     }
     for (long long base = warp0; base < itemsI; base += nthreads) {
         const long long i = base + lane;
         const int b = (int)(i / Ip), c = (int)(i % Ip);
         const bool valid = c < n_in;
         const float xv = valid ? run.x[((size_t)b * run.T_total + run.t0) * n_in + c] : 0.0f;
-        emit(net, run, ws, 0, valid, b, N + c, xv, gated, lane);
+        emit_any(0, valid, b, N + c, xv);
     }
     if (!bar.sync(ws.err)) return;
 
     for (int t = 0; t < T; t++) {
         const int t_abs = run.t0 + t;
         const bool emit_next = t + 1 < T;
-        // ---------------- phase A: the neurons ----------------
-        for (long long base = warp0; base < itemsN; base += nthreads) {
-            const long long i = base + lane;
-            const int b = (int)(i / Np), n = (int)(i % Np);
+        const bool has_x = t > 0;
+        unsigned long long *Xprev = ws.X + (size_t)((t + 1) & 1) * C * BNp;  // X_{t-1}
+        // The first D items' copies go out now and land while the warp scatters.
+        Cursor qi = start;
+        int wr = 0;
+        for (int d = 0; d < D; d++) {
+            issue(d, qi, wr, Xprev, has_x);
+            qi.next(B, N, Np, TN);
+            if (++wr == D) wr = 0;
+        }
+
+        // ---------------- scatter the events of step t into X_t ----------------
+        // Step t's events were emitted during step t - 1 and X_t's buffer emptied then.
+        // The events go round the warps; a warp reads up to 32 of its events at once (one
+        // per lane, from L2: other blocks wrote them), then walks them one by one, loading
+        // the next event's edges before it issues the current one's reductions.
+        {
+            const long long count = min((long long)*reinterpret_cast<volatile unsigned *>(&ws.ev_count[t]),
+                                        (long long)ws.ev_cap);  // never above: one event per (trial, chunk)
+            const WtEvent *evs = ws.ev + (size_t)(t & 1) * ws.ev_cap;
+            unsigned long long *X = ws.X + (size_t)(t & 1) * C * BNp;
+            for (long long base = gwarp; base < count; base += nwarps * 32) {
+                // lane k holds event base + k nwarps: the events go round the warps
+                int4 raw = make_int4(0, 0, 0, 0);
+                const long long mine = base + lane * nwarps;
+                if (mine < count) raw = __ldcg(reinterpret_cast<const int4 *>(evs + mine));
+                const int ne = (int)min(32LL, (count - base + nwarps - 1) / nwarps);
+                unsigned long long cw[4], cw_n[4];
+                auto load = [&](int e, unsigned long long *dst) {
+                    const unsigned x = __shfl_sync(kFull, raw.x, e), y = __shfl_sync(kFull, raw.y, e);
+                    const int len = __shfl_sync(kFull, raw.z, e) & 255;
+                    const long long e0 = ((long long)y << 32) | x;
+#pragma unroll
+                    for (int u = 0; u < 4; u++) {
+                        const int q = lane + 32 * u;
+                        dst[u] = q < len ? __ldg(net.edge_cw + e0 + q) : 0ull;
+                    }
+                };
+                load(0, cw_n);
+                for (int e = 0; e < ne; e++) {
+                    const unsigned bl = (unsigned)__shfl_sync(kFull, raw.z, e);
+                    const float amp = __int_as_float(__shfl_sync(kFull, raw.w, e));
+                    const int len = (int)(bl & 255u);
+#pragma unroll
+                    for (int u = 0; u < 4; u++) cw[u] = cw_n[u];
+                    if (e + 1 < ne) load(e + 1, cw_n);
+                    unsigned long long *Xb = X + (size_t)(bl >> 8) * Np;
+                    if (ws.edges) {  // counting edges (instrumented runs)
+                        const unsigned x = __shfl_sync(kFull, raw.x, e), y = __shfl_sync(kFull, raw.y, e);
+                        if (lane == 0)
+                            atomicAdd(ws.edges + ((((long long)y << 32) | x) >= net.n_rec_edges),
+                                      (unsigned long long)len);
+                    }
+#pragma unroll
+                    for (int u = 0; u < 4; u++) {
+                        if (lane + 32 * u >= len) break;
+                        const uint32_t col = (uint32_t)cw[u];
+                        const float prod = __uint_as_float((uint32_t)(cw[u] >> 32)) * amp;
+                        if (fabsf(prod) >= 0x1p62f) {
+                            set_error(ws.err, WT_ERR_FIXED_POINT);
+                            continue;
+                        }
+                        atomicAdd(Xb + (size_t)(col >> 27) * BNp + (col & 0x7ffffffu),
+                                  (unsigned long long)__float2ll_rn(prod));
+                    }
+                }
+            }
+        }
+
+        // ---------------- the neurons: step t, and the spikes of step t + 1 ----------------
+        Cursor q = start;
+        int g_k = -1, rd = 0;
+        NeuronConsts k{};
+        float *rp = wsm + lane;
+        const size_t tN = (size_t)t_abs * N;
+        for (int j = 0; j < nitems; j++) {
+            const int b = q.b;
+            const int n = q.g * 32 + lane;
             const bool valid = n < N;
+            if (q.g != g_k) {
+                k = consts_of(n);
+                g_k = q.g;
+            }
+            // item j's slot: wait for its copies (this lane's, then the warp's)
+            cp_async_wait(D - 1);
+            __syncwarp();
+            const float *slot = ring + rd * slot_words;
+            const long long *sx = reinterpret_cast<const long long *>(slot) + lane;
+            float xin[S];
+#pragma unroll
+            for (int c = 0; c < S; c++) xin[c] = (has_x && in_c[c] >= 0) ? __ll2float_rn(sx[in_c[c] * 32]) * fx_c[c] : 0.0f;
+            float xall[GEN ? WT_MAX_CHANNELS : 1];
+            if (SAVE_IN && has_x)
+                for (int c = 0; c < C; c++) xall[c] = __ll2float_rn(sx[c * 32]) * net.fx_inv[c];
+            // the item's state: resident, or staged in its slot, words 32 floats apart
+            const float *src = RES ? rp : slot + 2 * C * 32 + lane;
+            const float v = src[0];
+            int cnt = REF ? __float_as_int(src[w_cnt * 32]) : 0;
+            float ga = ADAPT ? src[w_ga * 32] : 0.0f;
+            float gr[S], gd[S];
+#pragma unroll
+            for (int c = 0; c < S; c++) {
+                gd[c] = src[(w_gd + c) * 32];
+                gr[c] = rw[c] >= 0 ? src[rw[c] * 32] : 0.0f;
+            }
+            __syncwarp();  // the slot is free: stage item j + D into it
+            issue(j + D, qi, wr, Xprev, has_x);
+            qi.next(B, N, Np, TN);
+            if (++wr == D) wr = 0;
+            if (++rd == D) rd = 0;
+
+            const size_t o = q.bN + n;
+            const size_t out = q.bTN + tN + n;
             float s = 0.0f, held = 0.0f, s_next = 0.0f;
             if (valid) {
-                const size_t o = (size_t)b * N + n;
-                float v = run.v[o];
-                float gr[S], gd[S];
-                float *g_b = run.g + (size_t)b * 2 * S * N + n;
+                float *g_b = run.g + q.bN * 2 * S + n;
+                if (!has_x) {  // a rise that does not decay is known only entering the run
 #pragma unroll
-                for (int c = 0; c < S; c++) {
-                    gr[c] = g_b[(size_t)c * N];
-                    gd[c] = g_b[(size_t)(S + c) * N];
-                }
-                if (t > 0) {  // the input of step t - 1 completes g_t
-                    const unsigned long long *Xp = ws.X + (size_t)((t - 1) & 1) * C * BN + o;
+                    for (int c = 0; c < S; c++)
+                        if (rw[c] < 0) gr[c] = g_b[(size_t)c * N];
+                } else {  // the input of step t - 1 completes g_t
 #pragma unroll
                     for (int c = 0; c < S; c++) {
-                        gr[c] = gr[c] * tab.dr[c];
-                        gd[c] = gd[c] * tab.dd[c];
-                        const int in = tab.in[c];
-                        if (in >= 0) {
-                            const float xin =
-                                __ll2float_rn((long long)__ldcg(Xp + (size_t)in * BN)) * tab.fx_inv[in];
-                            gr[c] = gr[c] + tab.jr[c] * xin;
-                            gd[c] = gd[c] + tab.jd[c] * xin;
+                        gr[c] = gr[c] * net.decay_r[c];
+                        gd[c] = gd[c] * net.decay_d[c];
+                        if (in_c[c] >= 0) {
+                            gr[c] = gr[c] + net.jump_r[c] * xin[c];
+                            gd[c] = gd[c] + net.jump_d[c] * xin[c];
                         }
                     }
-                    unsigned long long *Xz = ws.X + (size_t)((t - 1) & 1) * C * BN + o;
-                    for (int c = 0; c < C; c++) {
-                        if (flags & WT_F_SAVE_INPUT)
-                            run.X_saved[(((size_t)b * run.T_total + t_abs - 1) * C + c) * N + n] =
-                                __ll2float_rn((long long)__ldcg(Xz + (size_t)c * BN)) * tab.fx_inv[c];
-                        Xz[(size_t)c * BN] = 0ull;
-                    }
-                    if ((flags & WT_F_TRACK) && (run.track_b < 0 || run.track_b == b)) {
+                    unsigned long long *xz = Xprev + q.bNp + n;
+                    for (int c = 0; c < C; c++, xz += BNp) *xz = 0ull;
+                    if (SAVE_IN)
+                        for (int c = 0; c < C; c++)
+                            run.X_saved[(((size_t)b * run.T_total + t_abs - 1) * C + c) * N + n] = xall[c];
+                    if (TRACK && (run.track_b < 0 || run.track_b == b)) {
                         const int bt = run.track_b < 0 ? b : 0;
                         float *tg = run.track_g + (((size_t)bt * run.T_total + t_abs - 1) * N + n) * 2 * S;
 #pragma unroll
@@ -252,165 +577,147 @@ __global__ void __launch_bounds__(kBlock) forward_kernel(const WtNet net, const 
                         }
                     }
                 }
-                int cnt = (flags & WT_F_REFRACTORY) ? run.counter[o] : 0;
-                const float theta = net.theta[n];
-                const float u = (flags & WT_F_SAMPLE) ? run.noise[((size_t)b * run.T_total + t_abs) * N + n] : 0.0f;
-                s = spike_of(v, theta, cnt, u, flags, ksur, held);
+                const float u01 = SAMPLE ? run.noise[out] : 0.0f;
+                s = spike_of(v, k.theta, cnt, u01, sflags, ksur, held);
                 // membrane (conductance/dynamics.py:116-143), float32, in its order
                 float Gt[S];
                 float G = 0.0f, Isum = 0.0f;
 #pragma unroll
                 for (int c = 0; c < S; c++) {
                     float gs = gr[c] + gd[c];
-                    gs = fminf(fmaxf(gs, 0.0f), tab.clip[c]);
-                    if (flags & WT_F_MG_BLOCK) gs = gs * sigmoid(tab.mga[c] * v - tab.mglc[c]);
+                    gs = fminf(fmaxf(gs, 0.0f), net.g_clip[c]);
+                    if (MG) gs = gs * sigmoid(net.mg_a[c] * v - net.mg_lc[c]);
                     Gt[c] = gs;
                 }
 #pragma unroll
                 for (int c = 0; c < S; c++) G = G + Gt[c];
 #pragma unroll
-                for (int c = 0; c < S; c++) Isum = Isum + Gt[c] * (v - tab.E[c]);
-                const float Cm = net.C_m[n];
-                const float rate = -log1pf(net.beta[n] - 1.0f) / dt;
-                const float g_L = Cm * rate;
-                const float I_leak = g_L * (v - net.E_L[n]);
+                for (int c = 0; c < S; c++) Isum = Isum + Gt[c] * (v - net.E_syn[c]);
+                const float I_leak = k.g_L * (v - k.E_L);
                 float J = Isum + I_leak;
-                float ga = 0.0f;
-                if (flags & WT_F_ADAPT) {
-                    ga = run.g_a[o];
+                if (ADAPT) {
                     G = G + ga;
-                    J = J + ga * (v - net.E_adapt[n]);
+                    J = J + ga * (v - k.E_a);
                 }
-                const float xx = dt * rate + dt * G / Cm;
-                const float step = -expm1f(-xx) / (g_L + G);
-                const float r = fmaxf(s, held);
-                const float U_reset = net.U_reset[n];
-                const float v_next = (v - step * J) * (1.0f - r) + U_reset * r;
-
-                if (flags & WT_F_SAVE) {
-                    const size_t so = ((size_t)b * run.T_total + t_abs) * N + n;
-                    run.v_saved[so] = v;
-                    float *Gs = run.G_saved + ((size_t)b * run.T_total + t_abs) * S * N + n;
+                const float xx = dt * k.rate + dt * G / k.Cm;
+                const float step = -expm1f(-xx) / (k.g_L + G);
+                const float rr = fmaxf(s, held);
+                const float v_next = (v - step * J) * (1.0f - rr) + k.U_reset * rr;
+                if (SAVE) {
+                    run.v_saved[out] = v;
+                    float *Gs = run.G_saved + (q.bTN + tN) * S + n;
 #pragma unroll
                     for (int c = 0; c < S; c++) Gs[(size_t)c * N] = gr[c] + gd[c];
-                    if (flags & WT_F_ADAPT) run.a_saved[so] = ga;
+                    if (ADAPT) run.a_saved[out] = ga;
                 }
-                if (flags & WT_F_REFRACTORY) {
+                if (REF) {
                     const int c1 = cnt - 1;
-                    cnt = s > 0.0f ? net.n_ref[n] : (c1 > 0 ? c1 : 0);
-                    run.counter[o] = cnt;
+                    cnt = s > 0.0f ? k.n_ref : (c1 > 0 ? c1 : 0);
                 }
-                if (flags & WT_F_ADAPT) {
-                    ga = ga * net.adapt_decay[n] + net.adapt[n] * s;
-                    run.g_a[o] = ga;
-                }
-                const size_t out = ((size_t)b * run.T_total + t_abs) * N + n;
+                if (ADAPT) ga = ga * k.a_decay + k.adapt * s;
                 run.spikes[out] = s;
-                if (flags & WT_F_PROB) {
-                    const float p = sigmoid(ksur * (v - theta));
-                    run.prob[out] = (flags & WT_F_REFRACTORY) ? p * (1.0f - held) : p;
+                if (PROB) {
+                    const float p = sigmoid(ksur * (v - k.theta));
+                    run.prob[out] = REF ? p * (1.0f - held) : p;
                 }
-                if ((flags & WT_F_TRACK) && (run.track_b < 0 || run.track_b == b)) {
+                if (TRACK && (run.track_b < 0 || run.track_b == b)) {
                     const int bt = run.track_b < 0 ? b : 0;
                     const size_t to = ((size_t)bt * run.T_total + t_abs) * N + n;
                     run.track_v[to] = v_next;
                     float *tI = run.track_I + to * (S + 1);
 #pragma unroll
-                    for (int c = 0; c < S; c++) tI[c] = Gt[c] * (v - tab.E[c]);
+                    for (int c = 0; c < S; c++) tI[c] = Gt[c] * (v - net.E_syn[c]);
                     tI[S] = I_leak;
-                    if (flags & WT_F_ADAPT) run.track_a[to] = ga;
+                    if (ADAPT) run.track_a[to] = ga;
                 }
-                run.v[o] = v_next;
+                // the state entering step t + 1 (g: before this step's input)
+                if (RES) {
+                    rp[0] = v_next;
+                    if (REF) rp[w_cnt * 32] = __int_as_float(cnt);
+                    if (ADAPT) rp[w_ga * 32] = ga;
 #pragma unroll
-                for (int c = 0; c < S; c++) {
-                    g_b[(size_t)c * N] = gr[c];
-                    g_b[(size_t)(S + c) * N] = gd[c];
+                    for (int c = 0; c < S; c++) {
+                        rp[(w_gd + c) * 32] = gd[c];
+                        if (rw[c] >= 0) rp[rw[c] * 32] = gr[c];
+                    }
+                } else {
+                    run.v[o] = v_next;
+                    if (REF) run.counter[o] = cnt;
+                    if (ADAPT) run.g_a[o] = ga;
+#pragma unroll
+                    for (int c = 0; c < S; c++) {
+                        g_b[(size_t)(S + c) * N] = gd[c];
+                        if (rw[c] >= 0) g_b[(size_t)c * N] = gr[c];
+                    }
                 }
                 if (emit_next) {
                     float h2;
-                    const float u2 = (flags & WT_F_SAMPLE) ? run.noise[((size_t)b * run.T_total + t_abs + 1) * N + n] : 0.0f;
-                    s_next = spike_of(v_next, theta, cnt, u2, flags, ksur, h2);
+                    const float u2 = SAMPLE ? run.noise[out + N] : 0.0f;
+                    s_next = spike_of(v_next, k.theta, cnt, u2, sflags, ksur, h2);
                 }
             }
-            if (flags & WT_F_SAVE) {
+            if (SAVE) {
                 const unsigned sb = __ballot_sync(kFull, s > 0.0f);
                 const unsigned hb = __ballot_sync(kFull, held > 0.0f);
-                if (lane == 0) {
-                    const size_t w = ((size_t)b * run.T_total + t_abs) * words + (n >> 5);
+                if (lane == 0) {  // lane 0 holds the word's first neuron
+                    const size_t w = ((size_t)b * run.T_total + t_abs) * words + q.g;
                     run.spike_bits[w] = sb;
-                    if (flags & WT_F_REFRACTORY) run.held_bits[w] = hb;
+                    if (REF) run.held_bits[w] = hb;
                 }
             }
-            if (emit_next) emit(net, run, ws, t + 1, valid, b, n, s_next, gated, lane);
+            if (emit_next) emit_any(t + 1, valid, b, n, s_next);
+            q.next(B, N, Np, TN);
+            rp += ks * 32;
         }
-        // ---------------- phase A: the input columns of the next step ----------------
+        cp_async_wait(0);  // the last (empty) groups
+        // ---------------- the input columns of the next step ----------------
         if (emit_next) {
             for (long long base = warp0; base < itemsI; base += nthreads) {
                 const long long i = base + lane;
                 const int b = (int)(i / Ip), c = (int)(i % Ip);
                 const bool valid = c < n_in;
                 const float xv = valid ? run.x[((size_t)b * run.T_total + t_abs + 1) * n_in + c] : 0.0f;
-                emit(net, run, ws, t + 1, valid, b, N + c, xv, gated, lane);
-            }
-        }
-        // ---------------- phase B: scatter the events of step t into X_t ----------------
-        {
-            const unsigned count = *reinterpret_cast<volatile unsigned *>(&ws.ev_count[t]);
-            const uint32_t *items = ws.ev_item + (size_t)(t & 1) * ws.ev_cap;
-            const float *amps = ws.ev_amp + (size_t)(t & 1) * ws.ev_cap;
-            unsigned long long *X = ws.X + (size_t)(t & 1) * C * BN;
-            const uint32_t nch = (uint32_t)net.n_chunks;
-            for (long long it = gwarp; it < (long long)count; it += nwarps) {
-                const uint32_t item = __ldcg(items + it);  // written by other blocks: L2, not L1
-                const float amp = __ldcg(amps + it);
-                const uint32_t b = item / nch, chunk = item - b * nch;
-                const long long e0 = net.chunk_begin[chunk];
-                const int len = net.chunk_len[chunk];
-                unsigned long long *Xb = X + (size_t)b * N;
-                if (ws.edges && lane == 0) atomicAdd(ws.edges + (chunk >= (uint32_t)net.n_rec_chunks), (unsigned long long)len);
-                for (int q = lane; q < len; q += 32) {
-                    const uint32_t pc = net.edge_col[e0 + q];
-                    const float prod = net.edge_w[e0 + q] * amp;
-                    if (fabsf(prod) >= 0x1p62f) {
-                        set_error(ws.err, WT_ERR_FIXED_POINT);
-                        continue;
-                    }
-                    const long long fx = __float2ll_rn(prod);
-                    atomicAdd(Xb + (size_t)(pc >> 27) * BN + (pc & 0x7ffffffu), (unsigned long long)fx);
-                }
+                emit_any(t + 1, valid, b, N + c, xv);
             }
         }
         if (!bar.sync(ws.err)) return;
     }
 
-    // The input of the last step completes the conductances the run leaves.
+    // The input of the last step completes the conductances the run leaves; resident
+    // state goes back to HBM.
     if (T > 0) {
         const int t_last = run.t0 + T - 1;
-        for (long long i = gtid; i < itemsN; i += nthreads) {
-            const int b = (int)(i / Np), n = (int)(i % Np);
+        const unsigned long long *Xl = ws.X + (size_t)((T - 1) & 1) * C * BNp;
+        Cursor q = start;
+        const float *rp = wsm + lane;
+        for (int j = 0; j < nitems; j++, q.next(B, N, Np, TN), rp += ks * 32) {
+            const int b = q.b;
+            const int n = q.g * 32 + lane;
             if (n >= N) continue;
-            const size_t o = (size_t)b * N + n;
-            float *g_b = run.g + (size_t)b * 2 * S * N + n;
-            const unsigned long long *Xp = ws.X + (size_t)((T - 1) & 1) * C * BN + o;
+            const size_t o = q.bN + n;
+            const size_t xo = q.bNp + n;
+            float *g_b = run.g + q.bN * 2 * S + n;
             float gr[S], gd[S];
 #pragma unroll
             for (int c = 0; c < S; c++) {
-                gr[c] = g_b[(size_t)c * N] * tab.dr[c];
-                gd[c] = g_b[(size_t)(S + c) * N] * tab.dd[c];
-                const int in = tab.in[c];
-                if (in >= 0) {
-                    const float xin = __ll2float_rn((long long)__ldcg(Xp + (size_t)in * BN)) * tab.fx_inv[in];
-                    gr[c] = gr[c] + tab.jr[c] * xin;
-                    gd[c] = gd[c] + tab.jd[c] * xin;
+                gd[c] = (RES ? rp[(w_gd + c) * 32] : g_b[(size_t)(S + c) * N]) * net.decay_d[c];
+                if (rw[c] >= 0)
+                    gr[c] = (RES ? rp[rw[c] * 32] : g_b[(size_t)c * N]) * net.decay_r[c];
+                else
+                    gr[c] = (T > 1 ? 0.0f : g_b[(size_t)c * N]) * net.decay_r[c];
+                if (in_c[c] >= 0) {
+                    const float xi = __ll2float_rn((long long)__ldcg(Xl + (size_t)in_c[c] * BNp + xo)) * fx_c[c];
+                    gr[c] = gr[c] + net.jump_r[c] * xi;
+                    gd[c] = gd[c] + net.jump_d[c] * xi;
                 }
                 g_b[(size_t)c * N] = gr[c];
                 g_b[(size_t)(S + c) * N] = gd[c];
             }
-            if (flags & WT_F_SAVE_INPUT)
+            if (SAVE_IN)
                 for (int c = 0; c < C; c++)
                     run.X_saved[(((size_t)b * run.T_total + t_last) * C + c) * N + n] =
-                        __ll2float_rn((long long)__ldcg(Xp + (size_t)c * BN)) * tab.fx_inv[c];
-            if ((flags & WT_F_TRACK) && (run.track_b < 0 || run.track_b == b)) {
+                        __ll2float_rn((long long)__ldcg(Xl + (size_t)c * BNp + xo)) * net.fx_inv[c];
+            if (TRACK && (run.track_b < 0 || run.track_b == b)) {
                 const int bt = run.track_b < 0 ? b : 0;
                 float *tg = run.track_g + (((size_t)bt * run.T_total + t_last) * N + n) * 2 * S;
 #pragma unroll
@@ -419,46 +726,155 @@ __global__ void __launch_bounds__(kBlock) forward_kernel(const WtNet net, const 
                     tg[S + c] = gd[c];
                 }
             }
+            if (RES) {
+                run.v[o] = rp[0];
+                if (REF) run.counter[o] = __float_as_int(rp[w_cnt * 32]);
+                if (ADAPT) run.g_a[o] = rp[w_ga * 32];
+            }
         }
     }
 }
 
 }  // namespace
 
-template <int S>
-static cudaError_t launch_s(const WtNet &net, const WtForward &run, const WtWorkspace &ws, cudaStream_t st,
-                            int grid_cap) {
-    static int max_blocks[16] = {0};  // per device
+// The launch geometry: one block of kWarps warps per SM (fewer blocks when there are
+// fewer items than warps); state resident in shared memory when every warp's share fits
+// beside a ring of at least two slots, else streamed with the deepest ring that fits.
+// Cached per device, kernel and shape.
+struct GeoKey {
+    const void *kernel;
+    int dev, B, N, C, n_rise, feat;
+    bool operator==(const GeoKey &o) const {
+        return kernel == o.kernel && dev == o.dev && B == o.B && N == o.N && C == o.C && n_rise == o.n_rise &&
+               feat == o.feat;
+    }
+};
+
+template <int S, int FEAT>
+static cudaError_t geometry_for(const WtNet &net, int flags, Geometry &geo, int &grid, size_t &dyn) {
+    static GeoKey keys[64];
+    static Geometry geos[64];
+    static int grids[64];
+    static size_t dyns[64];
+    static int n_cached = 0;
+    const void *kern = (const void *)forward_kernel<S, FEAT>;
     int dev = 0;
     cudaGetDevice(&dev);
-    if (dev < 16 && max_blocks[dev] == 0) {
-        int per_sm = 0, sms = 0;
-        cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, forward_kernel<S>, kBlock, 0);
-        if (e != cudaSuccess) return e;
-        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-        max_blocks[dev] = per_sm * sms;
+    int n_rise = 0;
+    for (int c = 0; c < S; c++) n_rise += net.decay_r[c] != 0.0f;
+    const bool REF = flags & WT_F_REFRACTORY, ADAPT = flags & WT_F_ADAPT;
+    const GeoKey key{kern, dev, net.B, net.N, net.C, n_rise, REF * 2 + ADAPT};
+    for (int i = 0; i < n_cached; i++)
+        if (keys[i] == key) {
+            geo = geos[i];
+            grid = grids[i];
+            dyn = dyns[i];
+            return cudaSuccess;
+        }
+    int sms = 0, optin = 0;
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+    cudaFuncAttributes attr;
+    cudaError_t e = cudaFuncGetAttributes(&attr, forward_kernel<S, FEAT>);
+    if (e != cudaSuccess) return e;
+    const long long max_dyn = optin - (long long)attr.sharedSizeBytes;
+    e = cudaFuncSetAttribute(forward_kernel<S, FEAT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)max_dyn);
+    if (e != cudaSuccess) return e;
+    Geometry g{};
+    g.groups = (net.N + 31) / 32;
+    g.Np = g.groups * 32;
+    g.W = (long long)g.groups * net.B;
+    g.w_cnt = 1;
+    g.w_ga = 1 + REF;
+    g.w_gd = 1 + REF + ADAPT;
+    g.w_gr = g.w_gd + S;
+    g.ks = g.w_gr + n_rise;
+    const long long blocks = std::min<long long>(sms, (g.W + kWarps - 1) / kWarps);
+    const long long nw = blocks * kWarps;
+    g.max_items = (int)((g.W + nw - 1) / nw);
+    const long long x_rows = 2LL * net.C;  // a slot's int64 inputs, in 128-byte rows
+    g.D = 0;
+    for (int D = kMaxRing; D >= 2 && !g.D; D--) {  // resident, with at least two slots
+        const long long rows = (long long)g.max_items * g.ks + D * x_rows;
+        if (rows * 128 * kWarps <= max_dyn) {
+            g.resident = 1;
+            g.D = D;
+            g.slot_rows = (int)x_rows;
+            g.warp_rows = (int)rows;
+        }
     }
-    int grid = dev < 16 ? max_blocks[dev] : 148;
-    if (grid_cap > 0 && grid_cap < grid) grid = grid_cap;
-    if (grid < 1) grid = 1;
+    for (int D = kMaxRing; D >= 1 && !g.D; D--) {  // streamed
+        const long long rows = D * (x_rows + g.ks);
+        if (rows * 128 * kWarps <= max_dyn) {
+            g.resident = 0;
+            g.D = D;
+            g.slot_rows = (int)(x_rows + g.ks);
+            g.warp_rows = (int)rows;
+        }
+    }
+    if (!g.D) return cudaErrorInvalidConfiguration;
+    const size_t d = (size_t)g.warp_rows * 128 * kWarps;
+    int per_sm = 0;
+    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, forward_kernel<S, FEAT>, kThreads, d);
+    if (e != cudaSuccess) return e;
+    if (per_sm < 1) return cudaErrorInvalidConfiguration;
+    geo = g;
+    grid = (int)blocks;
+    dyn = d;
+    if (n_cached < 64) {
+        keys[n_cached] = key;
+        geos[n_cached] = geo;
+        grids[n_cached] = grid;
+        dyns[n_cached] = dyn;
+        n_cached++;
+    }
+    return cudaSuccess;
+}
+
+template <int S, int FEAT>
+static cudaError_t launch_sf(const WtNet &net, const WtForward &run, const WtWorkspace &ws, cudaStream_t st) {
+    Geometry geo;
+    int grid = 1;
+    size_t dyn = 0;
+    cudaError_t e = geometry_for<S, FEAT>(net, run.flags, geo, grid, dyn);
+    if (e != cudaSuccess) return e;
     WtNet n = net;
     WtForward r = run;
     WtWorkspace w = ws;
-    void *args[] = {&n, &r, &w};
-    return cudaLaunchCooperativeKernel((const void *)forward_kernel<S>, dim3(grid), dim3(kBlock), args, 0, st);
+    void *args[] = {&n, &r, &w, &geo};
+    return cudaLaunchCooperativeKernel((const void *)forward_kernel<S, FEAT>, dim3(grid), dim3(kThreads), args, dyn,
+                                       st);
 }
 
+// The specialised kernels cover the common runs (up to four channels; refractory period
+// and saving as given; no other feature); everything else runs the generic kernel.
+template <int S>
+static cudaError_t launch_s(const WtNet &net, const WtForward &run, const WtWorkspace &ws, cudaStream_t st) {
+    const int generic = WT_F_ADAPT | WT_F_MG_BLOCK | WT_F_SAMPLE | WT_F_GATED | WT_F_PROB | WT_F_TRACK | WT_F_SAVE_INPUT;
+    if (S > 4 || (run.flags & generic)) return launch_sf<S, kGeneric>(net, run, ws, st);
+    const int feat = ((run.flags & WT_F_REFRACTORY) ? kRef : 0) | ((run.flags & WT_F_SAVE) ? kSave : 0);
+    switch (feat) {
+        case 0: return launch_sf<S, 0>(net, run, ws, st);
+        case kRef: return launch_sf<S, kRef>(net, run, ws, st);
+        case kSave: return launch_sf<S, kSave>(net, run, ws, st);
+        default: return launch_sf<S, kRef | kSave>(net, run, ws, st);
+    }
+}
+
+// The 128-byte-aligned accumulator row stride the kernel uses for X.
+long long forward_x_row(int N) { return (long long)((N + 31) / 32) * 32; }
+
 cudaError_t launch_forward_s(const WtNet &net, const WtForward &run, const WtWorkspace &ws, cudaStream_t st,
-                             int grid_cap) {
+                             int /*unused*/) {
     switch (net.S) {
-        case 1: return launch_s<1>(net, run, ws, st, grid_cap);
-        case 2: return launch_s<2>(net, run, ws, st, grid_cap);
-        case 3: return launch_s<3>(net, run, ws, st, grid_cap);
-        case 4: return launch_s<4>(net, run, ws, st, grid_cap);
-        case 5: return launch_s<5>(net, run, ws, st, grid_cap);
-        case 6: return launch_s<6>(net, run, ws, st, grid_cap);
-        case 7: return launch_s<7>(net, run, ws, st, grid_cap);
-        case 8: return launch_s<8>(net, run, ws, st, grid_cap);
+        case 1: return launch_s<1>(net, run, ws, st);
+        case 2: return launch_s<2>(net, run, ws, st);
+        case 3: return launch_s<3>(net, run, ws, st);
+        case 4: return launch_s<4>(net, run, ws, st);
+        case 5: return launch_s<5>(net, run, ws, st);
+        case 6: return launch_s<6>(net, run, ws, st);
+        case 7: return launch_s<7>(net, run, ws, st);
+        case 8: return launch_s<8>(net, run, ws, st);
         default: return cudaErrorInvalidValue;
     }
 }

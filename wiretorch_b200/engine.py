@@ -100,16 +100,16 @@ def _external_g(plan, g):
 def _workspace(plan, T, device):
     B, N, C = plan.B, plan.N, plan.ch.C
     cap = B * max(plan.n_chunks, 1)
+    Np = -(-N // 32) * 32  # accumulator rows are padded to whole 32-neuron groups
     ws = {
-        "X": torch.empty(2 * C * B * N, dtype=torch.int64, device=device),
-        "ev_item": torch.empty(2 * cap, dtype=torch.int32, device=device),
-        "ev_amp": torch.empty(2 * cap, dtype=torch.float32, device=device),
+        "X": torch.empty(2 * C * B * Np, dtype=torch.int64, device=device),
+        "ev": torch.empty(2 * cap * _lib.EVENT_BYTES, dtype=torch.uint8, device=device),
         "ev_count": torch.empty(T + 1, dtype=torch.int32, device=device),
         "barrier": torch.zeros(64, dtype=torch.int32, device=device),
         "err": torch.zeros(1, dtype=torch.int32, device=device),
     }
     w = _lib.WtWorkspace()
-    for name in ("X", "ev_item", "ev_amp", "ev_count", "barrier", "err"):
+    for name in ("X", "ev", "ev_count", "barrier", "err"):
         setattr(w, name, ws[name].data_ptr())
     w.ev_cap = cap
     if EDGE_COUNTER is not None:

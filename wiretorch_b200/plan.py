@@ -181,7 +181,7 @@ class Plan:
     fx_exp: list = field(default_factory=list)
     n_slots: int = 0
     n_chunks: int = 0
-    n_rec_chunks: int = 0
+    n_rec_edges: int = 0
     n_edges: int = 0
     R: int = 0
     R_f: int = 0
@@ -194,7 +194,8 @@ class Plan:
         n.B, n.N, n.n_in, n.S, n.C = self.B, self.N, self.n_in, self.ch.Sp, self.ch.C
         t = self.tensors
         n.src_slot, n.slot_chunk = t["src_slot"].data_ptr(), t["slot_chunk"].data_ptr()
-        n.chunk_begin, n.chunk_len = t["chunk_begin"].data_ptr(), t["chunk_len"].data_ptr()
+        n.src_chunk = t["src_chunk"].data_ptr()
+        n.chunk_desc = t["chunk_desc"].data_ptr()
         n.edge_col = t["edge_col"].data_ptr()
         n.n_slots, n.n_chunks = self.n_slots, self.n_chunks
         one = t.setdefault("_one", torch.ones(1, device=self.device))
@@ -239,10 +240,11 @@ class Plan:
         n.surr_scale = float(p.surr_scale)
         t = self.tensors
         n.src_slot, n.slot_chunk = t["src_slot"].data_ptr(), t["slot_chunk"].data_ptr()
-        n.chunk_begin, n.chunk_len = t["chunk_begin"].data_ptr(), t["chunk_len"].data_ptr()
-        n.edge_col, n.edge_w = t["edge_col"].data_ptr(), t["edge_w"].data_ptr()
+        n.src_chunk = t["src_chunk"].data_ptr()
+        n.chunk_desc = t["chunk_desc"].data_ptr()
+        n.edge_col, n.edge_cw = t["edge_col"].data_ptr(), t["edge_cw"].data_ptr()
         n.n_slots, n.n_chunks = self.n_slots, self.n_chunks
-        n.n_rec_chunks = self.n_rec_chunks
+        n.n_rec_edges = self.n_rec_edges
         if self.gated:
             n.slot_gate, n.slot_row = t["slot_gate"].data_ptr(), t["slot_row"].data_ptr()
             n.gate_params, n.gate_cols = t["gate_params"].data_ptr(), t["gate_cols"].data_ptr()
@@ -282,6 +284,8 @@ def build(drive, p, B: int, n_in: int, device, pool: bool = False) -> Plan:
             base += int(cols.numel())
         seg_of.append(segs)
     plan.n_edges = base
+    # the recurrent pathways' segments come first in the edge arrays
+    plan.n_rec_edges = sum(int(csrs[k][-1]) * len(seg_of[k]) for k in range(len(drive.recurrent)))
     plan.seg_meta = [(k, c, b0, int(csrs[k][-1])) for k, segs in enumerate(seg_of) for c, b0 in segs]
     plan.csr_row_ptr = csrs
     edge_col = (torch.cat(seg_cols).to(torch.int32) if seg_cols
@@ -343,8 +347,6 @@ def build(drive, p, B: int, n_in: int, device, pool: bool = False) -> Plan:
     slot_chunk = torch.zeros(plan.n_slots + 1, dtype=torch.int64, device=device)
     slot_chunk[1:] = torch.cumsum(per_slot, 0)
     plan.n_chunks = total
-    # the neurons' slots come first (sources are ordered neurons, then inputs)
-    plan.n_rec_chunks = int(slot_chunk[int(src_slot[N])])
     if total >= 2**31 or plan.n_edges >= 2**62:
         raise NotImplementedError("more than 2^31 chunks")
 
@@ -378,8 +380,11 @@ def build(drive, p, B: int, n_in: int, device, pool: bool = False) -> Plan:
 
     t["src_slot"] = src_slot.to(torch.int32).contiguous()
     t["slot_chunk"] = slot_chunk.to(torch.int32).contiguous()
+    # a source's chunks are contiguous (its slots are, and so are their chunks)
+    t["src_chunk"] = slot_chunk[src_slot].to(torch.int32).contiguous()
+    t["chunk_desc"] = (chunk_begin | (chunk_len.to(torch.int64) << 56)).contiguous()
+    t["chunk_len"] = chunk_len.to(torch.int32).contiguous()  # for the host-side walks
     t["chunk_begin"] = chunk_begin.contiguous()
-    t["chunk_len"] = chunk_len.to(torch.int32).contiguous()
     t["chunk_path"] = chunk_path.to(torch.int32).contiguous()
     t["edge_col"] = edge_col.contiguous()
     t["w_raw"] = w_raw.contiguous()
@@ -421,35 +426,41 @@ def edge_pathway(plan: Plan) -> torch.Tensor:
 
 
 def fold(plan: Plan, scale: torch.Tensor, p=None) -> None:
-    """``edge_w = w * scale[k, col] * jf[k, c] * 2^s_c`` for this call's ``scale``: the
-    ``wt_fold_weights`` kernel on CUDA (numpy-free torch on the CPU, for the tests of the
-    tables)."""
+    """The folded edges of this call's ``scale``: ``edge_cw`` packs each edge's target
+    word with the bits of ``w * scale[k, col] * jf[k, c] * 2^s_c`` — the
+    ``wt_fold_weights`` kernel on CUDA (torch on the CPU, for the tests of the tables)."""
     t = plan.tensors
     scale = scale.detach().to(plan.device, torch.float32).contiguous()
     if plan.fx_scale is None:
         _choose_fixed_point(plan, scale)
     if plan.n_edges == 0:
-        t["edge_w"] = torch.zeros(1, device=plan.device)
+        t["edge_cw"] = torch.zeros(1, dtype=torch.int64, device=plan.device)
         return
     if plan.device.type != "cuda":
         k = edge_pathway(plan)
         packed = t["edge_col"].to(torch.int64) & 0xFFFFFFFF
         col, c = packed & 0x7FFFFFF, packed >> 27
-        t["edge_w"] = (t["w_raw"] * scale[k, col] * t["jf"][k, c] * plan.fx_scale[c]).contiguous()
+        w = (t["w_raw"] * scale[k, col] * t["jf"][k, c] * plan.fx_scale[c]).contiguous()
+        t["edge_cw"] = packed | (w.view(torch.int32).to(torch.int64) << 32)
         return
-    if "edge_w" not in t:
-        t["edge_w"] = torch.empty_like(t["w_raw"])
+    if "edge_cw" not in t:
+        t["edge_cw"] = torch.empty(plan.n_edges, dtype=torch.int64, device=plan.device)
     net = plan.net(p) if p is not None else plan.net_for_fold()
     with _lib.timed("wt_fold_weights"):
         rc = _lib.lib().wt_fold_weights(
             _lib.C.byref(net), _lib.C.c_void_p(t["w_raw"].data_ptr()),
             _lib.C.c_void_p(t["chunk_path"].data_ptr()), _lib.C.c_void_p(scale.data_ptr()),
             _lib.C.c_void_p(t["jf"].data_ptr()), _lib.C.c_void_p(plan.fx_scale.data_ptr()),
-            _lib.C.c_void_p(t["edge_w"].data_ptr()), _lib.C.c_void_p(_lib.stream_of(plan.device)),
+            _lib.C.c_void_p(t["edge_cw"].data_ptr()), _lib.C.c_void_p(_lib.stream_of(plan.device)),
         )
     _lib.check(rc, "wt_fold_weights")
     _lib.count_launches(1)
     plan.tensors["_scale"] = scale  # alive until the kernel has read it
+
+
+def edge_weights(plan: Plan) -> torch.Tensor:
+    """The folded weights of ``edge_cw`` (float32), for inspection and tests."""
+    return (plan.tensors["edge_cw"] >> 32).to(torch.int32).view(torch.float32)
 
 
 def _choose_fixed_point(plan: Plan, scale: torch.Tensor) -> None:
