@@ -156,6 +156,19 @@ int wt_fold_weights(const WtNet *net, const float *w_raw, const int32_t *chunk_p
  * conductance/engine.py:285-303 `_scan`). */
 int wt_forward(const WtNet *net, const WtForward *run, const WtWorkspace *ws, void *stream);
 
+/* wt_forward with no caller-allocated workspace: the scratch is a static device array of
+ * 32 MiB per device; runs whose workspace (wt_workspace_bytes) does not fit are rejected
+ * with WT_ERR_ARGS. No counterpart in the reference (its engine allocates its buffers
+ * with PyTorch on every call). For callers that cannot allocate device memory on this
+ * path. The first call on a device looks up the array (do it before any stream capture);
+ * calls overlapping in time share the array and race, so a caller serialises them. The
+ * run's device error code is read with wt_noalloc_error. Allocates nothing. */
+int wt_forward_noalloc(const WtNet *net, const WtForward *run, void *stream);
+
+/* The device error code (0: none) of the last wt_forward_noalloc on the current device,
+ * after waiting for `stream`. No counterpart in the reference. */
+int wt_noalloc_error(void *stream, int32_t *code);
+
 /* Gradients wanted by a backward pass (WtBackward.wants): the physiology, in the order
  * of the reference's PHYSIOLOGY (conductance/engine.py:190-193). */
 enum {

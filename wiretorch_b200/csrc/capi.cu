@@ -47,6 +47,12 @@ int check_net(const WtNet *n) {
 }
 }  // namespace
 
+namespace wt {
+// Records `message` as the last error (wt_last_error) and returns `code`; for the entry
+// points defined in other files.
+int set_last_error(int code, const char *message) { return fail(code, "%s", message); }
+}  // namespace wt
+
 extern "C" {
 
 const char *wt_last_error(void) { return g_error; }
