@@ -15,7 +15,8 @@ trials (trial-batch sharding, weak scaling). Inputs are larger than L2.
 
 ``value``: neuron-steps per second of the whole job (trials x neurons x time steps of all
 ranks / the slowest rank's device time). ``synaptic_events_per_s``: edges traversed by
-recurrent spikes (counted on the device) per second, input events separately.
+recurrent spikes per second (counted on the device over one extra, untimed step and
+multiplied by the steps timed), input events separately.
 ``roofline``: the dominant kernel's algorithmic bytes per launch / its CUDA-event
 duration against the measured HBM copy bandwidth. ``e2e``: the same step fed from pinned
 host memory (spike input as bytes, target rates), with the loss and gradient read back.
@@ -366,9 +367,15 @@ def main():
     torch.cuda.synchronize()
     plan = engine.get_plan(cfg.drive, cfg.p, cfg.B, cfg.n_in, device)
 
-    # ---- timed region: K steps, device time, max over ranks ----
+    # ---- synaptic events: counted on the device over one untimed step (the counter's
+    # atomics stay out of the timed region) ----
     edges = torch.zeros(2, dtype=torch.int64, device=device)
     engine.EDGE_COUNTER = edges
+    step(x, target)
+    torch.cuda.synchronize()
+    engine.EDGE_COUNTER = None
+
+    # ---- timed region: K steps, device time, max over ranks ----
     _lib.TIMER = {}
     launches0 = _lib.LAUNCHES
     barrier(world)
@@ -383,12 +390,11 @@ def main():
     barrier(world)
     launches = _lib.LAUNCHES - launches0
     timer, _lib.TIMER = _lib.TIMER, None
-    engine.EDGE_COUNTER = None
     elapsed = start.elapsed_time(end) / 1000.0
     elapsed_max = max_over_ranks(elapsed, world)
     K = args.steps
     neuron_steps = cfg.B * cfg.N * cfg.T * K * world
-    rec_edges, in_edges = float(edges[0]), float(edges[1])
+    rec_edges, in_edges = float(edges[0]) * K, float(edges[1]) * K  # one step counted
     rec_edges_all = sum_over_ranks(rec_edges, world)
     in_edges_all = sum_over_ranks(in_edges, world)
     clock = clocks.summary()

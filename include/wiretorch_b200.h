@@ -254,6 +254,44 @@ int wt_filter_forward(const WtFilterArgs *f, void *stream);
 /* Replaces `_filter_backward` (training_utils/filtering.py:123-135). */
 int wt_filter_backward(const WtFilterGradArgs *f, void *stream);
 
+/* The van Rossum rate loss of one chunk in one pass: the double-exponential filter of the
+ * output x and of the target rate y (each from its carried state), the difference of the
+ * smoothed trains err = smooth(x) - smooth(y), saved for the backward pass, and per block
+ * of 256 (trial, neuron) columns the sum of err^2 (partial[ceil(B N / 256)]). x and y have
+ * unit neuron stride; y's strides may be 0 (a rate constant in time or across trials). */
+typedef struct {
+    int32_t B, T, N;
+    const float *x;
+    int64_t x_bstride, x_tstride;
+    const float *y;
+    int64_t y_bstride, y_tstride;
+    const float *carry; /* (4, B, N) or NULL: output rise, output smooth, target rise, smooth */
+    float a_rise, a_decay;
+    float *err;         /* (B, T, N) */
+    float *last;        /* (4, B, N): the states after the last step, as carry */
+    double *partial;    /* (ceil(B N / 256)) */
+} WtVanRossumArgs;
+
+/* dL/dx of the loss mean(err^2): the filter's adjoint applied to scale * grad_loss * err,
+ * scale = 2 / (B T N), grad_loss a device scalar (no host read). */
+typedef struct {
+    int32_t B, T, N;
+    const float *err;
+    const float *grad_loss;
+    float scale;
+    float a_rise, a_decay;
+    float *grad_x;
+} WtVanRossumGradArgs;
+
+/* Replaces `VanRossumRateLoss.forward` (training_utils/losses.py:140-194): its two
+ * `double_exponential` calls (training_utils/filtering.py:28-48) and the mean of the
+ * squared difference, which the reference computes as separate passes. */
+int wt_van_rossum_forward(const WtVanRossumArgs *a, void *stream);
+
+/* The backward pass of that loss down to the output train (filtering.py:123-135 applied
+ * to the loss's gradient). */
+int wt_van_rossum_backward(const WtVanRossumGradArgs *a, void *stream);
+
 /* Reading back: a static description of the last host-side error on this thread. */
 const char *wt_last_error(void);
 

@@ -37,8 +37,15 @@ def test_abi_version(lib):
 def test_structures_match_the_header_sizes():
     """The ctypes mirrors have the members the header declares, in order."""
     text = HEADER.read_text()
+    from wiretorch_b200 import autograd, filtering
+
     for struct, cls in (("WtNet", _lib.WtNet), ("WtForward", _lib.WtForward),
-                        ("WtWorkspace", _lib.WtWorkspace)):  # fmt: skip
+                        ("WtWorkspace", _lib.WtWorkspace),
+                        ("WtBackward", autograd._BackwardArgs), ("WtEdgeGrads", autograd._EdgeArgs),
+                        ("WtFilterArgs", filtering._FilterArgs),
+                        ("WtFilterGradArgs", filtering._FilterGradArgs),
+                        ("WtVanRossumArgs", filtering._VanRossumArgs),
+                        ("WtVanRossumGradArgs", filtering._VanRossumGradArgs)):  # fmt: skip
         body = re.search(r"typedef struct \{((?:(?!typedef struct).)*?)\}\s*" + struct + ";", text,
                          re.S).group(1)
         body = re.sub(r"/\*.*?\*/", "", body, flags=re.S)

@@ -13,6 +13,8 @@ cudaError_t launch_backward(const WtNet &net, const WtBackward &bw, cudaStream_t
 cudaError_t launch_edge_grads(const WtNet &net, const WtEdgeGrads &eg, cudaStream_t st);
 cudaError_t launch_filter(const WtFilterArgs &f, cudaStream_t st);
 cudaError_t launch_filter_grad(const WtFilterGradArgs &f, cudaStream_t st);
+cudaError_t launch_van_rossum(const WtVanRossumArgs &a, cudaStream_t st);
+cudaError_t launch_van_rossum_grad(const WtVanRossumGradArgs &a, cudaStream_t st);
 cudaError_t launch_fold(const WtNet &net, const float *w_raw, const int32_t *chunk_path, const float *scale,
                         const float *jf, const float *fx_scale, uint64_t *out, cudaStream_t st);
 }
@@ -165,6 +167,20 @@ int wt_filter_backward(const WtFilterGradArgs *f, void *stream) {
     if (!f || f->B < 0 || f->T < 0 || f->N < 0 || (f->B && f->T && f->N && (!f->grad_smooth || !f->grad_x)))
         return fail(WT_ERR_ARGS, "bad filter-gradient arguments%s");
     return launch_status(wt::launch_filter_grad(*f, (cudaStream_t)stream), "filter gradient");
+}
+
+int wt_van_rossum_forward(const WtVanRossumArgs *a, void *stream) {
+    if (!a || a->B < 0 || a->T < 0 || a->N < 0) return fail(WT_ERR_ARGS, "bad loss arguments%s");
+    if (a->B && a->N && (!a->last || !a->partial || (a->T && (!a->x || !a->y || !a->err))))
+        return fail(WT_ERR_ARGS, "missing loss buffers%s");
+    return launch_status(wt::launch_van_rossum(*a, (cudaStream_t)stream), "van Rossum loss");
+}
+
+int wt_van_rossum_backward(const WtVanRossumGradArgs *a, void *stream) {
+    if (!a || a->B < 0 || a->T < 0 || a->N < 0) return fail(WT_ERR_ARGS, "bad loss-gradient arguments%s");
+    if (a->B && a->N && a->T && (!a->err || !a->grad_loss || !a->grad_x))
+        return fail(WT_ERR_ARGS, "missing loss-gradient buffers%s");
+    return launch_status(wt::launch_van_rossum_grad(*a, (cudaStream_t)stream), "van Rossum loss gradient");
 }
 
 }  // extern "C"

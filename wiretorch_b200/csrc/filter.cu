@@ -170,11 +170,90 @@ __global__ void filter_grad_chunked(const WtFilterGradArgs f) {
     }
 }
 
+// The van Rossum rate loss (training_utils/losses.py:140-194) in one pass per column:
+// both filters, the difference saved, its square summed in double (per thread, then
+// over the block: one partial per block, summed by the caller in a fixed order).
+__global__ void __launch_bounds__(256) van_rossum_fwd(const WtVanRossumArgs a) {
+    __shared__ double part[8];
+    const long long cols = (long long)a.B * a.N;
+    const long long i = (long long)blockIdx.x * 256 + threadIdx.x;
+    double sq = 0.0;
+    if (i < cols) {
+        const int b = (int)(i / a.N), n = (int)(i % a.N);
+        float ro = 0.0f, so = 0.0f, rt = 0.0f, st = 0.0f;
+        if (a.carry) {
+            ro = a.carry[i];
+            so = a.carry[cols + i];
+            rt = a.carry[2 * cols + i];
+            st = a.carry[3 * cols + i];
+        }
+        const float *x = a.x + b * a.x_bstride + n;
+        const float *y = a.y + b * a.y_bstride + n;
+        float *e = a.err + (size_t)b * a.T * a.N + n;
+#pragma unroll 4
+        for (int t = 0; t < a.T; t++) {
+            const float xt = x[t * a.x_tstride], yt = y[t * a.y_tstride];
+            // the carried state enters undecayed at t = 0 (filtering.py:112-117)
+            ro = (t == 0 ? ro : a.a_rise * ro) + xt;
+            so = (t == 0 ? so : a.a_decay * so) + ro;
+            rt = (t == 0 ? rt : a.a_rise * rt) + yt;
+            st = (t == 0 ? st : a.a_decay * st) + rt;
+            const float d = so - st;
+            e[(size_t)t * a.N] = d;
+            sq += (double)d * (double)d;
+        }
+        if (a.T > 0) {
+            a.last[i] = ro;
+            a.last[cols + i] = so;
+            a.last[2 * cols + i] = rt;
+            a.last[3 * cols + i] = st;
+        }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) sq += __shfl_down_sync(kFull, sq, o);
+    if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = sq;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        double tot = 0.0;
+        for (int w = 0; w < 8; w++) tot += part[w];
+        a.partial[blockIdx.x] = tot;
+    }
+}
+
+__global__ void van_rossum_bwd(const WtVanRossumGradArgs a) {
+    const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= (long long)a.B * a.N) return;
+    const int b = (int)(i / a.N), n = (int)(i % a.N);
+    const float c = a.scale * *a.grad_loss;
+    const size_t base = (size_t)b * a.T * a.N + n;
+    float gs = 0.0f, gx = 0.0f;
+    for (int t = a.T - 1; t >= 0; t--) {
+        const size_t o = base + (size_t)t * a.N;
+        gs = a.err[o] * c + a.a_decay * gs;
+        gx = gs + a.a_rise * gx;
+        a.grad_x[o] = gx;
+    }
+}
+
 // Columns below which the parallel-over-T kernels run (148 SMs x 2048 threads would
 // want ~300k sequential columns to fill the GPU).
 constexpr long long kParallelBelow = 1 << 16;
 
 }  // namespace
+
+cudaError_t launch_van_rossum(const WtVanRossumArgs &a, cudaStream_t st) {
+    const long long cols = (long long)a.B * a.N;
+    if (cols == 0) return cudaSuccess;
+    van_rossum_fwd<<<(unsigned)((cols + 255) / 256), 256, 0, st>>>(a);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_van_rossum_grad(const WtVanRossumGradArgs &a, cudaStream_t st) {
+    const long long cols = (long long)a.B * a.N;
+    if (cols == 0 || a.T == 0) return cudaSuccess;
+    van_rossum_bwd<<<(unsigned)((cols + 255) / 256), 256, 0, st>>>(a);
+    return cudaGetLastError();
+}
 
 cudaError_t launch_filter(const WtFilterArgs &f, cudaStream_t st) {
     const long long cols = (long long)f.B * f.N;

@@ -10,7 +10,8 @@ on the CPU and a Triton recursion on CUDA; here it is the ``wt_filter_forward`` 
 
 ``VanRossumRateLoss`` is ``training_utils/losses.py:140-194``: the mean squared
 difference of the filtered output and the filtered target rate (expected spikes per
-step), carrying the filter state from chunk to chunk.
+step), carrying the filter state from chunk to chunk; both filters and the mean square
+run fused in one kernel (``wt_van_rossum_forward``), the gradient in one more.
 """
 
 from __future__ import annotations
@@ -116,11 +117,82 @@ def double_exponential(x, kernel_rise, kernel_decay, carried_rise, carried_smoot
     )  # fmt: skip
 
 
+class _VanRossumArgs(_lib.C.Structure):
+    _fields_ = [
+        ("B", _lib.C.c_int32), ("T", _lib.C.c_int32), ("N", _lib.C.c_int32),
+        ("x", _lib.P), ("x_bstride", _lib.C.c_int64), ("x_tstride", _lib.C.c_int64),
+        ("y", _lib.P), ("y_bstride", _lib.C.c_int64), ("y_tstride", _lib.C.c_int64),
+        ("carry", _lib.P), ("a_rise", _lib.C.c_float), ("a_decay", _lib.C.c_float),
+        ("err", _lib.P), ("last", _lib.P), ("partial", _lib.P),
+    ]  # fmt: skip
+
+
+class _VanRossumGradArgs(_lib.C.Structure):
+    _fields_ = [
+        ("B", _lib.C.c_int32), ("T", _lib.C.c_int32), ("N", _lib.C.c_int32),
+        ("err", _lib.P), ("grad_loss", _lib.P), ("scale", _lib.C.c_float),
+        ("a_rise", _lib.C.c_float), ("a_decay", _lib.C.c_float), ("grad_x", _lib.P),
+    ]  # fmt: skip
+
+
+def _unit_neuron_stride(t):
+    t = t if t.dtype == torch.float32 else t.float()
+    return t if t.stride(2) == 1 else t.contiguous()
+
+
+class _VanRossumRate(torch.autograd.Function):
+    """mean((smooth(x) - smooth(y))^2) in one kernel; the backward in one more. The
+    states after the chunk are left in ``state["last"]`` ``(4, B, N)``."""
+
+    @staticmethod
+    def forward(ctx, x, y, carry, a_rise, a_decay, state):
+        if not x.is_cuda:
+            raise RuntimeError("wiretorch_b200 runs on CUDA tensors only (no CPU path)")
+        B, T, N = x.shape
+        x, y = _unit_neuron_stride(x.detach()), _unit_neuron_stride(y.detach())
+        dev = x.device
+        err = torch.empty((B, T, N), device=dev)
+        last = torch.empty((4, B, N), device=dev)
+        partial = torch.empty((max(-(-B * N // 256), 1),), dtype=torch.float64, device=dev)
+        a = _VanRossumArgs()
+        a.B, a.T, a.N = B, T, N
+        a.x, a.x_bstride, a.x_tstride = x.data_ptr(), x.stride(0), x.stride(1)
+        a.y, a.y_bstride, a.y_tstride = y.data_ptr(), y.stride(0), y.stride(1)
+        a.carry = _lib.ptr(carry)
+        a.a_rise, a.a_decay = a_rise, a_decay
+        a.err, a.last, a.partial = err.data_ptr(), last.data_ptr(), partial.data_ptr()
+        with _lib.timed("wt_van_rossum_forward"):
+            rc = _lib.lib().wt_van_rossum_forward(_lib.C.byref(a), _lib.C.c_void_p(_lib.stream_of(dev)))
+        _lib.check(rc, "wt_van_rossum_forward")
+        _lib.count_launches(1)
+        state["last"] = last
+        ctx.save_for_backward(err)
+        ctx.decays = (a_rise, a_decay)
+        return (partial.sum() / max(B * T * N, 1)).float()
+
+    @staticmethod
+    def backward(ctx, grad):
+        (err,) = ctx.saved_tensors
+        B, T, N = err.shape
+        grad = grad.detach().float().reshape(1).contiguous()
+        grad_x = torch.empty_like(err)
+        a = _VanRossumGradArgs()
+        a.B, a.T, a.N = B, T, N
+        a.err, a.grad_loss, a.scale = err.data_ptr(), grad.data_ptr(), 2.0 / max(B * T * N, 1)
+        a.a_rise, a.a_decay, a.grad_x = *ctx.decays, grad_x.data_ptr()
+        with _lib.timed("wt_van_rossum_backward"):
+            rc = _lib.lib().wt_van_rossum_backward(_lib.C.byref(a), _lib.C.c_void_p(_lib.stream_of(err.device)))
+        _lib.check(rc, "wt_van_rossum_backward")
+        _lib.count_launches(1)
+        return grad_x, None, None, None, None, None
+
+
 class VanRossumRateLoss(nn.Module):
     """Mean squared difference of the double-filtered output spikes and the filtered
     target rate (``training_utils/losses.py:31-194``), carrying the filter state across
     chunks. ``target_rate`` is expected spikes per step, ``(B, T, N)`` (any strides: a
-    rate constant in time can be an expanded view)."""
+    rate constant in time can be an expanded view). Both filters, the difference and its
+    mean square run as one kernel (``wt_van_rossum_forward``), its gradient as another."""
 
     def __init__(self, tau_rise, tau_decay, dt, window_size, device="cuda"):
         super().__init__()
@@ -136,13 +208,15 @@ class VanRossumRateLoss(nn.Module):
     def forward(self, target_rate, output_spikes=None, output_probabilities=None):
         signal = output_probabilities if output_probabilities is not None else output_spikes
         a_r, a_d = _step_decay(self.kernel_rise), _step_decay(self.kernel_decay)
-        out_rise, out_smooth = _DoubleExponential.apply(
-            signal, a_r, a_d, self.prev_output_rise, self.prev_output_smooth)  # fmt: skip
-        with torch.no_grad():
-            _, tgt_smooth, tgt_last_r, tgt_last_s = filter_forward(
-                target_rate, a_r, a_d, self.prev_target_rise, self.prev_target_smooth, rise=False)  # fmt: skip
-        self.prev_output_rise = out_rise[:, -1:].detach()
-        self.prev_output_smooth = out_smooth[:, -1:].detach()
-        self.prev_target_rise = tgt_last_r[:, None]
-        self.prev_target_smooth = tgt_last_s[:, None]
-        return ((out_smooth - tgt_smooth) ** 2).mean()
+        B, T, N = signal.shape
+        carry = None
+        if self.prev_output_rise is not None:
+            parts = [self.prev_output_rise, self.prev_output_smooth, self.prev_target_rise,
+                     self.prev_target_smooth]  # fmt: skip
+            carry = torch.stack([q.detach().reshape(B, N).float() for q in parts]).contiguous()
+        state = {}
+        loss = _VanRossumRate.apply(signal, target_rate.expand(B, T, N), carry, a_r, a_d, state)
+        last = state["last"]
+        self.prev_output_rise, self.prev_output_smooth = last[0][:, None], last[1][:, None]
+        self.prev_target_rise, self.prev_target_smooth = last[2][:, None], last[3][:, None]
+        return loss
