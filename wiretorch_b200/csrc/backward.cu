@@ -19,28 +19,18 @@
 namespace wt {
 namespace {
 
-struct BwdTables {
-    float dr[WT_MAX_CHANNELS], dd[WT_MAX_CHANNELS], jr[WT_MAX_CHANNELS], jd[WT_MAX_CHANNELS];
-    float E[WT_MAX_CHANNELS], clip[WT_MAX_CHANNELS], mga[WT_MAX_CHANNELS], mglc[WT_MAX_CHANNELS];
-    int in[WT_MAX_CHANNELS];
+// The saved quantities of one step, loaded ahead of their use: they do not depend on the
+// adjoint recursion, so the scan keeps kAhead steps of loads in flight.
+template <int S>
+struct StepIn {
+    float v, gs, ga, gp;
+    unsigned sb, hb;
+    float G[S];
 };
+constexpr int kAhead = 3;
 
 template <int S, bool SYN>
 __global__ void __launch_bounds__(kBlock) backward_kernel(const WtNet net, const WtBackward bw) {
-    __shared__ BwdTables tab;
-    if (threadIdx.x < WT_MAX_CHANNELS) {
-        const int c = threadIdx.x;
-        tab.dr[c] = net.decay_r[c];
-        tab.dd[c] = net.decay_d[c];
-        tab.jr[c] = net.jump_r[c];
-        tab.jd[c] = net.jump_d[c];
-        tab.E[c] = net.E_syn[c];
-        tab.clip[c] = net.g_clip[c];
-        tab.mga[c] = net.mg_a[c];
-        tab.mglc[c] = net.mg_lc[c];
-        tab.in[c] = net.input_of[c];
-    }
-    __syncthreads();
     const int N = net.N, C = net.C, T = bw.T;
     const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= (long long)net.B * N) return;
@@ -56,6 +46,9 @@ __global__ void __launch_bounds__(kBlock) backward_kernel(const WtNet net, const
     const float g_L = Cm * rate, inv_C = 1.0f / Cm;
     const float a_decay = ADAPT ? net.adapt_decay[n] : 0.0f;
     const float E_a = ADAPT ? net.E_adapt[n] : 0.0f;
+    int in_c[S];
+#pragma unroll
+    for (int c = 0; c < S; c++) in_c[c] = net.input_of[c];
 
     float dv = 0.0f, la = 0.0f;
     float lr[S], ld[S];
@@ -70,47 +63,68 @@ __global__ void __launch_bounds__(kBlock) backward_kernel(const WtNet net, const
     float acc_theta = 0.0f, acc_reset = 0.0f, acc_E_L = 0.0f, acc_C_m = 0.0f, acc_beta = 0.0f;
     float acc_adapt = 0.0f, acc_adapt_decay = 0.0f, acc_E_a = 0.0f;
 
-    for (int t = T - 1; t >= 0; t--) {
-        const size_t o = ((size_t)b * T + t) * N + n;
-        const float v = bw.v_saved[o];
-        const size_t wd = ((size_t)b * T + t) * words + (n >> 5);
-        const float s = (bw.spike_bits[wd] >> (n & 31)) & 1u ? 1.0f : 0.0f;
-        const float held = (REF && ((bw.held_bits[wd] >> (n & 31)) & 1u)) ? 1.0f : 0.0f;
-        const float r = fmaxf(s, held);
-        float G[S];
-        const float *Gs = bw.G_saved + ((size_t)b * T + t) * S * N + n;
+    const size_t TN = (size_t)T * N;
+    const float *v_b = bw.v_saved + (size_t)b * TN + n;
+    const float *gs_b = bw.grad_spikes + (size_t)b * TN + n;
+    const float *G_b = bw.G_saved + (size_t)b * TN * S + n;
+    const uint32_t *sb_b = bw.spike_bits + (size_t)b * T * words + (n >> 5);
+    const uint32_t *hb_b = REF ? bw.held_bits + (size_t)b * T * words + (n >> 5) : nullptr;
+    auto load = [&](int t, StepIn<S> &in) {
+        const size_t o = (size_t)t * N;
+        in.v = __ldg(v_b + o);
+        in.gs = __ldg(gs_b + o);
+        in.sb = __ldg(sb_b + (size_t)t * words);
+        in.hb = REF ? __ldg(hb_b + (size_t)t * words) : 0u;
+        in.ga = ADAPT ? __ldg(bw.a_saved + (size_t)b * TN + o + n) : 0.0f;
+        in.gp = (PROB && bw.grad_prob) ? __ldg(bw.grad_prob + (size_t)b * TN + o + n) : 0.0f;
 #pragma unroll
-        for (int c = 0; c < S; c++) G[c] = Gs[(size_t)c * N];
+        for (int c = 0; c < S; c++) in.G[c] = __ldg(G_b + ((size_t)t * S + c) * N);
+    };
+    StepIn<S> q[kAhead];
+#pragma unroll
+    for (int d = 0; d < kAhead; d++)
+        if (T - 1 - d >= 0) load(T - 1 - d, q[d]);
+
+    for (int t = T - 1; t >= 0; t--) {
+        const StepIn<S> cur = q[0];
+#pragma unroll
+        for (int d = 0; d + 1 < kAhead; d++) q[d] = q[d + 1];
+        if (t - kAhead >= 0) load(t - kAhead, q[kAhead - 1]);
+        const float v = cur.v;
+        const float s = (cur.sb >> (n & 31)) & 1u ? 1.0f : 0.0f;
+        const float held = (REF && ((cur.hb >> (n & 31)) & 1u)) ? 1.0f : 0.0f;
+        const float r = fmaxf(s, held);
+        const float *G = cur.G;
 
         // The input of step t entered the state step t + 1 saw: its adjoint.
         float *Qt = bw.Q + ((size_t)b * T + t) * C * N + n;
         for (int c = 0; c < C; c++) {
-            float q = 0.0f;
+            float qc = 0.0f;
 #pragma unroll
             for (int j = 0; j < S; j++)
-                if (tab.in[j] == c) q = q + (tab.jr[j] * lr[j] + tab.jd[j] * ld[j]);
-            Qt[(size_t)c * N] = q;
+                if (in_c[j] == c) qc = qc + (net.jump_r[j] * lr[j] + net.jump_d[j] * ld[j]);
+            Qt[(size_t)c * N] = qc;
         }
         if (SYN && (wants & (WT_W_DECAY | WT_W_JUMP))) {
             const float *Xt = bw.X_saved + ((size_t)b * T + t) * C * N + n;
 #pragma unroll
             for (int c = 0; c < S; c++) {
-                const float base = tab.in[c] >= 0 ? Xt[(size_t)tab.in[c] * N] : 0.0f;
+                const float base = in_c[c] >= 0 ? Xt[(size_t)in_c[c] * N] : 0.0f;
                 if (wants & WT_W_JUMP) {
                     acc_jr[c] += lr[c] * base;
                     acc_jd[c] += ld[c] * base;
                 }
                 if (wants & WT_W_DECAY) {
-                    acc_dr[c] += tab.jr[c] * base * H_r[c];
-                    acc_dd[c] += tab.jd[c] * base * H_d[c];
-                    H_r[c] = lr[c] + tab.dr[c] * H_r[c];
-                    H_d[c] = ld[c] + tab.dd[c] * H_d[c];
+                    acc_dr[c] += net.jump_r[c] * base * H_r[c];
+                    acc_dd[c] += net.jump_d[c] * base * H_d[c];
+                    H_r[c] = lr[c] + net.decay_r[c] * H_r[c];
+                    H_d[c] = ld[c] + net.decay_d[c] * H_d[c];
                 }
             }
         }
         float g_a = 0.0f;
         if (ADAPT) {
-            g_a = bw.a_saved[o];
+            g_a = cur.ga;
             if (wants & WT_W_ADAPT) acc_adapt += la * s;
             if (wants & WT_W_ADAPT_DECAY) acc_adapt_decay += la * g_a;
         }
@@ -120,13 +134,13 @@ __global__ void __launch_bounds__(kBlock) backward_kernel(const WtNet net, const
         float Ssum = 0.0f, EG = 0.0f;
 #pragma unroll
         for (int c = 0; c < S; c++) {
-            Gc[c] = fminf(fmaxf(G[c], 0.0f), tab.clip[c]);
-            float cg = G[c] < tab.clip[c] ? 1.0f : (G[c] == tab.clip[c] ? 0.5f : 0.0f);
+            Gc[c] = fminf(fmaxf(G[c], 0.0f), net.g_clip[c]);
+            float cg = G[c] < net.g_clip[c] ? 1.0f : (G[c] == net.g_clip[c] ? 0.5f : 0.0f);
             clampg[c] = G[c] >= 0.0f ? cg : 0.0f;
-            Bm[c] = MG ? sigmoid(tab.mga[c] * v - tab.mglc[c]) : 1.0f;
+            Bm[c] = MG ? sigmoid(net.mg_a[c] * v - net.mg_lc[c]) : 1.0f;
             Ge[c] = MG ? Gc[c] * Bm[c] : Gc[c];
             Ssum = Ssum + Ge[c];
-            EG = EG + Ge[c] * tab.E[c];
+            EG = EG + Ge[c] * net.E_syn[c];
         }
         const float gx = dv * (1.0f - r);
         float J = g_L * (v - E_L) + v * Ssum - EG;
@@ -143,9 +157,9 @@ __global__ void __launch_bounds__(kBlock) backward_kernel(const WtNet net, const
         float dG[S];
 #pragma unroll
         for (int c = 0; c < S; c++) {
-            const float dGe = k0 + k1 * tab.E[c];
+            const float dGe = k0 + k1 * net.E_syn[c];
             if (MG) {
-                dv_in += dGe * Gc[c] * tab.mga[c] * Bm[c] * (1.0f - Bm[c]);
+                dv_in += dGe * Gc[c] * net.mg_a[c] * Bm[c] * (1.0f - Bm[c]);
                 dG[c] = dGe * Bm[c] * clampg[c];
             } else {
                 dG[c] = dGe * clampg[c];
@@ -170,7 +184,7 @@ __global__ void __launch_bounds__(kBlock) backward_kernel(const WtNet net, const
         }
         // The spike (surrogate) and probability of step t, both of v - theta.
         const float xv = v - theta;
-        const float gs = bw.grad_spikes[o];
+        const float gs = cur.gs;
         float g_x;
         if (SAMPLE) {
             const float p = sigmoid(k * xv);
@@ -181,15 +195,15 @@ __global__ void __launch_bounds__(kBlock) backward_kernel(const WtNet net, const
         }
         if (PROB && bw.grad_prob) {
             const float p = sigmoid(k * xv);
-            g_x += bw.grad_prob[o] * k * p * (1.0f - p);
+            g_x += cur.gp * k * p * (1.0f - p);
         }
         if (REF) g_x *= 1.0f - held;
         dv = dv_in + g_x;
         acc_theta -= g_x;
 #pragma unroll
         for (int c = 0; c < S; c++) {
-            lr[c] = lr[c] * tab.dr[c] + dG[c];
-            ld[c] = ld[c] * tab.dd[c] + dG[c];
+            lr[c] = lr[c] * net.decay_r[c] + dG[c];
+            ld[c] = ld[c] * net.decay_d[c] + dG[c];
         }
     }
 
