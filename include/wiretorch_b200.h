@@ -198,7 +198,8 @@ typedef struct {
 /* Gradients carried along the connectome's edges, from the adjoints Q of a reverse scan:
  * for every event of the run (a recurrent spike, from the saved spike bits, or a
  * non-zero input x) and every edge e of its slot (pathway k, target n, input channel c),
- * with a = the event's value times its gating factor:
+ * with a = the event's value times its gating factor (summed per edge over the source's
+ * events first, then added once per edge):
  *   g_scale[k, n] += a * w[e] * jf[k, c] * Q[b, t, c, n]      (B-summed, float64)
  *   g_w[e]        += a * scale[k, n] * jf[k, c] * Q[b, t, c, n] (float64)
  * and, for every input column i, trial and step, whether or not it fired,
@@ -210,9 +211,16 @@ typedef struct {
     const float *w_raw, *scale, *jf;
     const int32_t *chunk_path;
     double *g_scale;             /* (K, N) or NULL */
-    double *g_w;                 /* (E) or NULL */
+    double *g_w;                 /* (E) or NULL; accumulated into (the caller zeroes it) */
     float *g_x;                  /* (B, T, n_in) or NULL */
+    /* scratch for g_scale / g_w: each source's firing bits over (trial, step),
+     * wt_edge_grads_scratch_words(net, T) words, and a work counter (1 word) */
+    uint32_t *fired;
+    uint32_t *work;
 } WtEdgeGrads;
+
+/* 32-bit words of WtEdgeGrads.fired for a run of T steps. */
+int64_t wt_edge_grads_scratch_words(const WtNet *net, int32_t T);
 
 /* The reverse scan. Replaces `scan_backward` (conductance/kernels.py:382-568, driven by
  * conductance/engine.py:358-383 `_backward`). */

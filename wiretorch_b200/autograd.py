@@ -47,6 +47,7 @@ class _EdgeArgs(_lib.C.Structure):
         ("T", _lib.C.c_int32), ("spike_bits", _lib.P), ("x", _lib.P), ("f_saved", _lib.P),
         ("Q", _lib.P), ("w_raw", _lib.P), ("scale", _lib.P), ("jf", _lib.P),
         ("chunk_path", _lib.P), ("g_scale", _lib.P), ("g_w", _lib.P), ("g_x", _lib.P),
+        ("fired", _lib.P), ("work", _lib.P),
     ]  # fmt: skip
 
 
@@ -177,6 +178,11 @@ class _Simulate(torch.autograd.Function):
             if need_x:
                 g_x = torch.empty(x.shape, device=device)
                 eg.g_x = g_x.data_ptr()
+            if need_scale or need_w:
+                words = _lib.lib().wt_edge_grads_scratch_words(_lib.C.byref(net), T)
+                _lib.check(0 if words >= 0 else 1, "wt_edge_grads_scratch_words")
+                fired = torch.empty(words + 1, dtype=torch.int32, device=device)
+                eg.fired, eg.work = fired.data_ptr(), fired[words:].data_ptr()
             with _lib.timed("wt_edge_grads"):
                 rc = _lib.lib().wt_edge_grads(_lib.C.byref(net), _lib.C.byref(eg), stream)
             _lib.check(rc, "wt_edge_grads")

@@ -233,69 +233,178 @@ __global__ void __launch_bounds__(kBlock) backward_kernel(const WtNet net, const
     }
 }
 
-// One warp per (trial, step, word of 32 sources): every set source's slots and chunks,
-// the whole warp over each chunk's edges.
-__global__ void edge_grads_kernel(const WtNet net, const WtEdgeGrads eg, int rec_words, int in_words) {
+// The edge gradients, source by source. First each source's firing over the whole run
+// is transposed into a bit row over (trial, step) ("fired"); then one warp per source
+// (taken from a work counter) lists the (trial, step) of its events in shared memory and
+// walks every edge of its slots with them: each lane sums a * Q[b, t, c, n] for its
+// edges in registers and adds the sum once per edge — one reduction per edge instead of
+// one per (event, edge), and each edge's target and weight read once per source instead
+// of once per event.
+
+constexpr int kFiredGroup = 8;  // 32-step words written together per source (32 bytes)
+
+// Recurrent sources: a warp per (word of 32 neurons, group of 8 x 32 (trial, step)).
+__global__ void fired_rec_kernel(const WtEdgeGrads eg, int N, long long BT, int words, long long BTw8) {
     const int lane = threadIdx.x & 31;
     const long long warp = ((long long)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
-    const long long nwarps = ((long long)gridDim.x * blockDim.x) >> 5;
-    const int N = net.N, C = net.C, T = eg.T, n_in = net.n_in;
-    const long long per_bt = rec_words + in_words;
-    const long long total = (long long)net.B * T * per_bt;
-    for (long long w = warp; w < total; w += nwarps) {
-        const int bt = (int)(w / per_bt);
-        const int word = (int)(w % per_bt);
-        const int b = bt / T, t = bt % T;
-        unsigned mask;
-        float value;
-        int j;
-        if (word < rec_words) {
-            mask = eg.spike_bits[(size_t)bt * rec_words + word];
-            j = word * 32 + lane;
-            value = 1.0f;
-        } else {
-            const int c = (word - rec_words) * 32 + lane;
-            const float xv = c < n_in ? eg.x[(size_t)bt * n_in + c] : 0.0f;
-            mask = __ballot_sync(kFull, xv != 0.0f);
-            j = N + c;
-            value = xv;
+    const long long groups = BTw8 / kFiredGroup;
+    if (warp >= (long long)words * groups) return;
+    const int w = (int)(warp / groups);
+    const long long g = warp % groups;
+    uint32_t out[kFiredGroup];
+#pragma unroll
+    for (int k = 0; k < kFiredGroup; k++) {
+        const long long bt = (g * kFiredGroup + k) * 32 + lane;
+        const uint32_t word = bt < BT ? __ldg(eg.spike_bits + bt * words + w) : 0u;
+        uint32_t mine = 0;
+        for (int l = 0; l < 32; l++) {
+            const uint32_t r = __ballot_sync(kFull, (word >> l) & 1u);
+            if (lane == l) mine = r;
         }
-        const float *Qbt = eg.Q + (size_t)bt * C * N;
-        while (mask) {
-            const int l = __ffs(mask) - 1;
-            mask &= mask - 1;
-            const int src = __shfl_sync(kFull, j, l);
-            const float val = __shfl_sync(kFull, value, l);
-            for (int slot = net.src_slot[src]; slot < net.src_slot[src + 1]; slot++) {
-                float amp = val;
+        out[k] = mine;
+    }
+    const int src = w * 32 + lane;
+    if (src < N) {
+        uint4 *dst = reinterpret_cast<uint4 *>(eg.fired + (size_t)src * BTw8 + g * kFiredGroup);
+        dst[0] = make_uint4(out[0], out[1], out[2], out[3]);
+        dst[1] = make_uint4(out[4], out[5], out[6], out[7]);
+    }
+}
+
+// Input columns (x != 0): a warp per (32 columns, group of 8 x 32 (trial, step)).
+__global__ void fired_in_kernel(const WtEdgeGrads eg, int N, int n_in, long long BT, long long BTw8) {
+    const int lane = threadIdx.x & 31;
+    const long long warp = ((long long)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const long long groups = BTw8 / kFiredGroup;
+    const int cblocks = (n_in + 31) >> 5;
+    if (warp >= (long long)cblocks * groups) return;
+    const int c = (int)(warp / groups) * 32 + lane;
+    const long long g = warp % groups;
+    uint32_t out[kFiredGroup];
+#pragma unroll
+    for (int k = 0; k < kFiredGroup; k++) {
+        uint32_t mine = 0;
+        const long long bt0 = (g * kFiredGroup + k) * 32;
+        for (int i = 0; i < 32; i++) {
+            const long long bt = bt0 + i;
+            if (bt < BT && c < n_in && __ldg(eg.x + bt * n_in + c) != 0.0f) mine |= 1u << i;
+        }
+        out[k] = mine;
+    }
+    if (c < n_in) {
+        uint4 *dst = reinterpret_cast<uint4 *>(eg.fired + (size_t)(N + c) * BTw8 + g * kFiredGroup);
+        dst[0] = make_uint4(out[0], out[1], out[2], out[3]);
+        dst[1] = make_uint4(out[4], out[5], out[6], out[7]);
+    }
+}
+
+constexpr int kEventCap = 512;      // events a warp lists before walking its edges
+constexpr int kEdgeWarps = 8;
+
+__global__ void __launch_bounds__(kEdgeWarps * 32) edge_grads_kernel(const WtNet net, const WtEdgeGrads eg,
+                                                                     long long BT, long long BTw8) {
+    __shared__ int s_bt[kEdgeWarps][kEventCap];
+    __shared__ float s_a[kEdgeWarps][kEventCap];
+    const int lane = threadIdx.x & 31, wib = threadIdx.x >> 5;
+    int *lbt = s_bt[wib];
+    float *la = s_a[wib];
+    const int N = net.N, C = net.C, n_in = net.n_in;
+    const int n_src = N + n_in;
+    const long long BTw = (BT + 31) >> 5;
+    for (;;) {
+        int j = 0;
+        if (lane == 0) j = (int)atomicAdd(eg.work, 1u);
+        j = __shfl_sync(kFull, j, 0);
+        if (j >= n_src) break;
+        const int slot0 = net.src_slot[j], slot1 = net.src_slot[j + 1];
+        if (slot0 == slot1) continue;
+        const uint32_t *fw = eg.fired + (size_t)j * BTw8;
+        const bool is_in = j >= N;
+        const int col = j - N;
+
+        // Walk every edge of the source with the listed events.
+        auto flush = [&](int len) {
+            __syncwarp();
+            for (int slot = slot0; slot < slot1; slot++) {
+                int fcol = -1;
                 if (net.slot_gate) {
                     const int gate = net.slot_gate[slot];
-                    if (gate >= 0)
-                        amp = val * eg.f_saved[(size_t)bt * net.R_f + net.gate_cols[4 * gate + 3] + net.slot_row[slot]];
+                    if (gate >= 0) fcol = net.gate_cols[4 * gate + 3] + net.slot_row[slot];
                 }
                 for (int ch = net.slot_chunk[slot]; ch < net.slot_chunk[slot + 1]; ch++) {
                     const long long d = net.chunk_desc[ch];
                     const long long e0 = d & ((1LL << 56) - 1);
-                    const int len = (int)((unsigned long long)d >> 56);
+                    const int elen = (int)((unsigned long long)d >> 56);
                     const int kp = eg.chunk_path[ch];
-                    for (int q = lane; q < len; q += 32) {
-                        const uint32_t pc = net.edge_col[e0 + q];
-                        const int n = pc & 0x7ffffffu, c = pc >> 27;
-                        const float Qv = Qbt[(size_t)c * N + n];
-                        if (Qv == 0.0f) continue;
-                        const float jfv = eg.jf[(size_t)kp * C + c];
-                        if (eg.g_scale)
-                            atomicAdd(eg.g_scale + (size_t)kp * N + n,
-                                      (double)amp * (double)eg.w_raw[e0 + q] * (double)jfv * (double)Qv);
-                        if (eg.g_w)
-                            atomicAdd(eg.g_w + e0 + q,
-                                      (double)amp * (double)eg.scale[(size_t)kp * N + n] * (double)jfv * (double)Qv);
+                    for (int q0 = 0; q0 < elen; q0 += 128) {
+                        int nq[4], cq[4];
+                        float acc[4];
+#pragma unroll
+                        for (int u = 0; u < 4; u++) {
+                            const int q = q0 + lane + 32 * u;
+                            nq[u] = -1;
+                            cq[u] = 0;
+                            acc[u] = 0.0f;
+                            if (q < elen) {
+                                const uint32_t pc = net.edge_col[e0 + q];
+                                nq[u] = (int)(pc & 0x7ffffffu);
+                                cq[u] = (int)(pc >> 27);
+                            }
+                        }
+#pragma unroll 4
+                        for (int i = 0; i < len; i++) {
+                            const long long bt = lbt[i];
+                            float a = la[i];
+                            if (fcol >= 0) a *= eg.f_saved[bt * net.R_f + fcol];
+                            const float *Qb = eg.Q + bt * C * N;
+#pragma unroll
+                            for (int u = 0; u < 4; u++)
+                                if (nq[u] >= 0) acc[u] += a * __ldg(Qb + (size_t)cq[u] * N + nq[u]);
+                        }
+#pragma unroll
+                        for (int u = 0; u < 4; u++) {
+                            if (nq[u] < 0) continue;
+                            const long long e = e0 + q0 + lane + 32 * u;
+                            const double jfv = eg.jf[(size_t)kp * C + cq[u]];
+                            if (eg.g_scale)
+                                atomicAdd(eg.g_scale + (size_t)kp * N + nq[u], (double)acc[u] * (double)eg.w_raw[e] * jfv);
+                            if (eg.g_w)
+                                atomicAdd(eg.g_w + e, (double)acc[u] * (double)eg.scale[(size_t)kp * N + nq[u]] * jfv);
+                        }
                     }
                 }
             }
+            __syncwarp();
+        };
+
+        // List the source's events, kEventCap/32 words (of 32 steps) at a time.
+        int len = 0;
+        constexpr int kWin = kEventCap / 32;
+        for (long long wb = 0; wb < BTw; wb += kWin) {
+            uint32_t word = (lane < kWin && wb + lane < BTw) ? fw[wb + lane] : 0u;
+            const int cnt = __popc(word);
+            const int incl = warp_inclusive_sum(cnt, lane);
+            const int total = __shfl_sync(kFull, incl, 31);
+            if (total == 0) continue;
+            if (len + total > kEventCap) {
+                flush(len);
+                len = 0;
+            }
+            int off = len + incl - cnt;
+            while (word) {
+                const int bit = __ffs(word) - 1;
+                word &= word - 1;
+                const long long bt = (wb + lane) * 32 + bit;
+                lbt[off] = (int)bt;
+                la[off] = is_in ? eg.x[bt * n_in + col] : 1.0f;
+                off++;
+            }
+            len += total;
         }
+        if (len) flush(len);
     }
 }
+
 
 // One warp per (trial, step, input column): the input's gradient, fired or not.
 __global__ void input_grads_kernel(const WtNet net, const WtEdgeGrads eg) {
@@ -364,14 +473,32 @@ cudaError_t launch_backward(const WtNet &net, const WtBackward &bw, cudaStream_t
     }
 }
 
+long long edge_grads_fired_words(const WtNet &net, int T) {
+    const long long BT = (long long)net.B * T;
+    const long long BTw8 = ((BT + 31) / 32 + kFiredGroup - 1) / kFiredGroup * kFiredGroup;
+    return (long long)(net.N + net.n_in) * BTw8;
+}
+
 cudaError_t launch_edge_grads(const WtNet &net, const WtEdgeGrads &eg, cudaStream_t st) {
-    const int rec_words = (net.N + 31) >> 5, in_words = (net.n_in + 31) >> 5;
+    const long long BT = (long long)net.B * eg.T;
+    const long long BTw8 = ((BT + 31) / 32 + kFiredGroup - 1) / kFiredGroup * kFiredGroup;
     if (eg.g_scale || eg.g_w) {
-        const long long warps = (long long)net.B * eg.T * (rec_words + in_words);
-        long long blocks = (warps + 7) / 8;
-        if (blocks > 148 * 64) blocks = 148 * 64;
-        if (blocks > 0) edge_grads_kernel<<<(int)blocks, 256, 0, st>>>(net, eg, rec_words, in_words);
-        cudaError_t e = cudaGetLastError();
+        const int words = (net.N + 31) >> 5;
+        const long long groups = BTw8 / kFiredGroup;
+        long long warps = (long long)words * groups;
+        if (warps > 0) fired_rec_kernel<<<(unsigned)((warps + 7) / 8), 256, 0, st>>>(eg, net.N, BT, words, BTw8);
+        warps = (long long)((net.n_in + 31) >> 5) * groups;
+        if (warps > 0) fired_in_kernel<<<(unsigned)((warps + 7) / 8), 256, 0, st>>>(eg, net.N, net.n_in, BT, BTw8);
+        cudaError_t e = cudaMemsetAsync(eg.work, 0, sizeof(uint32_t), st);
+        if (e != cudaSuccess) return e;
+        int sms = 0, dev = 0;
+        cudaGetDevice(&dev);
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+        int per_sm = 0;
+        e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, edge_grads_kernel, kEdgeWarps * 32, 0);
+        if (e != cudaSuccess) return e;
+        edge_grads_kernel<<<sms * (per_sm > 0 ? per_sm : 1), kEdgeWarps * 32, 0, st>>>(net, eg, BT, BTw8);
+        e = cudaGetLastError();
         if (e != cudaSuccess) return e;
     }
     if (eg.g_x && net.n_in > 0) {

@@ -11,6 +11,7 @@ cudaError_t launch_forward_s(const WtNet &net, const WtForward &run, const WtWor
                              cudaStream_t st, int grid_cap);
 cudaError_t launch_backward(const WtNet &net, const WtBackward &bw, cudaStream_t st);
 cudaError_t launch_edge_grads(const WtNet &net, const WtEdgeGrads &eg, cudaStream_t st);
+long long edge_grads_fired_words(const WtNet &net, int T);
 cudaError_t launch_filter(const WtFilterArgs &f, cudaStream_t st);
 cudaError_t launch_filter_grad(const WtFilterGradArgs &f, cudaStream_t st);
 cudaError_t launch_van_rossum(const WtVanRossumArgs &a, cudaStream_t st);
@@ -153,8 +154,15 @@ int wt_edge_grads(const WtNet *net, const WtEdgeGrads *eg, void *stream) {
     if ((eg->g_w || eg->g_x) && !eg->scale) return fail(WT_ERR_ARGS, "missing scale%s");
     if (eg->g_x && !eg->w_raw) return fail(WT_ERR_ARGS, "missing raw weights%s");
     if (net->slot_gate && !eg->f_saved) return fail(WT_ERR_ARGS, "missing gating factors%s");
+    if ((eg->g_scale || eg->g_w) && (!eg->fired || !eg->work)) return fail(WT_ERR_ARGS, "missing edge scratch%s");
+    if ((long long)net->B * eg->T >= (1LL << 31)) return fail(WT_ERR_UNSUPPORTED, "trials x steps must be below 2^31%s");
     if (eg->T == 0) return WT_OK;
     return launch_status(wt::launch_edge_grads(*net, *eg, (cudaStream_t)stream), "edge gradients");
+}
+
+int64_t wt_edge_grads_scratch_words(const WtNet *net, int32_t T) {
+    if (check_net(net) || T < 0) return -1;
+    return wt::edge_grads_fired_words(*net, T);
 }
 
 int wt_filter_forward(const WtFilterArgs *f, void *stream) {
