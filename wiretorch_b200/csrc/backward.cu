@@ -29,13 +29,15 @@ struct StepIn {
 };
 constexpr int kAhead = 3;
 
-template <int S, bool SYN>
-__global__ void __launch_bounds__(kBlock) backward_kernel(const WtNet net, const WtBackward bw) {
+// PHYS: some physiology gradient is wanted (else the scan carries only dL/dv, dL/dg and
+// Q); SYN: some synapse parameter's.
+template <int S, bool PHYS, bool SYN>
+__global__ void __launch_bounds__(kBlock, (PHYS || S > 2) ? 1 : 3) backward_kernel(const WtNet net, const WtBackward bw) {
     const int N = net.N, C = net.C, T = bw.T;
     const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= (long long)net.B * N) return;
     const int b = (int)(i / N), n = (int)(i % N);
-    const int flags = bw.flags, wants = bw.wants;
+    const int flags = bw.flags, wants = PHYS ? bw.wants : 0;
     const bool REF = flags & WT_F_REFRACTORY, MG = flags & WT_F_MG_BLOCK, ADAPT = flags & WT_F_ADAPT;
     const bool SAMPLE = flags & WT_F_SAMPLE, PROB = flags & WT_F_PROB;
     const int words = (N + 31) >> 5;
@@ -149,7 +151,7 @@ __global__ void __launch_bounds__(kBlock) backward_kernel(const WtNet net, const
             J = J + g_a * (v - E_a);
         }
         const float em = expm1f(-dt * (rate + Ssum * inv_C));
-        const float inv_g = 1.0f / (g_L + Ssum);
+        const float inv_g = __fdividef(1.0f, g_L + Ssum);  // a gradient: 2-ulp division suffices
         const float a = 1.0f + em, phi = -em * inv_g;
         const float phi_S = (a * dt * inv_C - phi) * inv_g;
         const float k0 = -gx * (phi_S * J + phi * v), k1 = gx * phi;
@@ -191,7 +193,7 @@ __global__ void __launch_bounds__(kBlock) backward_kernel(const WtNet net, const
             g_x = gs * k * p * (1.0f - p);
         } else {
             const float d = k * fabsf(xv) + 1.0f;
-            g_x = gs / (d * d);
+            g_x = __fdividef(gs, d * d);
         }
         if (PROB && bw.grad_prob) {
             const float p = sigmoid(k * xv);
@@ -451,9 +453,11 @@ cudaError_t launch_bwd_s(const WtNet &net, const WtBackward &bw, cudaStream_t st
     const long long items = (long long)net.B * net.N;
     const int blocks = (int)((items + kBlock - 1) / kBlock);
     if (bw.wants & (WT_W_E_SYN | WT_W_DECAY | WT_W_JUMP))
-        backward_kernel<S, true><<<blocks, kBlock, 0, st>>>(net, bw);
+        backward_kernel<S, true, true><<<blocks, kBlock, 0, st>>>(net, bw);
+    else if (bw.wants)
+        backward_kernel<S, true, false><<<blocks, kBlock, 0, st>>>(net, bw);
     else
-        backward_kernel<S, false><<<blocks, kBlock, 0, st>>>(net, bw);
+        backward_kernel<S, false, false><<<blocks, kBlock, 0, st>>>(net, bw);
     return cudaGetLastError();
 }
 

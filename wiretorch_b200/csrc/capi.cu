@@ -40,6 +40,8 @@ int check_net(const WtNet *n) {
     if (n->S < 1 || n->S > WT_MAX_CHANNELS) return fail(WT_ERR_UNSUPPORTED, "S must be in 1..8%s");
     if (n->C < 1 || n->C > WT_MAX_CHANNELS) return fail(WT_ERR_UNSUPPORTED, "C must be in 1..8%s");
     if (n->N >= (1 << 27)) return fail(WT_ERR_UNSUPPORTED, "N must be below 2^27%s");
+    if ((unsigned long long)n->B * (((unsigned long long)n->n_in + 31) & ~31ull) + 32 >= (1ull << 32))
+        return fail(WT_ERR_UNSUPPORTED, "trials x input columns must be below 2^32%s");
     if ((unsigned long long)n->B * (unsigned long long)(n->n_chunks > 0 ? n->n_chunks : 1) >= (1ull << 32))
         return fail(WT_ERR_UNSUPPORTED, "trials x chunks must be below 2^32%s");
     if (!n->theta || !n->U_reset || !n->E_L || !n->C_m || !n->beta)

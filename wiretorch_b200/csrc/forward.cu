@@ -170,16 +170,13 @@ __device__ void emit(const WtNet &net, const WtForward &run, const WtWorkspace &
 
 // Emission of ungated sources: a source's chunks are contiguous (src_chunk), so the warp
 // reserves room for all its lanes' events with one atomic, then writes each spiking
-// lane's events with all 32 lanes. `on`: the lane's source j fires with `value`.
+// lane's events with all 32 lanes. `on`: the lane's source fires with `value`.
+// A source's chunks are [c0, c0 + cnt) (its src_chunk range, which the caller has loaded).
 __device__ __forceinline__ void emit_fast(const WtNet &net, const WtWorkspace &ws, int step, bool on, int b,
-                                          int j, float value, int lane) {
+                                          int c0, int cnt, float value, int lane) {
     unsigned m = __ballot_sync(kFull, on);
     if (!m) return;
-    int c0 = 0, cnt = 0;
-    if (on) {
-        c0 = net.src_chunk[j];
-        cnt = net.src_chunk[j + 1] - c0;
-    }
+    if (!on) cnt = 0;
     const int incl = warp_inclusive_sum(cnt, lane);
     const int total = __shfl_sync(kFull, incl, 31);
     if (total == 0) return;
@@ -252,6 +249,7 @@ struct Cursor {
 struct NeuronConsts {
     float theta, U_reset, E_L, Cm, rate, g_L, adapt, a_decay, E_a;
     int n_ref;
+    int c0, cnt;  // the neuron's chunks (as a source)
 };
 
 template <int S, int FEAT>
@@ -329,6 +327,8 @@ __global__ void __launch_bounds__(kThreads, 1) forward_kernel(const WtNet net, c
             k.rate = -log1pf(net.beta[n] - 1.0f) / dt;
             k.g_L = k.Cm * k.rate;
             k.n_ref = REF ? net.n_ref[n] : 0;
+            k.c0 = net.src_chunk[n];
+            k.cnt = net.src_chunk[n + 1] - k.c0;
             if (ADAPT) {
                 k.adapt = net.adapt[n];
                 k.a_decay = net.adapt_decay[n];
@@ -364,11 +364,25 @@ __global__ void __launch_bounds__(kThreads, 1) forward_kernel(const WtNet net, c
         }
         cp_async_commit();
     };
-    auto emit_any = [&](int step, bool valid, int b, int j, float value) {
+    // a neuron's spike (its chunk range known), or an input column's value
+    auto emit_neuron = [&](int step, bool valid, int b, int j, const NeuronConsts &k, float value) {
         if (gated)
             emit(net, run, ws, step, valid, b, j, value, true, lane);
         else
-            emit_fast(net, ws, step, valid && value != 0.0f, b, j, value, lane);
+            emit_fast(net, ws, step, valid && value != 0.0f, b, k.c0, k.cnt, value, lane);
+    };
+    auto emit_input = [&](int step, bool valid, int b, int j, float value) {
+        if (gated) {
+            emit(net, run, ws, step, valid, b, j, value, true, lane);
+        } else {
+            const bool on = valid && value != 0.0f;
+            int c0 = 0, cnt = 0;
+            if (on) {
+                c0 = net.src_chunk[j];
+                cnt = net.src_chunk[j + 1] - c0;
+            }
+            emit_fast(net, ws, step, on, b, c0, cnt, value, lane);
+        }
     };
 
     // Phase 0: empty accumulators and event counts; resident state.
@@ -417,15 +431,15 @@ __global__ void __launch_bounds__(kThreads, 1) forward_kernel(const WtNet net, c
                 float held;
                 s = spike_of(v, k.theta, cnt, u01, sflags, ksur, held);
             }
-            emit_any(0, valid, q.b, n, s);
+            emit_neuron(0, valid, q.b, n, k, s);
         }
     }
     for (long long base = warp0; base < itemsI; base += nthreads) {
-        const long long i = base + lane;
-        const int b = (int)(i / Ip), c = (int)(i % Ip);
+        const unsigned i = (unsigned)(base + lane);  // B x Ip < 2^32 (checked by the host)
+        const int b = (int)(i / (unsigned)Ip), c = (int)(i - (unsigned)b * Ip);
         const bool valid = c < n_in;
         const float xv = valid ? run.x[((size_t)b * run.T_total + run.t0) * n_in + c] : 0.0f;
-        emit_any(0, valid, b, N + c, xv);
+        emit_input(0, valid, b, N + c, xv);
     }
     if (!bar.sync(ws.err)) return;
 
@@ -665,7 +679,7 @@ __global__ void __launch_bounds__(kThreads, 1) forward_kernel(const WtNet net, c
                     if (REF) run.held_bits[w] = hb;
                 }
             }
-            if (emit_next) emit_any(t + 1, valid, b, n, s_next);
+            if (emit_next) emit_neuron(t + 1, valid, b, n, k, s_next);
             q.next(B, N, Np, TN);
             rp += ks * 32;
         }
@@ -673,11 +687,11 @@ __global__ void __launch_bounds__(kThreads, 1) forward_kernel(const WtNet net, c
         // ---------------- the input columns of the next step ----------------
         if (emit_next) {
             for (long long base = warp0; base < itemsI; base += nthreads) {
-                const long long i = base + lane;
-                const int b = (int)(i / Ip), c = (int)(i % Ip);
+                const unsigned i = (unsigned)(base + lane);
+                const int b = (int)(i / (unsigned)Ip), c = (int)(i - (unsigned)b * Ip);
                 const bool valid = c < n_in;
                 const float xv = valid ? run.x[((size_t)b * run.T_total + t_abs + 1) * n_in + c] : 0.0f;
-                emit_any(t + 1, valid, b, N + c, xv);
+                emit_input(t + 1, valid, b, N + c, xv);
             }
         }
         if (!bar.sync(ws.err)) return;
