@@ -217,14 +217,18 @@ __device__ __forceinline__ float spike_of(float v, float theta, int counter, flo
 }
 
 static_assert(WT_CHUNK_EDGES <= 128, "a chunk's edges take at most four per lane");
-constexpr int kWarps = 16;                // warps per block of the forward kernel
-constexpr int kThreads = kWarps * 32;     // one block per SM
-constexpr int kMaxRing = 4;               // deepest ring of staged items
-
 // Feature bits of a specialised kernel: the refractory period and saving for the backward
 // pass known at compile time; everything else (adaptation, Mg block, escape noise,
 // gating, probabilities, tracking, saved input) in the generic variant, tested at run time.
 constexpr int kRef = 1, kSave = 2, kGeneric = 4;
+
+// Warps per block of the forward kernel (one block per SM): 24 for the specialised
+// kernels of up to four channels (80 registers a thread, as good as no spill), 16 for
+// the others (up to 128 registers).
+template <int S, int FEAT>
+constexpr int warps_of() { return ((FEAT & kGeneric) == 0 && S <= 4) ? 24 : 16; }
+constexpr int kMaxRing = 4;               // deepest ring of staged items
+
 
 // A warp's position in its run of items: neuron group g, trial b, and the trial's row
 // offsets in the (B, N) state, the (B, Np) accumulators and the (B, T_total, N) outputs.
@@ -253,7 +257,7 @@ struct NeuronConsts {
 };
 
 template <int S, int FEAT>
-__global__ void __launch_bounds__(kThreads, 1) forward_kernel(const WtNet net, const WtForward run,
+__global__ void __launch_bounds__(warps_of<S, FEAT>() * 32, 1) forward_kernel(const WtNet net, const WtForward run,
                                                              const WtWorkspace ws, const Geometry geo) {
     extern __shared__ __align__(16) float smem[];
     constexpr bool GEN = FEAT & kGeneric;
@@ -751,7 +755,7 @@ __global__ void __launch_bounds__(kThreads, 1) forward_kernel(const WtNet net, c
 
 }  // namespace
 
-// The launch geometry: one block of kWarps warps per SM (fewer blocks when there are
+// The launch geometry: one block of warps_of<S, FEAT>() warps per SM (fewer blocks when there are
 // fewer items than warps); state resident in shared memory when every warp's share fits
 // beside a ring of at least two slots, else streamed with the deepest ring that fits.
 // Cached per device, kernel and shape.
@@ -771,6 +775,7 @@ static cudaError_t geometry_for(const WtNet &net, int flags, Geometry &geo, int 
     static int grids[64];
     static size_t dyns[64];
     static int n_cached = 0;
+    constexpr int NW = warps_of<S, FEAT>();
     const void *kern = (const void *)forward_kernel<S, FEAT>;
     int dev = 0;
     cudaGetDevice(&dev);
@@ -803,14 +808,14 @@ static cudaError_t geometry_for(const WtNet &net, int flags, Geometry &geo, int 
     g.w_gd = 1 + REF + ADAPT;
     g.w_gr = g.w_gd + S;
     g.ks = g.w_gr + n_rise;
-    const long long blocks = std::min<long long>(sms, (g.W + kWarps - 1) / kWarps);
-    const long long nw = blocks * kWarps;
+    const long long blocks = std::min<long long>(sms, (g.W + NW - 1) / NW);
+    const long long nw = blocks * NW;
     g.max_items = (int)((g.W + nw - 1) / nw);
     const long long x_rows = 2LL * net.C;  // a slot's int64 inputs, in 128-byte rows
     g.D = 0;
     for (int D = kMaxRing; D >= 2 && !g.D; D--) {  // resident, with at least two slots
         const long long rows = (long long)g.max_items * g.ks + D * x_rows;
-        if (rows * 128 * kWarps <= max_dyn) {
+        if (rows * 128 * NW <= max_dyn) {
             g.resident = 1;
             g.D = D;
             g.slot_rows = (int)x_rows;
@@ -819,7 +824,7 @@ static cudaError_t geometry_for(const WtNet &net, int flags, Geometry &geo, int 
     }
     for (int D = kMaxRing; D >= 1 && !g.D; D--) {  // streamed
         const long long rows = D * (x_rows + g.ks);
-        if (rows * 128 * kWarps <= max_dyn) {
+        if (rows * 128 * NW <= max_dyn) {
             g.resident = 0;
             g.D = D;
             g.slot_rows = (int)(x_rows + g.ks);
@@ -827,9 +832,9 @@ static cudaError_t geometry_for(const WtNet &net, int flags, Geometry &geo, int 
         }
     }
     if (!g.D) return cudaErrorInvalidConfiguration;
-    const size_t d = (size_t)g.warp_rows * 128 * kWarps;
+    const size_t d = (size_t)g.warp_rows * 128 * NW;
     int per_sm = 0;
-    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, forward_kernel<S, FEAT>, kThreads, d);
+    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, forward_kernel<S, FEAT>, NW * 32, d);
     if (e != cudaSuccess) return e;
     if (per_sm < 1) return cudaErrorInvalidConfiguration;
     geo = g;
@@ -856,7 +861,7 @@ static cudaError_t launch_sf(const WtNet &net, const WtForward &run, const WtWor
     WtForward r = run;
     WtWorkspace w = ws;
     void *args[] = {&n, &r, &w, &geo};
-    return cudaLaunchCooperativeKernel((const void *)forward_kernel<S, FEAT>, dim3(grid), dim3(kThreads), args, dyn,
+    return cudaLaunchCooperativeKernel((const void *)forward_kernel<S, FEAT>, dim3(grid), dim3(warps_of<S, FEAT>() * 32), args, dyn,
                                        st);
 }
 
