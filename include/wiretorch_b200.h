@@ -300,6 +300,23 @@ int wt_van_rossum_forward(const WtVanRossumArgs *a, void *stream);
  * to the loss's gradient). */
 int wt_van_rossum_backward(const WtVanRossumGradArgs *a, void *stream);
 
+/* The factorised recurrent drive of one step on the tensor cores: for pathways k < KP
+ * (1..4) with weights W_k = U_k V^T, D[k, b, n] = sum_r V[n, r] P[b, k, r], P_k = S_k U_k
+ * the spikes' sum of U rows (fp32), V bf16 with 64 rank slots (a lower rank zero-padded).
+ * tcgen05.mma with the accumulator in tensor memory; P enters as three bf16 parts, so the
+ * product keeps fp32 accuracy. Replaces the dense per-step gather of the assembled
+ * factorised weights (network_simulators/network.py:731-752 `_assemble`, then
+ * conductance/kernels.py:657-689). */
+typedef struct {
+    int32_t B, N, KP;
+    const uint16_t *V;  /* (N, 64) bf16 */
+    const float *P;     /* (B, KP, 64) */
+    float *D;           /* (KP, B, N) */
+    int32_t *err;       /* device error word (WT_ERR_BARRIER if an MMA never completed) */
+} WtLowRankProduct;
+
+int wt_lowrank_product(const WtLowRankProduct *a, void *stream);
+
 /* Reading back: a static description of the last host-side error on this thread. */
 const char *wt_last_error(void);
 

@@ -37,7 +37,7 @@ def test_abi_version(lib):
 def test_structures_match_the_header_sizes():
     """The ctypes mirrors have the members the header declares, in order."""
     text = HEADER.read_text()
-    from wiretorch_b200 import autograd, filtering
+    from wiretorch_b200 import autograd, filtering, lowrank
 
     for struct, cls in (("WtNet", _lib.WtNet), ("WtForward", _lib.WtForward),
                         ("WtWorkspace", _lib.WtWorkspace),
@@ -45,7 +45,8 @@ def test_structures_match_the_header_sizes():
                         ("WtFilterArgs", filtering._FilterArgs),
                         ("WtFilterGradArgs", filtering._FilterGradArgs),
                         ("WtVanRossumArgs", filtering._VanRossumArgs),
-                        ("WtVanRossumGradArgs", filtering._VanRossumGradArgs)):  # fmt: skip
+                        ("WtVanRossumGradArgs", filtering._VanRossumGradArgs),
+                        ("WtLowRankProduct", lowrank._ProductArgs)):  # fmt: skip
         body = re.search(r"typedef struct \{((?:(?!typedef struct).)*?)\}\s*" + struct + ";", text,
                          re.S).group(1)
         body = re.sub(r"/\*.*?\*/", "", body, flags=re.S)

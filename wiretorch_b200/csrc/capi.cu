@@ -12,6 +12,7 @@ cudaError_t launch_forward_s(const WtNet &net, const WtForward &run, const WtWor
 cudaError_t launch_backward(const WtNet &net, const WtBackward &bw, cudaStream_t st);
 cudaError_t launch_edge_grads(const WtNet &net, const WtEdgeGrads &eg, cudaStream_t st);
 long long edge_grads_fired_words(const WtNet &net, int T);
+cudaError_t launch_lowrank_product(const WtLowRankProduct &a, cudaStream_t st);
 cudaError_t launch_filter(const WtFilterArgs &f, cudaStream_t st);
 cudaError_t launch_filter_grad(const WtFilterGradArgs &f, cudaStream_t st);
 cudaError_t launch_van_rossum(const WtVanRossumArgs &a, cudaStream_t st);
@@ -191,6 +192,14 @@ int wt_van_rossum_backward(const WtVanRossumGradArgs *a, void *stream) {
     if (a->B && a->N && a->T && (!a->err || !a->grad_loss || !a->grad_x))
         return fail(WT_ERR_ARGS, "missing loss-gradient buffers%s");
     return launch_status(wt::launch_van_rossum_grad(*a, (cudaStream_t)stream), "van Rossum loss gradient");
+}
+
+int wt_lowrank_product(const WtLowRankProduct *a, void *stream) {
+    if (!a || a->B < 0 || a->N < 0 || a->KP < 1 || a->KP > 4) return fail(WT_ERR_ARGS, "bad low-rank product arguments%s");
+    if (!a->B || !a->N) return WT_OK;
+    if (!a->V || !a->P || !a->D || !a->err) return fail(WT_ERR_ARGS, "missing low-rank product buffers%s");
+    if (((uintptr_t)a->V & 15) || ((uintptr_t)a->P & 15)) return fail(WT_ERR_ARGS, "V and P must be 16-byte aligned%s");
+    return launch_status(wt::launch_lowrank_product(*a, (cudaStream_t)stream), "low-rank product");
 }
 
 }  // extern "C"
