@@ -317,6 +317,45 @@ typedef struct {
 
 int wt_lowrank_product(const WtLowRankProduct *a, void *stream);
 
+/* A network whose recurrent pathways are all factorised, W_k = U_k V^T (k < KP <= 2, one
+ * shared V of rank <= 64), driven by one input column per neuron (n_in == N, input weight
+ * w_in[n]); conductance LIF with refractoriness, S <= 4 synapse channels (exact, one per
+ * synapse type). */
+typedef struct {
+    int32_t B, N, S, KP;
+    const float *theta, *U_reset, *E_L, *C_m, *beta; /* (N) */
+    const int32_t *n_ref;                            /* (N) or NULL */
+    float decay_r[WT_MAX_CHANNELS], decay_d[WT_MAX_CHANNELS];
+    float jump_r[WT_MAX_CHANNELS], jump_d[WT_MAX_CHANNELS];
+    float E_syn[WT_MAX_CHANNELS], g_clip[WT_MAX_CHANNELS];
+    float dt;
+    const uint16_t *U;      /* (N, 64) bf16: each neuron's U row as a source (zero if none) */
+    const int8_t *path_of;  /* (N): the pathway a neuron is a source of, -1: none */
+    const uint16_t *V;      /* (N, 64) bf16 */
+    const float *scale;     /* (KP + 1, N): each pathway's target scale, then the input's */
+    const float *w_in;      /* (N) */
+    uint32_t made;          /* bit 8 k + s: pathway k (k == KP: the input) drives channel s */
+} WtLowRankNet;
+
+/* One forward run of T steps of a WtLowRankNet (same state and output layout as
+ * WtForward: v (B, N), g (B, 2, S, N), counter (B, N), x and spikes (B, T_total, N)). */
+typedef struct {
+    int32_t T, T_total, t0;
+    float *v, *g;
+    int32_t *counter;       /* when n_ref */
+    const float *x;
+    float *spikes;
+    float *P;               /* scratch (3, B, KP, 64) */
+    uint32_t *barrier;      /* (64), zeroed by the call */
+    int32_t *err;           /* device error word */
+} WtLowRankRun;
+
+/* Simulate T steps of a factorised network: one persistent kernel, the recurrent input
+ * of every step a tcgen05.mma product with its accumulator in tensor memory, read by the
+ * same kernel's membrane update (network_simulators/network.py:731-752 and
+ * conductance/engine.py:306-355 in the reference: a dense W assembled, then gathered). */
+int wt_lowrank_forward(const WtLowRankNet *net, const WtLowRankRun *run, void *stream);
+
 /* Reading back: a static description of the last host-side error on this thread. */
 const char *wt_last_error(void);
 

@@ -63,8 +63,11 @@ def compare(engine_sim, net, drive, p, x, v, g, kw, window=10, margin=1e-3, v_at
                     assert m < margin, f"window {w} step {start + tt} trial {b} neuron {n}: flip {m:.2e} mV from threshold"
                     ok[b] = False
                     excused += 1
-        vt = run.tracked["v"].detach().cpu().numpy()
-        dv = np.abs(vt[ok] - v_track[ok, start:stop]).max(initial=0.0)
+        if run.tracked is not None:
+            vt = run.tracked["v"].detach().cpu().numpy()
+            dv = np.abs(vt[ok] - v_track[ok, start:stop]).max(initial=0.0)
+        else:  # an engine without tracking: the voltages the window leaves
+            dv = np.abs(run.v.detach().cpu().numpy()[ok] - states["v"][w + 1][ok]).max(initial=0.0)
         assert dv <= v_atol, f"window {w}: voltage differs by {dv:.2e} mV"
         gk = run.syn.detach().cpu().numpy()
         ref = states["g"][w + 1]

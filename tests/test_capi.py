@@ -46,7 +46,8 @@ def test_structures_match_the_header_sizes():
                         ("WtFilterGradArgs", filtering._FilterGradArgs),
                         ("WtVanRossumArgs", filtering._VanRossumArgs),
                         ("WtVanRossumGradArgs", filtering._VanRossumGradArgs),
-                        ("WtLowRankProduct", lowrank._ProductArgs)):  # fmt: skip
+                        ("WtLowRankProduct", lowrank._ProductArgs),
+                        ("WtLowRankNet", lowrank._LrNet), ("WtLowRankRun", lowrank._LrRun)):  # fmt: skip
         body = re.search(r"typedef struct \{((?:(?!typedef struct).)*?)\}\s*" + struct + ";", text,
                          re.S).group(1)
         body = re.sub(r"/\*.*?\*/", "", body, flags=re.S)

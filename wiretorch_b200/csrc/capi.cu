@@ -13,6 +13,7 @@ cudaError_t launch_backward(const WtNet &net, const WtBackward &bw, cudaStream_t
 cudaError_t launch_edge_grads(const WtNet &net, const WtEdgeGrads &eg, cudaStream_t st);
 long long edge_grads_fired_words(const WtNet &net, int T);
 cudaError_t launch_lowrank_product(const WtLowRankProduct &a, cudaStream_t st);
+cudaError_t launch_lowrank_forward(const WtLowRankNet &net, const WtLowRankRun &run, cudaStream_t st);
 cudaError_t launch_filter(const WtFilterArgs &f, cudaStream_t st);
 cudaError_t launch_filter_grad(const WtFilterGradArgs &f, cudaStream_t st);
 cudaError_t launch_van_rossum(const WtVanRossumArgs &a, cudaStream_t st);
@@ -200,6 +201,26 @@ int wt_lowrank_product(const WtLowRankProduct *a, void *stream) {
     if (!a->V || !a->P || !a->D || !a->err) return fail(WT_ERR_ARGS, "missing low-rank product buffers%s");
     if (((uintptr_t)a->V & 15) || ((uintptr_t)a->P & 15)) return fail(WT_ERR_ARGS, "V and P must be 16-byte aligned%s");
     return launch_status(wt::launch_lowrank_product(*a, (cudaStream_t)stream), "low-rank product");
+}
+
+int wt_lowrank_forward(const WtLowRankNet *net, const WtLowRankRun *run, void *stream) {
+    if (!net || !run) return fail(WT_ERR_ARGS, "net or run is null%s");
+    if (net->B <= 0 || net->N <= 0 || net->N >= (1 << 27)) return fail(WT_ERR_ARGS, "bad sizes%s");
+    if (net->S < 1 || net->S > 4) return fail(WT_ERR_UNSUPPORTED, "the factorised kernel carries 1..4 channels%s");
+    if (net->KP < 1 || net->KP > 2) return fail(WT_ERR_UNSUPPORTED, "the factorised kernel takes 1 or 2 pathways%s");
+    if (!net->theta || !net->U_reset || !net->E_L || !net->C_m || !net->beta || !net->U || !net->path_of ||
+        !net->V || !net->scale || !net->w_in)
+        return fail(WT_ERR_ARGS, "missing network tables%s");
+    if (((uintptr_t)net->U & 15) || ((uintptr_t)net->V & 15)) return fail(WT_ERR_ARGS, "U and V must be 16-byte aligned%s");
+    if (run->T < 0 || run->t0 < 0 || run->t0 + run->T > run->T_total) return fail(WT_ERR_ARGS, "steps out of range%s");
+    if (!run->v || !run->g || !run->spikes || !run->P || !run->barrier || !run->err || (run->T && !run->x) ||
+        (net->n_ref && !run->counter))
+        return fail(WT_ERR_ARGS, "missing run buffers%s");
+    if ((uintptr_t)run->P & 15) return fail(WT_ERR_ARGS, "P must be 16-byte aligned%s");
+    cudaStream_t st = (cudaStream_t)stream;
+    cudaError_t e = cudaMemsetAsync(run->barrier, 0, 64 * 4, st);
+    if (e != cudaSuccess) return launch_status(e, "barrier reset");
+    return launch_status(wt::launch_lowrank_forward(*net, *run, st), "factorised forward");
 }
 
 }  // extern "C"

@@ -242,6 +242,12 @@ def simulate(
             "track_gradients retains the autograd graph of every step, which only the "
             "reference's PyTorch path builds; the fused kernels do not"
         )
+    from wiretorch_b200 import lowrank
+
+    if lowrank.is_factorised(drive):
+        return lowrank.simulate(v, g, x, drive, p, refractory=refractory, gating=gating,
+                                adaptation=adaptation, probabilities=probabilities, track=track,
+                                track_batch_idx=track_batch_idx, retain=retain)  # fmt: skip
     if not x.is_cuda:
         raise RuntimeError("wiretorch_b200 runs on CUDA tensors only (no CPU path)")
     B, T, n_in = x.shape

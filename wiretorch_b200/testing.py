@@ -81,3 +81,48 @@ def random_network(N=300, n_in=100, B=2, T=100, seed=0, dt=1.0, tau_ref=None, mg
     if adapt is not None:
         kw["adaptation"] = torch.zeros((B, N), device=device)
     return drive, p, torch.from_numpy(x).to(device), v, g, kw
+
+
+def lowrank_network(N=300, B=130, T=60, rank=32, seed=0, dt=0.5, double_exp=False, device="cpu"):
+    """A seeded factorised network: excitatory and inhibitory sources with recurrent
+    weights ``W = U V^T`` (non-negative factors, rank ``rank``), one Poisson input column
+    per neuron. Returns ``(drive_lowrank, drive_dense, p, x, v, g, kw)``: the same network
+    with ``LowRank`` weights and with the assembled dense ones."""
+    from wiretorch_b200.lowrank import LowRank
+    from wiretorch_b200.types import SparseRows
+
+    rng = np.random.default_rng(seed)
+    f = lambda a: torch.tensor(np.asarray(a, dtype=np.float32), device=device)  # noqa: E731
+    exc = rng.random(N) < 0.8
+    rows_e = torch.tensor(np.flatnonzero(exc), device=device)
+    rows_i = torch.tensor(np.flatnonzero(~exc), device=device)
+    V = f(np.abs(rng.normal(0, 1, (N, rank))) / np.sqrt(rank))
+    U = f(np.abs(rng.normal(0, 1, (N, rank))) / np.sqrt(rank) * (4.0 / N))
+    lr_e, lr_i = LowRank(U[rows_e], V), LowRank(U[rows_i] * 3.0, V)
+    ar = torch.arange(N + 1, device=device)
+    w_in = SparseRows(ar, ar[:-1].to(torch.int32), f(rng.uniform(8.0, 14.0, N)), N)
+    # synapse types: 0 excitatory, 1 inhibitory (single exponentials unless double_exp)
+    tau_rise = f([2.0, 0.0]) if double_exp else f([0.0, 0.0])
+    tau_decay = f([5.0, 10.0])
+    dtt = torch.tensor(dt, device=device)
+    decay_r = torch.where(tau_rise > 0, torch.exp(-dtt / tau_rise.clamp(min=1e-6)), torch.zeros_like(tau_rise))
+    decay = torch.stack([decay_r, torch.exp(-dtt / tau_decay)])
+    jump = torch.stack([-torch.ones(2, device=device), torch.ones(2, device=device)])
+    made = torch.tensor([[1, 0], [0, 1], [1, 0]], dtype=torch.bool, device=device)
+    scale = torch.ones(3, N, device=device)
+    drive_lr = Drive(made=made, scale=scale, recurrent=[(rows_e, lr_e), (rows_i, lr_i)],
+                     feedforward=[(torch.arange(N, device=device), w_in)])  # fmt: skip
+    drive_dense = Drive(made=made, scale=scale, recurrent=[(rows_e, lr_e.dense()), (rows_i, lr_i.dense())],
+                        feedforward=[(torch.arange(N, device=device), w_in)])  # fmt: skip
+    p = Physiology(
+        theta=f(np.full(N, -50.0)), U_reset=f(np.full(N, -65.0)), E_L=f(np.full(N, -70.0)),
+        C_m=f(np.full(N, 200.0)), beta=torch.exp(-dtt / 20.0) * torch.ones(N, device=device),
+        E_syn=f([0.0, -80.0]), g_clip=f([float("inf")] * 2), decay=decay, jump=jump, dt=dtt,
+        surr_scale=torch.tensor(10.0, device=device),
+    )  # fmt: skip
+    p.n_ref = torch.full((N,), int(round(2.0 / dt)), dtype=torch.int32, device=device)
+    x = (torch.from_numpy(rng.random((B, T, N))) < 40.0 * dt / 1000.0).float().to(device)
+    v = torch.full((B, N), -65.0, device=device) + f(rng.uniform(0, 14, (B, N)))
+    g = torch.zeros((B, 2, 2, N), device=device).permute(0, 3, 1, 2)
+    kw = {"refractory": torch.zeros((B, N), dtype=torch.int32, device=device)}
+    return drive_lr, drive_dense, p, x, v, g, kw
