@@ -50,7 +50,8 @@ def parse():
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
-    ap.add_argument("--config", default="c2", choices=["c2", "c1"])
+    ap.add_argument("--config", default="c2", choices=["c2", "c1", "c3"])
+    ap.add_argument("--chunk", type=int, default=250, help="c3: steps per engine call (the state carries over)")
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--batch", type=int, default=None, help="trials per GPU (default: the config's)")
     ap.add_argument("--no-e2e", action="store_true")
@@ -176,6 +177,10 @@ def build(args, rank, device):
     if args.config == "c2":
         cfg = configs.c2(B=args.batch or 64, T=500, seed=0, device=device)
         engine.POOL_SYNAPSES = True  # 41 synapse types with 2 distinct dynamics
+    elif args.config == "c3":
+        cfg = configs.c3(B=args.batch or 256, T=2000, seed=0, device=device)
+        cfg.extra["chunk"] = args.chunk
+        return cfg, cfg.inputs(T=args.chunk, seed=1 + rank)  # one chunk of input, reused
     else:
         cfg = configs.c1(B=args.batch or 8, T=1000, seed=0, device=device)
     x = cfg.inputs(seed=1 + rank)
@@ -187,6 +192,17 @@ def make_step(cfg, world, train: bool):
     from wiretorch_b200 import configs, engine, filtering
 
     v0, g0, kw0 = cfg.state()
+    if cfg.name == "c3":
+        def forward_chunks(x, target=None):
+            """The T steps as engine calls of x.shape[1] steps, the state carried over."""
+            v, g, kw = v0, g0, kw0
+            with torch.no_grad():
+                for _ in range(cfg.T // x.shape[1]):
+                    run = engine.simulate(v, g, x, cfg.drive, cfg.p, **kw)
+                    v, g, kw = run.v, run.syn, {"refractory": run.refractory}
+            return v.sum()
+
+        return forward_chunks, None
     if not train:
         def forward(x, target=None):
             with torch.no_grad():
@@ -239,6 +255,15 @@ def forward_bytes(cfg, plan, T, spikes_bits_saved: bool, fired_sources_edges: fl
     if spikes_bits_saved:
         per += 4 + 4 * S + 2 / 8
     return cfg.B * T * cfg.N * per + cfg.B * T * cfg.n_in * 4 + fired_sources_edges * 8
+
+
+def factorised_bytes(cfg, T):
+    """Algorithmic bytes of one factorised launch of T steps: per neuron-step the state
+    read and written (v 8, conductances 16 per channel, refractory counter 2), the spike
+    bit and the input read (4); per step the factors U and V (N x 64 bf16 each)."""
+    C = 2
+    per = 8 + 16 * C + 2 + 1 / 8 + 4
+    return cfg.B * T * cfg.N * per + T * 2 * cfg.N * 64 * 2
 
 
 def fired_edges_once(cfg, spikes, x):
@@ -337,7 +362,9 @@ def run_reference(args, rank, world):
 def config_of(args, cfg, world):
     c = {
         "workload": f"{cfg.name}: {cfg.N} neurons, {cfg.B} trials/GPU, {cfg.T} steps of 0.1 ms"
-                    + (", forward + BPTT + van Rossum rate loss + SGD" if args.config == "c2" else ", forward"),
+                    + (", forward + BPTT + van Rossum rate loss + SGD" if args.config == "c2" else ", forward")
+                    + (f", factorised W = U V^T rank {cfg.extra.get('rank')}, {args.chunk} steps per call"
+                       if args.config == "c3" else ""),
         "global_batch": cfg.B * world, "seq_len": cfg.T, "parallelism": f"trial-batch x{world}",
         "l2": "inputs larger than L2 (spike input and state streams exceed 126 MB per step)",
     }  # fmt: skip
@@ -365,15 +392,23 @@ def main():
     for _ in range(max(args.warmup, 3)):
         step(x, target)
     torch.cuda.synchronize()
-    plan = engine.get_plan(cfg.drive, cfg.p, cfg.B, cfg.n_in, device)
+    factorised = cfg.name == "c3"
+    plan = None if factorised else engine.get_plan(cfg.drive, cfg.p, cfg.B, cfg.n_in, device)
 
     # ---- synaptic events: counted on the device over one untimed step (the counter's
     # atomics stay out of the timed region) ----
     edges = torch.zeros(2, dtype=torch.int64, device=device)
-    engine.EDGE_COUNTER = edges
-    step(x, target)
-    torch.cuda.synchronize()
-    engine.EDGE_COUNTER = None
+    if factorised:  # every spike reaches every neuron through W = U V^T
+        with torch.no_grad():
+            v0_, g0_, kw0_ = cfg.state()
+            r0 = engine.simulate(v0_, g0_, x, cfg.drive, cfg.p, **kw0_)
+        per_chunk = float(r0.output.sum()) * cfg.N, float((x != 0).sum())
+        edges[0], edges[1] = int(per_chunk[0] * cfg.T / x.shape[1]), int(per_chunk[1] * cfg.T / x.shape[1])
+    else:
+        engine.EDGE_COUNTER = edges
+        step(x, target)
+        torch.cuda.synchronize()
+        engine.EDGE_COUNTER = None
 
     # ---- timed region: K steps, device time, max over ranks ----
     _lib.TIMER = {}
@@ -408,16 +443,22 @@ def main():
 
         v0, g0, kw0 = cfg.state()
         run = eng.simulate(v0, g0, x, cfg.drive, cfg.p, **kw0)
-        fired = fired_edges_once(cfg, run.output, x)
-    fwd_bytes = forward_bytes(cfg, plan, cfg.T, train, fired)
+    if factorised:
+        kname = "wt_lowrank_forward"
+        fwd_bytes = factorised_bytes(cfg, x.shape[1])
+        kdesc = "wt_lowrank_forward (persistent factorised step kernel, tcgen05 product per step)"
+    else:
+        kname = "wt_forward"
+        fwd_bytes = forward_bytes(cfg, plan, cfg.T, train, fired_edges_once(cfg, run.output, x))
+        kdesc = "wt_forward (persistent forward step kernel)"
     peak, peak_kind = measured_peak()
-    fwd_s = kernel_ms["wt_forward"] / 1000.0
+    fwd_s = kernel_ms[kname] / 1000.0
     roofline = {
-        "kernel": "wt_forward (persistent forward step kernel)",
+        "kernel": kdesc,
         "bound": "hbm", "achieved": fwd_bytes / fwd_s / 1e9, "peak": peak, "unit": "GB/s",
         "frac": fwd_bytes / fwd_s / 1e9 / peak, "peak_kind": peak_kind,
         "traffic": None, "algorithmic_bytes_per_launch": fwd_bytes,
-        "launch_ms": kernel_ms["wt_forward"],
+        "launch_ms": kernel_ms[kname],
     }  # fmt: skip
     prof = ROOT / "profiles" / f"traffic_{args.config}.json"
     if prof.exists():
@@ -461,7 +502,7 @@ def main():
                "ms_per_step": e2e_el / K * 1000.0}  # fmt: skip
 
     cpu = None
-    if rank == 0 and world == 1 and not args.no_cpu:
+    if rank == 0 and world == 1 and not args.no_cpu and not factorised:
         rate, cores, sample = cpu_baseline(cfg)
         cpu = {"value": rate, "unit": "neuron-steps/s", "cores": cores, "kind": "port", "sample": sample}
 

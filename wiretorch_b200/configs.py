@@ -224,3 +224,36 @@ def synaptic_events(cfg: Config, spikes: torch.Tensor, x: torch.Tensor | None = 
     if x is not None:
         inp = int(((x != 0).double().sum((0, 1)) * deg[cfg.N :]).sum())
     return rec, inp
+
+
+def c3(B=256, T=2000, seed=0, device="cuda", rank=64, w_in=15.0, g_L=10.0):
+    """Factorised-weight network: N=50,000 conductance-LIF neurons, recurrent weights
+    W = U V^T of rank 64 with U and V ~ N(0, 1/sqrt(N)) in bf16, a sign mask per
+    presynaptic neuron (80% excitatory: their row of W drives the excitatory synapse
+    type, the rest the inhibitory one), batch 256, dt=0.1 ms, T=2,000, one 10 Hz Poisson
+    input per neuron; forward only. Physiology as ``c1`` (g_L = 10 nS, input weight
+    15 nS). The factors as specified give weights of order 8 / N nS, so the recurrent
+    drive is weak next to the input."""
+    from wiretorch_b200.lowrank import LowRank
+
+    dev = torch.device(device)
+    gen = torch.Generator(device=dev).manual_seed(seed)
+    N = 50000
+    sd = 1.0 / math.sqrt(N)
+    U = (torch.randn(N, rank, generator=gen, device=dev) * sd).to(torch.bfloat16)
+    V = (torch.randn(N, rank, generator=gen, device=dev) * sd).to(torch.bfloat16)
+    exc = torch.rand(N, generator=gen, device=dev) < 0.8
+    rows_e, rows_i = torch.nonzero(exc).flatten(), torch.nonzero(~exc).flatten()
+    ar = torch.arange(N, device=dev)
+    W_in = SparseRows(torch.arange(N + 1, device=dev), ar.to(torch.int32), torch.full((N,), w_in, device=dev), N)
+    S_params = [(0.0, 5.0, 0.0, 1.0), (0.0, 10.0, -80.0, 1.0)]
+    made = torch.tensor([[1, 0], [0, 1], [1, 0]], dtype=torch.bool, device=dev)
+    drive = Drive(made=made, scale=torch.ones(3, N, device=dev),
+                  recurrent=[(rows_e, LowRank(U[rows_e], V)), (rows_i, LowRank(U[rows_i], V))],
+                  feedforward=[(ar, W_in)])  # fmt: skip
+    p = _physiology(N, None, 0.1, S_params, dev, g_L=g_L)
+    types = (~exc).to(torch.int64)
+    out_deg = torch.cat([torch.full((N,), N, dtype=torch.int64, device=dev), torch.ones(N, dtype=torch.int64, device=dev)])
+    cfg = Config("c3", drive, p, B, T, N, N, torch.full((N,), 10.0, device=dev), types, 2, out_deg)
+    cfg.extra["rank"] = rank
+    return cfg
