@@ -257,7 +257,38 @@ __global__ void __launch_bounds__(kLfWarps * 32, 1) lowrank_forward_kernel(const
                             tmem_ld8(tmem + ((uint32_t)(q * 32) << 16) + k * kLrTile + cb * 32 + j0, A[k]);
                     }
 #pragma unroll
-                    for (int j = 0; j < 8; j++) {
+                    for (int jb = 0; jb < 8; jb += 4) {
+                    // 4 items' state and input, loaded together (their loads overlap)
+                    float v8[4], x8[4], gr8[4][S], gd8[4][S];
+                    int cnt8[4];
+#pragma unroll
+                    for (int jj = 0; jj < 4; jj++) {
+                        const int j = jb + jj;
+                        const int b = b0 + cb * 32 + j0 + j;
+                        const bool valid = nvalid && b < B;
+                        const size_t o = (size_t)b * N + n;
+                        const float *g_b = run.g + (size_t)b * 2 * S * N + n;
+                        v8[jj] = 0.0f;
+                        x8[jj] = 0.0f;
+                        cnt8[jj] = 0;
+#pragma unroll
+                        for (int c = 0; c < S; c++) gr8[jj][c] = gd8[jj][c] = 0.0f;
+                        if (valid) {
+#pragma unroll
+                            for (int c = 0; c < S; c++) {
+                                gd8[jj][c] = g_b[(size_t)(S + c) * N];
+                                if (net.decay_r[c] != 0.0f || t == 0) gr8[jj][c] = g_b[(size_t)c * N];
+                            }
+                            if (has_x) x8[jj] = run.x[(size_t)b * TN + (size_t)(t_abs - 1) * N + n];
+                            if (!finish) {
+                                v8[jj] = run.v[o];
+                                if (REF) cnt8[jj] = run.counter[o];
+                            }
+                        }
+                    }
+#pragma unroll
+                    for (int jj = 0; jj < 4; jj++) {
+                        const int j = jb + jj;
                         const int b = b0 + cb * 32 + j0 + j;
                         const bool valid = nvalid && b < B;
                         float s = 0.0f;
@@ -267,11 +298,11 @@ __global__ void __launch_bounds__(kLfWarps * 32, 1) lowrank_forward_kernel(const
                             float gr[S], gd[S];
 #pragma unroll
                             for (int c = 0; c < S; c++) {
-                                gd[c] = g_b[(size_t)(S + c) * N];
-                                gr[c] = (net.decay_r[c] != 0.0f || t == 0) ? g_b[(size_t)c * N] : 0.0f;
+                                gd[c] = gd8[jj][c];
+                                gr[c] = gr8[jj][c];
                             }
                             if (has_x) {
-                                const float xin = w_in * sc[KP] * run.x[(size_t)b * TN + (size_t)(t_abs - 1) * N + n];
+                                const float xin = w_in * sc[KP] * x8[jj];
 #pragma unroll
                                 for (int c = 0; c < S; c++) {
                                     float X = 0.0f;
@@ -290,8 +321,8 @@ __global__ void __launch_bounds__(kLfWarps * 32, 1) lowrank_forward_kernel(const
                                     g_b[(size_t)(S + c) * N] = gd[c];
                                 }
                             } else {
-                                const float v = run.v[o];
-                                int cnt = REF ? run.counter[o] : 0;
+                                const float v = v8[jj];
+                                int cnt = cnt8[jj];
                                 const float held = (REF && cnt > 0) ? 1.0f : 0.0f;
                                 s = (v - theta) > 0.0f ? 1.0f : 0.0f;
                                 if (REF) s = s * (1.0f - held);
@@ -337,6 +368,7 @@ __global__ void __launch_bounds__(kLfWarps * 32, 1) lowrank_forward_kernel(const
                             const float2 f2 = __bfloat1622float2(u2);
                             atomicAdd(reinterpret_cast<float2 *>(Pcur + ((size_t)b * KP + kl) * kLrK) + lane, f2);
                         }
+                    }
                     }
                 }
             }
