@@ -463,9 +463,10 @@ def main():
     prof = ROOT / "profiles" / f"traffic_{args.config}.json"
     if prof.exists():
         info = json.loads(prof.read_text())
-        per_ns = info.get("dram_bytes_per_neuron_step", {}).get(dominant if dominant in info.get("dram_bytes_per_neuron_step", {}) else "wt_forward")
-        if per_ns:
-            roofline["traffic"] = per_ns * cfg.B * cfg.N * cfg.T
+        per_ns = info.get("dram_bytes_per_neuron_step", {}).get(kname)
+        if per_ns:  # measured DRAM bytes per neuron-step, scaled to this launch
+            steps_per_launch = x.shape[1] if factorised else cfg.T
+            roofline["traffic"] = per_ns * cfg.B * cfg.N * steps_per_launch
             roofline["traffic_source"] = str(prof.relative_to(ROOT))
 
     # ---- end to end from host buffers ----
