@@ -1,0 +1,51 @@
+"""Short, representative launches of the engine's kernels for profiling (ncu captures).
+
+``python -m wiretorch_b200.profile_cases c2-active``: C2 (64 trials, pooled channels) run
+450 steps from rest, then one 20-step call from that state with saving for the backward
+pass, as in training. ``python -m wiretorch_b200.profile_cases c3-small``: C3 with 128
+trials, 200 steps, then one 10-step call from that state. In both the second launch is
+the one to capture (``-s 1 -c 1``).
+"""
+
+from __future__ import annotations
+
+import sys
+
+import torch
+
+
+def c2_active():
+    from wiretorch_b200 import configs, engine
+
+    cfg = configs.c2(B=64, T=500, device="cuda")
+    engine.POOL_SYNAPSES = True
+    x = cfg.inputs(seed=1)
+    v, g, kw = cfg.state()
+    with torch.no_grad():
+        run = engine.simulate(v, g, x[:, :450], cfg.drive, cfg.p, **kw)
+    log_sf = torch.zeros(cfg.extra["log_sf_shape"], device="cuda", requires_grad=True)
+    cfg.drive.scale = configs.scale_from_log_sf(cfg, log_sf)
+    run2 = engine.simulate(run.v, run.syn, x[:, 450:470].contiguous(), cfg.drive, cfg.p,
+                           refractory=run.refractory)  # fmt: skip
+    torch.cuda.synchronize()
+    print(f"c2-active: {float(run2.output.sum()) / 20:.0f} spikes per step")
+
+
+def c3_small():
+    from wiretorch_b200 import configs, engine
+
+    cfg = configs.c3(B=128, T=200, device="cuda")
+    x = cfg.inputs(T=200, seed=1)
+    v, g, kw = cfg.state()
+    with torch.no_grad():
+        run = engine.simulate(v, g, x, cfg.drive, cfg.p, **kw)
+        run2 = engine.simulate(run.v, run.syn, x[:, :10].contiguous(), cfg.drive, cfg.p,
+                               refractory=run.refractory)  # fmt: skip
+    torch.cuda.synchronize()
+    print(f"c3-small: {float(run2.output.sum()):.0f} spikes in 10 steps")
+
+
+CASES = {"c2-active": c2_active, "c3-small": c3_small}
+
+if __name__ == "__main__":
+    CASES[sys.argv[1]]()
