@@ -193,6 +193,15 @@ typedef struct {
     float *Q;
     float *g_theta, *g_reset, *g_E_L, *g_C_m, *g_beta, *g_E_syn, *g_decay, *g_jump;
     float *g_adapt, *g_adapt_decay, *g_E_adapt;
+    /* Steps t_hi - 1 down to t_lo (t_hi 0: T). With `adj` (B, 2 + 4 S, N) — dL/dv, the
+     * adaptation's adjoint, dL/dg rise and decay per channel, the decays' H — the scan
+     * starts from that state, leaves its end state there and adds to the physiology
+     * outputs instead of writing them (one chunk of a scan taken step by step); without,
+     * it starts from zero. R (B, N), when given, is added to dL/d(spike) of the steps
+     * (the recurrent pathways' carry of a single step, wt_recurrent_carry). */
+    int32_t t_lo, t_hi;
+    float *adj;
+    const float *R;
 } WtBackward;
 
 /* Gradients carried along the connectome's edges, from the adjoints Q of a reverse scan:
@@ -225,6 +234,24 @@ int64_t wt_edge_grads_scratch_words(const WtNet *net, int32_t T);
 /* The reverse scan. Replaces `scan_backward` (conductance/kernels.py:382-568, driven by
  * conductance/engine.py:358-383 `_backward`). */
 int wt_backward(const WtNet *net, const WtBackward *bwd, void *stream);
+
+/* Gradients through the recurrent spikes (Drive.recurrent_gradients): what step t's
+ * input adjoints pass back to the spikes of that step's recurrent sources,
+ * R[b, j] = sum over j's edges e (pathway k, target n, channel c) of
+ * w_e scale[k, n] jf[k, c] Q[b, t, c, n] (a gated pathway's edges times that step's
+ * factors), Q of step t formed from the adjoint state `adj` entering the step (the
+ * layout of WtBackward.adj). Qt (C, N, B) is scratch. Replaces `carry_to_sources` with
+ * `presynaptic` (network_simulators/engine.py:257-306), driven per step by
+ * `_recurrent_backward` (conductance/engine.py:386-436). */
+typedef struct {
+    int32_t T, t;
+    const float *adj;
+    const float *f_saved;  /* (B, T, R_f) when the net is gated */
+    float *Qt;
+    float *R;
+} WtRecurrentCarry;
+
+int wt_recurrent_carry(const WtNet *net, const WtRecurrentCarry *rc, void *stream);
 
 /* The edge gradients. Replaces the scale partials of `scan_backward`, the weight
  * gradient `weight_gradient` (network_simulators/engine.py:327-350) and the input

@@ -47,7 +47,8 @@ def test_structures_match_the_header_sizes():
                         ("WtVanRossumArgs", filtering._VanRossumArgs),
                         ("WtVanRossumGradArgs", filtering._VanRossumGradArgs),
                         ("WtLowRankProduct", lowrank._ProductArgs),
-                        ("WtLowRankNet", lowrank._LrNet), ("WtLowRankRun", lowrank._LrRun)):  # fmt: skip
+                        ("WtLowRankNet", lowrank._LrNet), ("WtLowRankRun", lowrank._LrRun),
+                        ("WtRecurrentCarry", autograd._CarryArgs)):  # fmt: skip
         body = re.search(r"typedef struct \{((?:(?!typedef struct).)*?)\}\s*" + struct + ";", text,
                          re.S).group(1)
         body = re.sub(r"/\*.*?\*/", "", body, flags=re.S)

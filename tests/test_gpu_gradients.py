@@ -21,7 +21,7 @@ from wiretorch_b200.types import PHYSIOLOGY
 pytestmark = pytest.mark.gpu
 
 TOL = 1e-3
-CASES = [c for c in golden_io.cases() if c != "recurrent_gradients"]
+CASES = golden_io.cases()
 
 
 def readout(seed, shape):
@@ -33,8 +33,10 @@ def _leaf(t):
     return t.detach().clone().requires_grad_(True)
 
 
-def engine_gradients(name):
+def engine_gradients(name, recurrent=None):
     drive, p, d, meta = golden_io.load(name, "cuda")
+    if recurrent is not None:
+        drive.recurrent_gradients = recurrent
     T = meta["grad_steps"]
     x = _leaf(torch.from_numpy(d["in.x"][:, :T]).cuda())
     drive.scale = _leaf(drive.scale)
@@ -91,3 +93,17 @@ def test_gradients_match_reference(name):
             got, expected = got[masks[key]], expected[masks[key]]
         scale = max(float(np.abs(expected).max()), 1e-12)
         np.testing.assert_allclose(got, expected, rtol=0, atol=TOL * scale, err_msg=key)
+
+
+def test_recurrent_carry_matters():
+    """The recurrent case's gradients without the carry along the recurrent edges miss
+    the reference's by far more than the tolerance: the carry is what makes them match."""
+    _, _, grads, d, masks = engine_gradients("recurrent_gradients", recurrent=False)
+    worst = 0.0
+    for key, got in grads.items():
+        if got is None or key.startswith("W."):
+            continue
+        expected = d[f"grad.{key}"]
+        scale = max(float(np.abs(expected).max()), 1e-12)
+        worst = max(worst, float(np.abs(got.detach().cpu().numpy() - expected).max()) / scale)
+    assert worst > 10 * TOL

@@ -12,10 +12,12 @@ backward pass is:
    ``(K, N)``, the weights (on their non-zero entries) and the input.
 
 Gradients flow through the voltages and conductances and, via the fast-sigmoid
-surrogate, into the spikes; never through the reset; and not through the recurrent
-spikes into their presynaptic neurons (``Drive.recurrent_gradients`` False, the
-reference's default for conductance-based networks: the recurrent input is then input
-like any other). The gradient of a dense weight matrix is computed on its non-zero
+surrogate, into the spikes; never through the reset. By default (``Drive.recurrent_gradients``
+False, the reference's default for conductance-based networks) not through the recurrent
+spikes into their presynaptic neurons: the recurrent input is then input like any other.
+With ``recurrent_gradients`` the scan is taken one step at a time: each step's input
+adjoints are carried back along the recurrent edges to that step's source spikes
+(``wt_recurrent_carry``) before the step's membrane adjoint. The gradient of a dense weight matrix is computed on its non-zero
 entries: every parametrisation of the reference multiplies its weights by their mask
 or connectome, so the entries that are zero carry no gradient to any parameter.
 """
@@ -39,6 +41,14 @@ class _BackwardArgs(_lib.C.Structure):
         ("g_theta", _lib.P), ("g_reset", _lib.P), ("g_E_L", _lib.P), ("g_C_m", _lib.P),
         ("g_beta", _lib.P), ("g_E_syn", _lib.P), ("g_decay", _lib.P), ("g_jump", _lib.P),
         ("g_adapt", _lib.P), ("g_adapt_decay", _lib.P), ("g_E_adapt", _lib.P),
+        ("t_lo", _lib.C.c_int32), ("t_hi", _lib.C.c_int32), ("adj", _lib.P), ("R", _lib.P),
+    ]  # fmt: skip
+
+
+class _CarryArgs(_lib.C.Structure):
+    _fields_ = [
+        ("T", _lib.C.c_int32), ("t", _lib.C.c_int32), ("adj", _lib.P), ("f_saved", _lib.P),
+        ("Qt", _lib.P), ("R", _lib.P),
     ]  # fmt: skip
 
 
@@ -143,13 +153,17 @@ class _Simulate(torch.autograd.Function):
                                             "g_E_syn", "g_decay", "g_jump", "g_adapt",
                                             "g_adapt_decay", "g_E_adapt")):  # fmt: skip
             if wants & WANT_BITS[name]:
-                partial[name] = torch.empty(shapes.get(name, (B, N)), device=device)
+                alloc = torch.zeros if cx.recurrent else torch.empty  # added to step by step
+                partial[name] = alloc(shapes.get(name, (B, N)), device=device)
                 setattr(bw, field, partial[name].data_ptr())
         stream = _lib.C.c_void_p(_lib.stream_of(device))
-        with _lib.timed("wt_backward"):
-            rc = _lib.lib().wt_backward(_lib.C.byref(net), _lib.C.byref(bw), stream)
-        _lib.check(rc, "wt_backward")
-        _lib.count_launches(1)
+        if cx.recurrent:
+            _recurrent_scan(plan, net, bw, save, T, stream)
+        else:
+            with _lib.timed("wt_backward"):
+                rc = _lib.lib().wt_backward(_lib.C.byref(net), _lib.C.byref(bw), stream)
+            _lib.check(rc, "wt_backward")
+            _lib.count_launches(1)
 
         n_weights = ctx.n_weights
         need_scale = ctx.needs_input_grad[1]
@@ -240,18 +254,38 @@ def _dense_weight_grads(plan, drive, weights, g_w, needs):
     return out
 
 
+def _recurrent_scan(plan, net, bw, save, T, stream):
+    """The reverse scan when gradients flow through the recurrent spikes: one step at a
+    time, each step's input adjoints carried back along the recurrent edges to that
+    step's source spikes (``wt_recurrent_carry``) before the step's membrane adjoint
+    (``wt_backward`` over that step, its adjoint state kept between the steps)."""
+    B, N, C, Sp = plan.B, plan.N, plan.ch.C, plan.ch.Sp
+    device = plan.device
+    adj = torch.zeros((B, 2 + 4 * Sp, N), device=device)
+    Qt = torch.empty((C, N, B), device=device)
+    R = torch.empty((B, N), device=device)
+    rc = _CarryArgs()
+    rc.T, rc.adj, rc.Qt, rc.R = T, adj.data_ptr(), Qt.data_ptr(), R.data_ptr()
+    rc.f_saved = _lib.ptr(save.get("f"))
+    bw.adj, bw.R = adj.data_ptr(), R.data_ptr()
+    lib = _lib.lib()
+    with _lib.timed("wt_backward"):
+        for t in reversed(range(T)):
+            rc.t = t
+            _lib.check(lib.wt_recurrent_carry(_lib.C.byref(net), _lib.C.byref(rc), stream), "wt_recurrent_carry")
+            bw.t_lo, bw.t_hi = t, t + 1
+            _lib.check(lib.wt_backward(_lib.C.byref(net), _lib.C.byref(bw), stream), "wt_backward")
+    _lib.count_launches(3 * T)
+
+
 def simulate_with_grad(plan, v, g, x, drive, p, refractory, gating, adaptation,
                        probabilities, track, track_batch_idx):  # fmt: skip
     """``engine.simulate`` when gradients are wanted."""
-    if drive.recurrent_gradients and drive.recurrent:
-        from wiretorch_b200 import recurrent_grad
-
-        return recurrent_grad.simulate(plan, v, g, x, drive, p, refractory, gating, adaptation,
-                                       probabilities, track, track_batch_idx)  # fmt: skip
     _plan.segments(plan)
     state = engine._prepare_state(plan, v, g, refractory, gating, adaptation, p)
     track_b = -1 if track_batch_idx is None else int(track_batch_idx)
     cx = Context(plan, p, drive, state, probabilities, track, track_b)
+    cx.recurrent = bool(drive.recurrent_gradients and drive.recurrent)
     weights, _ = _unique_weights(drive)
     phys = [getattr(p, n) if getattr(p, n) is not None else torch.zeros(0) for n in PHYSIOLOGY]
     spikes, prob = _Simulate.apply(cx, drive.scale, x, len(weights), *weights, *phys)

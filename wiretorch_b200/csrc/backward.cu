@@ -82,16 +82,34 @@ __global__ void __launch_bounds__(kBlock, (PHYS || S > 2) ? 1 : 3) backward_kern
 #pragma unroll
         for (int c = 0; c < S; c++) in.G[c] = __ldg(G_b + ((size_t)t * S + c) * N);
     };
+    const int t_hi = bw.t_hi > 0 ? bw.t_hi : T, t_lo = bw.t_lo;
+    // a chunk of a scan taken in pieces: the adjoint state entering it
+    const int NA = 2 + 4 * S;
+    float *adj = bw.adj ? bw.adj + (size_t)b * NA * N + n : nullptr;
+    if (adj) {
+        dv = adj[0];
+        la = adj[(size_t)N];
+#pragma unroll
+        for (int c = 0; c < S; c++) {
+            lr[c] = adj[(size_t)(2 + c) * N];
+            ld[c] = adj[(size_t)(2 + S + c) * N];
+            if (SYN) {
+                H_r[c] = adj[(size_t)(2 + 2 * S + c) * N];
+                H_d[c] = adj[(size_t)(2 + 3 * S + c) * N];
+            }
+        }
+    }
+    const float R_b = bw.R ? bw.R[(size_t)b * N + n] : 0.0f;
     StepIn<S> q[kAhead];
 #pragma unroll
     for (int d = 0; d < kAhead; d++)
-        if (T - 1 - d >= 0) load(T - 1 - d, q[d]);
+        if (t_hi - 1 - d >= t_lo) load(t_hi - 1 - d, q[d]);
 
-    for (int t = T - 1; t >= 0; t--) {
+    for (int t = t_hi - 1; t >= t_lo; t--) {
         const StepIn<S> cur = q[0];
 #pragma unroll
         for (int d = 0; d + 1 < kAhead; d++) q[d] = q[d + 1];
-        if (t - kAhead >= 0) load(t - kAhead, q[kAhead - 1]);
+        if (t - kAhead >= t_lo) load(t - kAhead, q[kAhead - 1]);
         const float v = cur.v;
         const float s = (cur.sb >> (n & 31)) & 1u ? 1.0f : 0.0f;
         const float held = (REF && ((cur.hb >> (n & 31)) & 1u)) ? 1.0f : 0.0f;
@@ -186,7 +204,7 @@ __global__ void __launch_bounds__(kBlock, (PHYS || S > 2) ? 1 : 3) backward_kern
         }
         // The spike (surrogate) and probability of step t, both of v - theta.
         const float xv = v - theta;
-        const float gs = cur.gs;
+        const float gs = cur.gs + R_b;
         float g_x;
         if (SAMPLE) {
             const float p = sigmoid(k * xv);
@@ -209,27 +227,44 @@ __global__ void __launch_bounds__(kBlock, (PHYS || S > 2) ? 1 : 3) backward_kern
         }
     }
 
-    const size_t bn = (size_t)b * N + n;
-    if (wants & WT_W_THETA) bw.g_theta[bn] = acc_theta;
-    if (wants & WT_W_RESET) bw.g_reset[bn] = acc_reset;
-    if (wants & WT_W_E_L) bw.g_E_L[bn] = acc_E_L;
-    if (wants & WT_W_C_M) bw.g_C_m[bn] = acc_C_m;
-    if (wants & WT_W_BETA) bw.g_beta[bn] = acc_beta;
-    if (wants & WT_W_ADAPT) bw.g_adapt[bn] = acc_adapt;
-    if (wants & WT_W_ADAPT_DECAY) bw.g_adapt_decay[bn] = acc_adapt_decay;
-    if (wants & WT_W_E_ADAPT) bw.g_E_adapt[bn] = acc_E_a;
-    if (SYN) {
-        const float *gi = bw.g_init + (size_t)b * 2 * S * N + n;
+    if (adj) {  // the state leaving the chunk
+        adj[0] = dv;
+        adj[(size_t)N] = la;
 #pragma unroll
         for (int c = 0; c < S; c++) {
-            if (wants & WT_W_E_SYN) bw.g_E_syn[((size_t)b * S + c) * N + n] = acc_E[c];
+            adj[(size_t)(2 + c) * N] = lr[c];
+            adj[(size_t)(2 + S + c) * N] = ld[c];
+            if (SYN) {
+                adj[(size_t)(2 + 2 * S + c) * N] = H_r[c];
+                adj[(size_t)(2 + 3 * S + c) * N] = H_d[c];
+            }
+        }
+    }
+    // outputs: written, or added to when the scan is taken in chunks
+    auto put = [&](float *dst, float val) { *dst = adj ? *dst + val : val; };
+    const size_t bn = (size_t)b * N + n;
+    if (wants & WT_W_THETA) put(bw.g_theta + bn, acc_theta);
+    if (wants & WT_W_RESET) put(bw.g_reset + bn, acc_reset);
+    if (wants & WT_W_E_L) put(bw.g_E_L + bn, acc_E_L);
+    if (wants & WT_W_C_M) put(bw.g_C_m + bn, acc_C_m);
+    if (wants & WT_W_BETA) put(bw.g_beta + bn, acc_beta);
+    if (wants & WT_W_ADAPT) put(bw.g_adapt + bn, acc_adapt);
+    if (wants & WT_W_ADAPT_DECAY) put(bw.g_adapt_decay + bn, acc_adapt_decay);
+    if (wants & WT_W_E_ADAPT) put(bw.g_E_adapt + bn, acc_E_a);
+    if (SYN) {
+        const float *gi = bw.g_init + (size_t)b * 2 * S * N + n;
+        const bool first = t_lo == 0;  // the conductances entering the run: once, at its start
+#pragma unroll
+        for (int c = 0; c < S; c++) {
+            if (wants & WT_W_E_SYN) put(bw.g_E_syn + ((size_t)b * S + c) * N + n, acc_E[c]);
             if (wants & WT_W_JUMP) {
-                bw.g_jump[((size_t)b * 2 * S + c) * N + n] = acc_jr[c];
-                bw.g_jump[((size_t)b * 2 * S + S + c) * N + n] = acc_jd[c];
+                put(bw.g_jump + ((size_t)b * 2 * S + c) * N + n, acc_jr[c]);
+                put(bw.g_jump + ((size_t)b * 2 * S + S + c) * N + n, acc_jd[c]);
             }
             if (wants & WT_W_DECAY) {
-                bw.g_decay[((size_t)b * 2 * S + c) * N + n] = acc_dr[c] + gi[(size_t)c * N] * H_r[c];
-                bw.g_decay[((size_t)b * 2 * S + S + c) * N + n] = acc_dd[c] + gi[(size_t)(S + c) * N] * H_d[c];
+                put(bw.g_decay + ((size_t)b * 2 * S + c) * N + n, acc_dr[c] + (first ? gi[(size_t)c * N] * H_r[c] : 0.0f));
+                put(bw.g_decay + ((size_t)b * 2 * S + S + c) * N + n,
+                    acc_dd[c] + (first ? gi[(size_t)(S + c) * N] * H_d[c] : 0.0f));
             }
         }
     }

@@ -14,6 +14,7 @@ cudaError_t launch_edge_grads(const WtNet &net, const WtEdgeGrads &eg, cudaStrea
 long long edge_grads_fired_words(const WtNet &net, int T);
 cudaError_t launch_lowrank_product(const WtLowRankProduct &a, cudaStream_t st);
 cudaError_t launch_lowrank_forward(const WtLowRankNet &net, const WtLowRankRun &run, cudaStream_t st);
+cudaError_t launch_recurrent_carry(const WtNet &net, const WtRecurrentCarry &rc, cudaStream_t st);
 cudaError_t launch_filter(const WtFilterArgs &f, cudaStream_t st);
 cudaError_t launch_filter_grad(const WtFilterGradArgs &f, cudaStream_t st);
 cudaError_t launch_van_rossum(const WtVanRossumArgs &a, cudaStream_t st);
@@ -221,6 +222,16 @@ int wt_lowrank_forward(const WtLowRankNet *net, const WtLowRankRun *run, void *s
     cudaError_t e = cudaMemsetAsync(run->barrier, 0, 64 * 4, st);
     if (e != cudaSuccess) return launch_status(e, "barrier reset");
     return launch_status(wt::launch_lowrank_forward(*net, *run, st), "factorised forward");
+}
+
+int wt_recurrent_carry(const WtNet *net, const WtRecurrentCarry *rc, void *stream) {
+    int r = check_net(net);
+    if (r) return r;
+    if (!rc || rc->t < 0 || rc->t >= rc->T || !rc->adj || !rc->Qt || !rc->R)
+        return fail(WT_ERR_ARGS, "bad recurrent-carry arguments%s");
+    if (net->n_chunks && !net->edge_cw) return fail(WT_ERR_ARGS, "missing folded edges%s");
+    if (net->slot_gate && !rc->f_saved) return fail(WT_ERR_ARGS, "missing gating factors%s");
+    return launch_status(wt::launch_recurrent_carry(*net, *rc, (cudaStream_t)stream), "recurrent carry");
 }
 
 }  // extern "C"

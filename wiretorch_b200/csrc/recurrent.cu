@@ -1,0 +1,105 @@
+// Gradients through the recurrent spikes (Drive.recurrent_gradients; the reference's
+// _recurrent_backward, conductance/engine.py:386-436, with carry_to_sources and
+// presynaptic, network_simulators/engine.py:257-306). Taken one reverse step t at a
+// time, between two chunks of the reverse scan (wt_backward with t_lo = t, t_hi = t + 1):
+//
+//   1. q_kernel: each (trial, neuron)'s input adjoint of step t,
+//      Q[b, c, n] = sum over channels j fed by c of jump_r[j] l_r[j] + jump_d[j] l_d[j],
+//      from the adjoint state entering the step, written transposed (C, N, B) through a
+//      shared-memory tile so that the next kernel reads it trials-fastest;
+//   2. carry_kernel: one warp per recurrent source j, lanes over trials: for every edge
+//      e of j (pathway k, target n, channel c), with the edge's folded weight
+//      w_e scale[k, n] jf[k, c] (its fixed-point word over 2^s_c),
+//      R[b, j] = sum_e coef_e Q[b, c, n]  (a gated slot's sum times its factor at t),
+//      each edge's 32 or 64 trials one coalesced read of the L2-resident Q.
+#include "common.cuh"
+
+namespace wt {
+namespace {
+
+constexpr int kTile = 32;
+
+__global__ void __launch_bounds__(256) q_kernel(const WtNet net, const WtRecurrentCarry rc) {
+    __shared__ float tile[WT_MAX_CHANNELS][kTile][kTile + 1];
+    const int N = net.N, B = net.B, S = net.S, C = net.C;
+    const int NA = 2 + 4 * S;
+    const int n0 = blockIdx.x * kTile, b0 = blockIdx.y * kTile;
+    const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;  // 32 x 8
+    for (int i = ty; i < kTile; i += 8) {
+        const int b = b0 + i, n = n0 + tx;
+        float q[WT_MAX_CHANNELS];
+        for (int c = 0; c < C; c++) q[c] = 0.0f;
+        if (b < B && n < N) {
+            const float *a = rc.adj + (size_t)b * NA * N + n;
+            for (int j = 0; j < S; j++) {
+                const int c = net.input_of[j];
+                if (c < 0) continue;
+                q[c] = q[c] + (net.jump_r[j] * a[(size_t)(2 + j) * N] + net.jump_d[j] * a[(size_t)(2 + S + j) * N]);
+            }
+        }
+        for (int c = 0; c < C; c++) tile[c][i][tx] = q[c];
+    }
+    __syncthreads();
+    for (int i = ty; i < kTile; i += 8) {
+        const int n = n0 + i, b = b0 + tx;
+        if (n < N && b < B)
+            for (int c = 0; c < C; c++) rc.Qt[((size_t)c * N + n) * B + b] = tile[c][tx][i];
+    }
+}
+
+__global__ void __launch_bounds__(256) carry_kernel(const WtNet net, const WtRecurrentCarry rc) {
+    const int lane = threadIdx.x & 31;
+    const int j = blockIdx.x * 8 + (threadIdx.x >> 5);
+    const int N = net.N, B = net.B;
+    if (j >= N) return;  // whole warps
+    const int slot0 = net.src_slot[j], slot1 = net.src_slot[j + 1];
+    for (int bb = 0; bb < B; bb += 64) {
+        const int b_a = bb + lane, b_b = bb + 32 + lane;
+        const bool ok_a = b_a < B, ok_b = b_b < B;
+        float acc_a = 0.0f, acc_b = 0.0f;
+        for (int slot = slot0; slot < slot1; slot++) {
+            float sub_a = 0.0f, sub_b = 0.0f;
+            for (int ch = net.slot_chunk[slot]; ch < net.slot_chunk[slot + 1]; ch++) {
+                const long long d = net.chunk_desc[ch];
+                const long long e0 = d & ((1LL << 56) - 1);
+                const int len = (int)((unsigned long long)d >> 56);
+                for (int q0 = 0; q0 < len; q0 += 32) {
+                    const unsigned long long cw = q0 + lane < len ? __ldg(net.edge_cw + e0 + q0 + lane) : 0ull;
+                    const int m = min(32, len - q0);
+                    for (int i = 0; i < m; i++) {
+                        const unsigned lo = __shfl_sync(kFull, (unsigned)cw, i);
+                        const unsigned hi = __shfl_sync(kFull, (unsigned)(cw >> 32), i);
+                        const int c = (int)(lo >> 27), n = (int)(lo & 0x7ffffffu);
+                        const float coef = __uint_as_float(hi) * net.fx_inv[c];
+                        const float *qrow = rc.Qt + ((size_t)c * N + n) * B;
+                        if (ok_a) sub_a += coef * __ldcg(qrow + b_a);
+                        if (ok_b) sub_b += coef * __ldcg(qrow + b_b);
+                    }
+                }
+            }
+            if (net.slot_gate && rc.f_saved) {  // a gated slot: this step's factor per trial
+                const int gate = net.slot_gate[slot];
+                if (gate >= 0) {
+                    const int col = net.gate_cols[4 * gate + 3] + net.slot_row[slot];
+                    if (ok_a) sub_a *= rc.f_saved[((size_t)b_a * rc.T + rc.t) * net.R_f + col];
+                    if (ok_b) sub_b *= rc.f_saved[((size_t)b_b * rc.T + rc.t) * net.R_f + col];
+                }
+            }
+            acc_a += sub_a;
+            acc_b += sub_b;
+        }
+        if (ok_a) rc.R[(size_t)b_a * N + j] = acc_a;
+        if (ok_b) rc.R[(size_t)b_b * N + j] = acc_b;
+    }
+}
+
+}  // namespace
+
+cudaError_t launch_recurrent_carry(const WtNet &net, const WtRecurrentCarry &rc, cudaStream_t st) {
+    const dim3 qgrid((net.N + kTile - 1) / kTile, (net.B + kTile - 1) / kTile);
+    q_kernel<<<qgrid, 256, 0, st>>>(net, rc);
+    carry_kernel<<<(net.N + 7) / 8, 256, 0, st>>>(net, rc);
+    return cudaGetLastError();
+}
+
+}  // namespace wt
