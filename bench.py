@@ -10,7 +10,7 @@ LIF neurons in 40 cell types, learnt per-type-pair scales, batch 64 per GPU, T=5
 of 0.1 ms, Poisson input. One step is one training step: the forward simulation through
 the engine (``wiretorch_b200.engine.simulate``), the van Rossum rate loss (20 ms-filtered
 output against filtered target rates), backpropagation through time to the 41x40 scales,
-the gradients' all-reduce across ranks and an SGD update. Every rank simulates its own 64
+the gradients' all-reduce across ranks and an SGD update (gradient norm clipped at 1). Every rank simulates its own 64
 trials (trial-batch sharding, weak scaling). Inputs are larger than L2.
 
 ``value``: neuron-steps per second of the whole job (trials x neurons x time steps of all
@@ -50,8 +50,11 @@ def parse():
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
-    ap.add_argument("--config", default="c2", choices=["c2", "c1", "c3"])
-    ap.add_argument("--chunk", type=int, default=250, help="c3: steps per engine call (the state carries over)")
+    ap.add_argument("--config", default="c2", choices=["c2", "c1", "c3", "c4"])
+    ap.add_argument("--chunk", type=int, default=None,
+                    help="c3 / c4: steps per engine call, the state carried over (default 250 / 1000)")
+    ap.add_argument("--recurrent-gradients", action="store_true",
+                    help="c2: gradients through the recurrent spikes (Drive.recurrent_gradients)")
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--batch", type=int, default=None, help="trials per GPU (default: the config's)")
     ap.add_argument("--no-e2e", action="store_true")
@@ -177,8 +180,14 @@ def build(args, rank, device):
     if args.config == "c2":
         cfg = configs.c2(B=args.batch or 64, T=500, seed=0, device=device)
         engine.POOL_SYNAPSES = True  # 41 synapse types with 2 distinct dynamics
-    elif args.config == "c3":
-        cfg = configs.c3(B=args.batch or 256, T=2000, seed=0, device=device)
+        cfg.drive.recurrent_gradients = args.recurrent_gradients
+    elif args.config in ("c3", "c4"):
+        if args.config == "c3":
+            cfg = configs.c3(B=args.batch or 256, T=2000, seed=0, device=device)
+        else:
+            cfg = configs.c4(B=args.batch or 32, T=10000, seed=0, device=device)
+            engine.POOL_SYNAPSES = True
+        args.chunk = args.chunk or (250 if args.config == "c3" else 1000)
         cfg.extra["chunk"] = args.chunk
         return cfg, cfg.inputs(T=args.chunk, seed=1 + rank)  # one chunk of input, reused
     else:
@@ -192,7 +201,7 @@ def make_step(cfg, world, train: bool):
     from wiretorch_b200 import configs, engine, filtering
 
     v0, g0, kw0 = cfg.state()
-    if cfg.name == "c3":
+    if cfg.name in ("c3", "c4"):
         def forward_chunks(x, target=None):
             """The T steps as engine calls of x.shape[1] steps, the state carried over."""
             v, g, kw = v0, g0, kw0
@@ -200,6 +209,8 @@ def make_step(cfg, world, train: bool):
                 for _ in range(cfg.T // x.shape[1]):
                     run = engine.simulate(v, g, x, cfg.drive, cfg.p, **kw)
                     v, g, kw = run.v, run.syn, {"refractory": run.refractory}
+                    if run.adaptation is not None:
+                        kw["adaptation"] = run.adaptation
             return v.sum()
 
         return forward_chunks, None
@@ -225,8 +236,9 @@ def make_step(cfg, world, train: bool):
             import torch.distributed as dist
 
             dist.all_reduce(log_sf.grad)
-        with torch.no_grad():
-            log_sf.sub_(lr * log_sf.grad)
+        with torch.no_grad():  # SGD with the gradient's norm clipped at 1 (no host read)
+            grad = log_sf.grad
+            log_sf.sub_(lr * grad * torch.clamp(1.0 / (grad.norm() + 1e-12), max=1.0))
         return loss
 
     return step, log_sf
@@ -363,8 +375,10 @@ def config_of(args, cfg, world):
     c = {
         "workload": f"{cfg.name}: {cfg.N} neurons, {cfg.B} trials/GPU, {cfg.T} steps of 0.1 ms"
                     + (", forward + BPTT + van Rossum rate loss + SGD" if args.config == "c2" else ", forward")
-                    + (f", factorised W = U V^T rank {cfg.extra.get('rank')}, {args.chunk} steps per call"
-                       if args.config == "c3" else ""),
+                    + (f", factorised W = U V^T rank {cfg.extra.get('rank')}" if args.config == "c3" else "")
+                    + (f", {cfg.extra.get('edges')} edges" if args.config == "c4" else "")
+                    + (f", {args.chunk} steps per call" if args.config in ("c3", "c4") else "")
+                    + (", gradients through the recurrent spikes" if getattr(args, "recurrent_gradients", False) else ""),
         "global_batch": cfg.B * world, "seq_len": cfg.T, "parallelism": f"trial-batch x{world}",
         "l2": "inputs larger than L2 (spike input and state streams exceed 126 MB per step)",
     }  # fmt: skip
@@ -449,7 +463,7 @@ def main():
         kdesc = "wt_lowrank_forward (persistent factorised step kernel, tcgen05 product per step)"
     else:
         kname = "wt_forward"
-        fwd_bytes = forward_bytes(cfg, plan, cfg.T, train, fired_edges_once(cfg, run.output, x))
+        fwd_bytes = forward_bytes(cfg, plan, x.shape[1], train, fired_edges_once(cfg, run.output, x))
         kdesc = "wt_forward (persistent forward step kernel)"
     peak, peak_kind = measured_peak()
     fwd_s = kernel_ms[kname] / 1000.0
@@ -465,7 +479,7 @@ def main():
         info = json.loads(prof.read_text())
         per_ns = info.get("dram_bytes_per_neuron_step", {}).get(kname)
         if per_ns:  # measured DRAM bytes per neuron-step, scaled to this launch
-            steps_per_launch = x.shape[1] if factorised else cfg.T
+            steps_per_launch = x.shape[1]
             roofline["traffic"] = per_ns * cfg.B * cfg.N * steps_per_launch
             roofline["traffic_source"] = str(prof.relative_to(ROOT))
 

@@ -257,3 +257,75 @@ def c3(B=256, T=2000, seed=0, device="cuda", rank=64, w_in=15.0, g_L=10.0):
     cfg = Config("c3", drive, p, B, T, N, N, torch.full((N,), 10.0, device=dev), types, 2, out_deg)
     cfg.extra["rank"] = rank
     return cfg
+
+
+def c4(B=32, T=10000, seed=0, device="cuda", N=139000, n_types=8000, mean_degree=360.0,
+       degree_sigma=1.2, g_unit=0.7, g_inh=3.0, w_in=20.0, adapt=0.5):  # fmt: skip
+    """Fly-scale synthetic connectome: N=139,000 neurons in 8,000 cell types (type sizes
+    multinomial), ~50M directed edges with log-normal out-degree (mean 360, sigma 1.2) and
+    targets drawn in proportion to a log-normal in-degree propensity (same law), integer
+    synapse counts geometric(p=0.2) clipped to 2,000, a transmitter sign per cell type
+    (60% excitatory, 35% inhibitory, 5% none: those make no synapses), conductance LIF
+    with spike-rate adaptation (excitatory neurons) and refractoriness, dt=0.1 ms,
+    T=10,000, batch 32, Poisson drive at 15 Hz to a random 5% of neurons; forward only.
+
+    Chosen here: a synapse's conductance is ``g_unit`` nS per count (``g_inh`` times that
+    for inhibitory sources) times a per-cell-type-pair scale ~ LogNormal(0, 0.5), folded
+    into the weights, so the network's two pathways are its excitatory and inhibitory
+    sources (the 8,000 types live in the weights, not in 8,000 pathways of (K, N) scales);
+    adaptation ``adapt`` nS per spike decaying with 200 ms, E_adapt -90 mV; the driven
+    neurons' input weight ``w_in`` nS. Physiology otherwise as ``c1``. At these values the
+    network fires at 5-10 Hz (the oracle at a tenth of the size: 13,900 neurons)."""
+    dev = torch.device(device)
+    gen = torch.Generator(device=dev).manual_seed(seed)
+    rng = np.random.default_rng(seed)
+    sizes = rng.multinomial(N, np.full(n_types, 1.0 / n_types))
+    types = torch.repeat_interleave(torch.arange(n_types, device=dev), torch.tensor(sizes, device=dev))
+    u = rng.random(n_types)
+    sign_t = torch.tensor(np.where(u < 0.60, 1, np.where(u < 0.95, -1, 0)), device=dev)
+    sign = sign_t[types]
+    mu = math.log(mean_degree) - degree_sigma**2 / 2
+    out_deg = torch.exp(mu + degree_sigma * torch.randn(N, generator=gen, device=dev)).round().long()
+    out_deg = torch.where(sign != 0, out_deg.clamp(max=N - 1), torch.zeros_like(out_deg))
+    propensity = torch.exp(degree_sigma * torch.randn(N, generator=gen, device=dev))
+    cdf = torch.cumsum(propensity.double(), 0)
+    cdf = cdf / cdf[-1]
+    src = torch.repeat_interleave(torch.arange(N, device=dev), out_deg)
+    dst = torch.searchsorted(cdf, torch.rand(src.numel(), generator=gen, device=dev, dtype=torch.float64))
+    dst = dst.clamp(max=N - 1)
+    key = torch.unique(src * N + dst)  # one edge per ordered pair, no self-connections
+    src, dst = key // N, key % N
+    keep = src != dst
+    src, dst = src[keep], dst[keep]
+    count = torch.clamp(torch.floor(torch.log(torch.rand(src.numel(), generator=gen, device=dev))
+                                    / math.log(0.8)) + 1, max=2000)  # fmt: skip
+    pair = torch.exp(0.5 * torch.randn(n_types * n_types // 64 + 1, generator=gen, device=dev))
+    pair_idx = (types[src] * n_types + types[dst]) % pair.numel()
+    w = count * g_unit * pair[pair_idx] * torch.where(sign[src] < 0, g_inh, 1.0)
+    exc = sign[src] > 0
+    rows_e = torch.nonzero(sign > 0).flatten()
+    rows_i = torch.nonzero(sign < 0).flatten()
+    # row index of each source within its pathway
+    pos = torch.full((N,), -1, dtype=torch.int64, device=dev)
+    pos[rows_e] = torch.arange(rows_e.numel(), device=dev)
+    pos[rows_i] = torch.arange(rows_i.numel(), device=dev)
+    W_e = _csr_from_edges(pos[src[exc]], dst[exc], w[exc], rows_e.numel(), N)
+    W_i = _csr_from_edges(pos[src[~exc]], dst[~exc], w[~exc], rows_i.numel(), N)
+    n_in = max(1, int(round(0.05 * N)))
+    driven = torch.randperm(N, generator=gen, device=dev)[:n_in]
+    W_in = _csr_from_edges(torch.arange(n_in, device=dev), driven, torch.full((n_in,), w_in, device=dev), n_in, N)
+    S_params = [(0.0, 5.0, 0.0, 1.0), (0.0, 10.0, -80.0, 1.0), (0.0, 5.0, 0.0, 1.0)]
+    made = torch.eye(3, dtype=torch.bool, device=dev)
+    drive = Drive(made=made, scale=torch.ones(3, N, device=dev),
+                  recurrent=[(rows_e, W_e), (rows_i, W_i)],
+                  feedforward=[(torch.arange(n_in, device=dev), W_in)])  # fmt: skip
+    p = _physiology(N, None, 0.1, S_params, dev)
+    p.adapt = torch.where(sign > 0, adapt, 0.0).float()
+    p.adapt_decay = torch.full((N,), math.exp(-0.1 / 200.0), device=dev)
+    p.E_adapt = torch.full((N,), -90.0, device=dev)
+    deg = torch.zeros(N + n_in, dtype=torch.int64, device=dev)
+    deg[:N] = torch.bincount(src, minlength=N)
+    deg[N:] = 1
+    cfg = Config("c4", drive, p, B, T, N, n_in, torch.full((n_in,), 15.0, device=dev), types, n_types, deg)
+    cfg.extra["edges"] = int(src.numel())
+    return cfg

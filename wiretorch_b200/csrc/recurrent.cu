@@ -66,14 +66,26 @@ __global__ void __launch_bounds__(256) carry_kernel(const WtNet net, const WtRec
                 for (int q0 = 0; q0 < len; q0 += 32) {
                     const unsigned long long cw = q0 + lane < len ? __ldg(net.edge_cw + e0 + q0 + lane) : 0ull;
                     const int m = min(32, len - q0);
-                    for (int i = 0; i < m; i++) {
-                        const unsigned lo = __shfl_sync(kFull, (unsigned)cw, i);
-                        const unsigned hi = __shfl_sync(kFull, (unsigned)(cw >> 32), i);
-                        const int c = (int)(lo >> 27), n = (int)(lo & 0x7ffffffu);
-                        const float coef = __uint_as_float(hi) * net.fx_inv[c];
-                        const float *qrow = rc.Qt + ((size_t)c * N + n) * B;
-                        if (ok_a) sub_a += coef * __ldcg(qrow + b_a);
-                        if (ok_b) sub_b += coef * __ldcg(qrow + b_b);
+                    // eight edges at a time: their sixteen trial-row loads in flight together
+                    for (int i0 = 0; i0 < m; i0 += 8) {
+                        float coef[8], qa[8], qb[8];
+#pragma unroll
+                        for (int u = 0; u < 8; u++) {
+                            const int i = i0 + u;  // lanes past m hold 0: coefficient 0, row 0
+                            const unsigned lo = __shfl_sync(kFull, (unsigned)cw, i & 31);
+                            const unsigned hi = __shfl_sync(kFull, (unsigned)(cw >> 32), i & 31);
+                            const bool live = i < m;
+                            const int c = live ? (int)(lo >> 27) : 0, n = live ? (int)(lo & 0x7ffffffu) : 0;
+                            coef[u] = live ? __uint_as_float(hi) * net.fx_inv[c] : 0.0f;
+                            const float *qrow = rc.Qt + ((size_t)c * N + n) * B;
+                            qa[u] = ok_a ? __ldcg(qrow + b_a) : 0.0f;
+                            qb[u] = ok_b ? __ldcg(qrow + b_b) : 0.0f;
+                        }
+#pragma unroll
+                        for (int u = 0; u < 8; u++) {
+                            sub_a += coef[u] * qa[u];
+                            sub_b += coef[u] * qb[u];
+                        }
                     }
                 }
             }
