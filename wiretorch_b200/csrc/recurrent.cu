@@ -11,7 +11,8 @@
 //      e of j (pathway k, target n, channel c), with the edge's folded weight
 //      w_e scale[k, n] jf[k, c] (its fixed-point word over 2^s_c),
 //      R[b, j] = sum_e coef_e Q[b, c, n]  (a gated slot's sum times its factor at t),
-//      each edge's 32 or 64 trials one coalesced read of the L2-resident Q.
+//      each lane decoding one of 32 edges, the warp then reading each edge's 64 trials
+//      as one coalesced 256-byte row of the L2-resident Q (two trials per lane).
 #include "common.cuh"
 
 namespace wt {
@@ -53,8 +54,11 @@ __global__ void __launch_bounds__(256) carry_kernel(const WtNet net, const WtRec
     const int N = net.N, B = net.B;
     if (j >= N) return;  // whole warps
     const int slot0 = net.src_slot[j], slot1 = net.src_slot[j + 1];
+    const bool pairs = (B & 1) == 0;  // trials two at a time: one 8-byte load per edge
     for (int bb = 0; bb < B; bb += 64) {
-        const int b_a = bb + lane, b_b = bb + 32 + lane;
+        // this lane's trials: bb + 2 lane, + 1 (pairs), else bb + lane, bb + 32 + lane
+        const int b_a = pairs ? bb + 2 * lane : bb + lane;
+        const int b_b = pairs ? b_a + 1 : bb + 32 + lane;
         const bool ok_a = b_a < B, ok_b = b_b < B;
         float acc_a = 0.0f, acc_b = 0.0f;
         for (int slot = slot0; slot < slot1; slot++) {
@@ -64,27 +68,41 @@ __global__ void __launch_bounds__(256) carry_kernel(const WtNet net, const WtRec
                 const long long e0 = d & ((1LL << 56) - 1);
                 const int len = (int)((unsigned long long)d >> 56);
                 for (int q0 = 0; q0 < len; q0 += 32) {
-                    const unsigned long long cw = q0 + lane < len ? __ldg(net.edge_cw + e0 + q0 + lane) : 0ull;
+                    // each lane decodes one edge: its Q row (c N + n) and coefficient
+                    unsigned row = 0;
+                    float coef = 0.0f;
+                    if (q0 + lane < len) {
+                        const unsigned long long cw = __ldg(net.edge_cw + e0 + q0 + lane);
+                        const unsigned lo = (unsigned)cw;
+                        const int c = (int)(lo >> 27);
+                        row = (unsigned)c * (unsigned)N + (lo & 0x7ffffffu);
+                        coef = __uint_as_float((unsigned)(cw >> 32)) * net.fx_inv[c];
+                    }
                     const int m = min(32, len - q0);
-                    // eight edges at a time: their sixteen trial-row loads in flight together
                     for (int i0 = 0; i0 < m; i0 += 8) {
-                        float coef[8], qa[8], qb[8];
+                        float cf[8], qa[8], qb[8];
 #pragma unroll
-                        for (int u = 0; u < 8; u++) {
-                            const int i = i0 + u;  // lanes past m hold 0: coefficient 0, row 0
-                            const unsigned lo = __shfl_sync(kFull, (unsigned)cw, i & 31);
-                            const unsigned hi = __shfl_sync(kFull, (unsigned)(cw >> 32), i & 31);
-                            const bool live = i < m;
-                            const int c = live ? (int)(lo >> 27) : 0, n = live ? (int)(lo & 0x7ffffffu) : 0;
-                            coef[u] = live ? __uint_as_float(hi) * net.fx_inv[c] : 0.0f;
-                            const float *qrow = rc.Qt + ((size_t)c * N + n) * B;
-                            qa[u] = ok_a ? __ldcg(qrow + b_a) : 0.0f;
-                            qb[u] = ok_b ? __ldcg(qrow + b_b) : 0.0f;
+                        for (int u = 0; u < 8; u++) {  // lanes past m hold row 0, coefficient 0
+                            const int src = (i0 + u) & 31;
+                            const unsigned r = __shfl_sync(kFull, row, src);
+                            cf[u] = __shfl_sync(kFull, coef, src);
+                            const float *qrow = rc.Qt + (size_t)r * B;
+                            if (pairs) {
+                                float2 q2 = make_float2(0.0f, 0.0f);
+                                if (ok_a) q2 = __ldcg(reinterpret_cast<const float2 *>(qrow + b_a));
+                                qa[u] = q2.x;
+                                qb[u] = q2.y;
+                            } else {
+                                qa[u] = ok_a ? __ldcg(qrow + b_a) : 0.0f;
+                                qb[u] = ok_b ? __ldcg(qrow + b_b) : 0.0f;
+                            }
                         }
 #pragma unroll
                         for (int u = 0; u < 8; u++) {
-                            sub_a += coef[u] * qa[u];
-                            sub_b += coef[u] * qb[u];
+                            if (i0 + u < m) {
+                                sub_a += cf[u] * qa[u];
+                                sub_b += cf[u] * qb[u];
+                            }
                         }
                     }
                 }
