@@ -53,6 +53,8 @@ def parse():
     ap.add_argument("--config", default="c2", choices=["c2", "c1", "c3", "c4"])
     ap.add_argument("--chunk", type=int, default=None,
                     help="c3 / c4: steps per engine call, the state carried over (default 250 / 1000)")
+    ap.add_argument("--partition", action="store_true",
+                    help="c2 / c4 forward: the network's neurons partitioned over the ranks (strong scaling)")
     ap.add_argument("--recurrent-gradients", action="store_true",
                     help="c2: gradients through the recurrent spikes (Drive.recurrent_gradients)")
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
@@ -385,9 +387,73 @@ def config_of(args, cfg, world):
     return c
 
 
+def main_partition(args, rank, world, local):
+    """``--partition``: one network (c2 or c4, forward only) with its neurons partitioned
+    over the ranks, each step's spikes exchanged by peer stores inside the forward kernel.
+    Total work is fixed as ranks are added (strong scaling)."""
+    from wiretorch_b200 import _lib, partition
+
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    cfg, x = build(args, 0, device)  # every rank: the same network and input
+    part = partition.Partition(cfg.N, cfg.B)
+    chunked = cfg.name == "c4"
+
+    def step():
+        v, g, kw = cfg.state()
+        with torch.no_grad():
+            for _ in range(cfg.T // x.shape[1] if chunked else 1):
+                run = partition.simulate(part, v, g, x, cfg.drive, cfg.p, **kw)
+                v, g, kw = run.v, run.syn, {"refractory": run.refractory}
+                if run.adaptation is not None:
+                    kw["adaptation"] = run.adaptation
+        return run
+
+    for _ in range(max(args.warmup, 3)):
+        step()
+    torch.cuda.synchronize()
+    _lib.TIMER = {}
+    barrier(world)
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with Clocks(local) as clocks:
+        start.record()
+        for _ in range(args.steps):
+            run = step()
+        end.record()
+        torch.cuda.synchronize()
+    barrier(world)
+    timer, _lib.TIMER = _lib.TIMER, None
+    elapsed_max = max_over_ranks(start.elapsed_time(end) / 1000.0, world)
+    kernel = {k: sum(a.elapsed_time(b) for a, b in v) / len(v) for k, v in timer.items()}
+    neuron_steps = cfg.B * cfg.N * cfg.T * args.steps  # the one network, whatever the ranks
+    spikes = sum_over_ranks(float(run.output.sum()), world)
+    if rank == 0:
+        print(json.dumps({
+            "metric": "neuron-steps/s", "value": neuron_steps / elapsed_max, "unit": "neuron-steps/s",
+            "n_gpus": world, "steps": args.steps, "warmup": max(args.warmup, 3),
+            "ms_per_step": elapsed_max / args.steps * 1000.0, "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded Poisson input, seeded connectome)",
+            "config": {**config_of(args, cfg, world), "parallelism": f"neuron-partition x{world}",
+                       "global_batch": cfg.B,
+                       "workload": f"{cfg.name}: {cfg.N} neurons ({world} blocks), {cfg.B} trials, {cfg.T} steps "
+                                   f"of 0.1 ms, forward, spikes exchanged each step by peer stores"},
+            "mean_rate_hz": spikes / (cfg.B * cfg.N * x.shape[1]) / (DT / 1000.0),
+            "kernel_ms": kernel, "clocks": clocks.summary(),
+        }))  # fmt: skip
+    barrier(world)
+    part.close()
+
+
 def main():
     args = parse()
     rank, world, local = dist_setup(args)
+    if args.partition and args.impl != "reference":
+        main_partition(args, rank, world, local)
+        if world > 1:
+            import torch.distributed as dist
+
+            dist.destroy_process_group()
+        return
     if args.impl == "reference":
         run_reference(args, rank, world)
         if world > 1:

@@ -53,6 +53,7 @@ enum {
     WT_F_TRACK = 1 << 6,      /* per-step v, currents, conductances */
     WT_F_PROB = 1 << 7,       /* escape-noise probabilities output */
     WT_F_SAVE_INPUT = 1 << 8, /* save each step's synaptic input X (learnt decay/jump) */
+    WT_F_PARTITION = 1 << 9,  /* one rank of a neuron-partitioned run (WtForward.words...) */
 };
 
 /* The network as the kernels see it (built once per network and per call from the
@@ -91,6 +92,9 @@ typedef struct {
     const int32_t *gate_cols;   /* (n_gates, 4): u column (-1: no STP), n rows,
                                    saturation column (-1: none), saved-factor column */
     int32_t R, R_f;             /* gating columns, saved-factor columns */
+    /* sources that are neurons: N, or in a neuron-partitioned run every rank's neurons
+     * (the N targets here are this rank's; input column i is source N_src + i) */
+    int32_t N_src;
 } WtNet;
 
 /* Buffers of one forward run of T steps (outputs indexed by step t0 + t of a chunk of
@@ -115,6 +119,18 @@ typedef struct {
      * (Bt, T_total, N, S + 1), conductances (Bt, T_total, N, 2, S), adaptation */
     float *track_v, *track_I, *track_g, *track_a;
     int32_t track_b;
+    /* WT_F_PARTITION: this rank holds neurons word0 * 32 .. of the N_src; each step's
+     * spike words of all ranks' neurons are replicated on every rank — words
+     * (2, B, ceil(N_src / 32)) here and the same buffers on the n_ranks ranks (peer
+     * pointers, this rank's own among them), written by their owners — and each rank's
+     * progress through the run is a slot, (epoch << 32) | (step + 1), in every rank's
+     * progress (n_ranks uint64). epoch: the same on all ranks, larger on every call. */
+    uint32_t *words;
+    uint32_t *peer_words[8];
+    unsigned long long *progress;
+    unsigned long long *peer_progress[8];
+    int32_t n_ranks, rank, word0;
+    uint32_t epoch;
 } WtForward;
 
 /* One scatter work item: a chunk of a source's edges, for one trial. */

@@ -1,0 +1,84 @@
+"""The neuron partition's host side on the CPU: the blocks, and each rank's local network
+(its targets' edges, sources kept global), checked in two gloo processes that together
+must hold every edge of the network exactly once."""
+
+import os
+import socket
+
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+from wiretorch_b200 import partition
+from wiretorch_b200.testing import random_network
+
+
+def test_blocks_are_whole_words_covering_the_neurons():
+    for N, P in [(20000, 3), (100, 2), (1000, 8), (33, 2)]:
+        b = partition.blocks(N, P)
+        assert b[0][0] == 0 and b[-1][1] == N
+        assert all(lo % 32 == 0 and lo < hi for lo, hi in b)
+        assert all(b[r][1] == b[r + 1][0] for r in range(P - 1))
+    with pytest.raises(ValueError):
+        partition.blocks(40, 3)
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _rank_main(rank, world, port, result):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        drive, p, *_ = random_network(N=500, n_in=60, B=2, T=10, seed=3)
+        n0, n1 = partition.blocks(500, world)[rank]
+        d_loc, p_loc = partition.local_network(drive, p, n0, n1)
+        # every local edge lands on this rank's block and matches the full weights
+        total = torch.zeros(1, dtype=torch.int64)
+        for (rows, W), (_, W_loc) in zip(drive.recurrent + drive.feedforward, d_loc.recurrent + d_loc.feedforward):
+            if hasattr(W_loc, "row_ptr"):  # SparseRows
+                dense = torch.zeros(W_loc.shape)
+                counts = torch.diff(W_loc.row_ptr)
+                r = torch.repeat_interleave(torch.arange(counts.numel()), counts)
+                dense[r, W_loc.cols.long()] = W_loc.values
+            else:
+                dense = W_loc
+            assert torch.equal(dense, W.detach()[:, n0:n1])
+            total += int((dense != 0).sum())
+        assert p_loc.theta.shape[0] == n1 - n0 and d_loc.scale.shape[1] == n1 - n0
+        dist.all_reduce(total)
+        full = sum(int((W != 0).sum()) for _, W in drive.recurrent + drive.feedforward)
+        result[rank] = int(total) == full
+    finally:
+        dist.destroy_process_group()
+
+
+def test_two_ranks_hold_every_edge_once():
+    world = 2
+    ctx = mp.get_context("spawn")
+    manager = ctx.Manager()
+    result = manager.dict()
+    mp.start_processes(_rank_main, args=(world, _free_port(), result), nprocs=world, start_method="spawn")
+    assert dict(result) == {0: True, 1: True}
+
+
+def test_sparse_rows_restriction():
+    from wiretorch_b200 import configs
+
+    cfg = configs.c1(B=1, T=5, device="cpu")
+    W = cfg.drive.recurrent[0][1]
+    n0, n1 = 320, 704
+    W_loc = partition._restrict(W, n0, n1)
+    dense = torch.zeros(W.shape)
+    counts = torch.diff(W.row_ptr)
+    r = torch.repeat_interleave(torch.arange(counts.numel()), counts)
+    dense[r, W.cols.long()] = W.values
+    loc = torch.zeros(W_loc.shape)
+    counts = torch.diff(W_loc.row_ptr)
+    r = torch.repeat_interleave(torch.arange(counts.numel()), counts)
+    loc[r, W_loc.cols.long()] = W_loc.values
+    assert torch.equal(loc, dense[:, n0:n1])

@@ -26,6 +26,7 @@ ERRORS = {
 }
 
 F_REFRACTORY, F_MG_BLOCK, F_ADAPT, F_SAMPLE, F_GATED = 1, 2, 4, 8, 16
+F_PARTITION = 1 << 9
 F_SAVE, F_TRACK, F_PROB, F_SAVE_INPUT = 32, 64, 128, 256
 
 P = C.c_void_p
@@ -46,7 +47,7 @@ class WtNet(C.Structure):
         ("src_slot", P), ("slot_chunk", P), ("src_chunk", P), ("chunk_desc", P), ("edge_col", P), ("edge_cw", P),
         ("n_slots", C.c_int32), ("n_chunks", C.c_int32), ("n_rec_edges", C.c_int64),
         ("slot_gate", P), ("slot_row", P), ("gate_params", P), ("gate_cols", P),
-        ("R", C.c_int32), ("R_f", C.c_int32),
+        ("R", C.c_int32), ("R_f", C.c_int32), ("N_src", C.c_int32),
     ]  # fmt: skip
 
 
@@ -59,6 +60,8 @@ class WtForward(C.Structure):
         ("a_saved", P), ("f_saved", P), ("X_saved", P),
         ("track_v", P), ("track_I", P), ("track_g", P), ("track_a", P),
         ("track_b", C.c_int32),
+        ("words", P), ("peer_words", P * 8), ("progress", P), ("peer_progress", P * 8),
+        ("n_ranks", C.c_int32), ("rank", C.c_int32), ("word0", C.c_int32), ("epoch", C.c_uint32),
     ]  # fmt: skip
 
 

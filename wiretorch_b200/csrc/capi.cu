@@ -51,6 +51,7 @@ int check_net(const WtNet *n) {
         return fail(WT_ERR_ARGS, "missing neuron tables%s");
     if (!n->src_slot || !n->slot_chunk || !n->src_chunk || (n->n_chunks && (!n->chunk_desc || !n->edge_col)))
         return fail(WT_ERR_ARGS, "missing connectivity%s");
+    if (n->N_src != 0 && (n->N_src < n->N || n->N_src >= (1 << 27))) return fail(WT_ERR_ARGS, "bad N_src%s");
     return WT_OK;
 }
 }  // namespace
@@ -122,6 +123,20 @@ int wt_forward(const WtNet *net, const WtForward *run, const WtWorkspace *ws, vo
     if (ws->ev_cap < (long long)net->B * net->n_chunks) return fail(WT_ERR_ARGS, "event capacity too small%s");
     if (((uintptr_t)ws->X & 15) || ((uintptr_t)ws->ev & 15))
         return fail(WT_ERR_ARGS, "workspace X and ev must be 16-byte aligned%s");
+    if (f & WT_F_PARTITION) {
+        if (f & (WT_F_SAVE | WT_F_GATED | WT_F_SAVE_INPUT))
+            return fail(WT_ERR_UNSUPPORTED, "a partitioned run is forward only and ungated%s");
+        if (run->n_ranks < 1 || run->n_ranks > 8 || run->rank < 0 || run->rank >= run->n_ranks || !run->words ||
+            !run->progress)
+            return fail(WT_ERR_ARGS, "bad partition%s");
+        for (int r = 0; r < run->n_ranks; r++)
+            if (!run->peer_words[r] || !run->peer_progress[r]) return fail(WT_ERR_ARGS, "missing peer buffers%s");
+        const int n_src = net->N_src ? net->N_src : net->N;
+        if (run->word0 < 0 || (long long)run->word0 * 32 + net->N > ((long long)n_src + 31) / 32 * 32)
+            return fail(WT_ERR_ARGS, "this rank's neurons lie outside the sources%s");
+    } else if (net->N_src && net->N_src != net->N) {
+        return fail(WT_ERR_ARGS, "a net with other neurons' sources needs WT_F_PARTITION%s");
+    }
     if (run->T == 0) return WT_OK;
     cudaStream_t st = (cudaStream_t)stream;
     cudaError_t e = cudaMemsetAsync(ws->barrier, 0, 64 * 4, st);
@@ -132,6 +147,7 @@ int wt_forward(const WtNet *net, const WtForward *run, const WtWorkspace *ws, vo
 int wt_backward(const WtNet *net, const WtBackward *bw, void *stream) {
     int rc = check_net(net);
     if (rc) return rc;
+    if (net->N_src && net->N_src != net->N) return fail(WT_ERR_UNSUPPORTED, "no backward pass for a partitioned net%s");
     if (!bw || bw->T < 0) return fail(WT_ERR_ARGS, "bad backward arguments%s");
     if (!bw->grad_spikes || !bw->v_saved || !bw->G_saved || !bw->spike_bits || !bw->Q)
         return fail(WT_ERR_ARGS, "missing saved tensors%s");
@@ -152,6 +168,7 @@ int wt_backward(const WtNet *net, const WtBackward *bw, void *stream) {
 int wt_edge_grads(const WtNet *net, const WtEdgeGrads *eg, void *stream) {
     int rc = check_net(net);
     if (rc) return rc;
+    if (net->N_src && net->N_src != net->N) return fail(WT_ERR_UNSUPPORTED, "no backward pass for a partitioned net%s");
     if (!eg || eg->T < 0 || !eg->Q || !eg->chunk_path || !eg->jf) return fail(WT_ERR_ARGS, "bad edge arguments%s");
     if ((eg->g_scale || eg->g_w) && (!eg->spike_bits || (net->n_in && !eg->x)))
         return fail(WT_ERR_ARGS, "missing events%s");

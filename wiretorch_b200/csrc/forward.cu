@@ -271,8 +271,11 @@ __global__ void __launch_bounds__(warps_of<S, FEAT>() * 32, 1) forward_kernel(co
     const bool PROB = GEN && (flags & WT_F_PROB);
     const bool TRACK = GEN && (flags & WT_F_TRACK);
     const bool SAVE_IN = GEN && (flags & WT_F_SAVE_INPUT);
+    const bool PART = GEN && (flags & WT_F_PARTITION);
 
     const int B = net.B, N = net.N, n_in = net.n_in, C = net.C, T = run.T, Np = geo.Np;
+    const int Nsrc = net.N_src > 0 ? net.N_src : N;  // neuron sources (all ranks' when partitioned)
+    const int words_src = (Nsrc + 31) >> 5;
     const int Ip = (n_in + 31) & ~31;
     const long long itemsI = (long long)B * Ip;
     const long long nthreads = (long long)gridDim.x * blockDim.x;
@@ -389,6 +392,55 @@ __global__ void __launch_bounds__(warps_of<S, FEAT>() * 32, 1) forward_kernel(co
         }
     };
 
+    // A partitioned run: the warp's spike word of `step` (32 neurons of trial b) into every
+    // rank's replica of the words (this rank's among them).
+    auto publish = [&](int step, int b, int g, float s) {
+        const unsigned word = __ballot_sync(kFull, s > 0.0f);
+        if (lane == 0) {
+            const size_t wi = ((size_t)(step & 1) * B + b) * words_src + run.word0 + g;
+            for (int r = 0; r < run.n_ranks; r++) run.peer_words[r][wi] = word;
+        }
+    };
+    // ... and once every rank has published `step` (each rank's progress slot, written
+    // by block 0 of its kernel after a grid barrier, waited for with a bounded spin),
+    // the events of that step of every source from the words. Leaves after a grid
+    // barrier; false when an error ended the run.
+    auto exchange = [&](int step) -> bool {
+        if (blockIdx.x == 0 && threadIdx.x == 0) {
+            const unsigned long long mine = ((unsigned long long)run.epoch << 32) | (unsigned)(step + 1);
+            for (int r = 0; r < run.n_ranks; r++)
+                asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(run.peer_progress[r] + run.rank), "l"(mine)
+                             : "memory");
+            for (int r = 0; r < run.n_ranks; r++) {
+                unsigned long long spins = 0, seen = 0;
+                for (;;) {
+                    asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(seen) : "l"(run.progress + r) : "memory");
+                    if (seen >= mine) break;
+                    if (++spins > kSpinLimit) {
+                        set_error(ws.err, WT_ERR_BARRIER);
+                        break;
+                    }
+                    __nanosleep(64);
+                }
+            }
+        }
+        if (!bar.sync(ws.err)) return false;
+        const uint32_t *wsrc = run.words + (size_t)(step & 1) * B * words_src;
+        for (long long it = gwarp; it < (long long)B * words_src; it += nwarps) {
+            const int b = (int)(it / words_src), w = (int)(it % words_src);
+            const unsigned word = __ldcg(wsrc + it);  // written by the ranks: L2, not L1
+            const int j = w * 32 + lane;
+            const bool on = (word >> lane) & 1u;
+            int c0 = 0, cnt = 0;
+            if (on) {
+                c0 = net.src_chunk[j];
+                cnt = net.src_chunk[j + 1] - c0;
+            }
+            emit_fast(net, ws, step, on, b, c0, cnt, 1.0f, lane);
+        }
+        return bar.sync(ws.err);
+    };
+
     // Phase 0: empty accumulators and event counts; resident state.
     for (long long i = gtid; i < 2LL * C * (long long)BNp; i += nthreads) ws.X[i] = 0ull;
     for (long long i = gtid; i <= T; i += nthreads) ws.ev_count[i] = 0u;
@@ -435,7 +487,10 @@ __global__ void __launch_bounds__(warps_of<S, FEAT>() * 32, 1) forward_kernel(co
                 float held;
                 s = spike_of(v, k.theta, cnt, u01, sflags, ksur, held);
             }
-            emit_neuron(0, valid, q.b, n, k, s);
+            if (PART)
+                publish(0, q.b, q.g, s);
+            else
+                emit_neuron(0, valid, q.b, n, k, s);
         }
     }
     for (long long base = warp0; base < itemsI; base += nthreads) {
@@ -443,9 +498,11 @@ __global__ void __launch_bounds__(warps_of<S, FEAT>() * 32, 1) forward_kernel(co
         const int b = (int)(i / (unsigned)Ip), c = (int)(i - (unsigned)b * Ip);
         const bool valid = c < n_in;
         const float xv = valid ? run.x[((size_t)b * run.T_total + run.t0) * n_in + c] : 0.0f;
-        emit_input(0, valid, b, N + c, xv);
+        emit_input(0, valid, b, Nsrc + c, xv);
     }
+    if (PART) __threadfence_system();  // the published words, before the barrier
     if (!bar.sync(ws.err)) return;
+    if (PART && !exchange(0)) return;
 
     for (int t = 0; t < T; t++) {
         const int t_abs = run.t0 + t;
@@ -683,7 +740,12 @@ __global__ void __launch_bounds__(warps_of<S, FEAT>() * 32, 1) forward_kernel(co
                     if (REF) run.held_bits[w] = hb;
                 }
             }
-            if (emit_next) emit_neuron(t + 1, valid, b, n, k, s_next);
+            if (emit_next) {
+                if (PART)
+                    publish(t + 1, b, q.g, s_next);
+                else
+                    emit_neuron(t + 1, valid, b, n, k, s_next);
+            }
             q.next(B, N, Np, TN);
             rp += ks * 32;
         }
@@ -695,10 +757,12 @@ __global__ void __launch_bounds__(warps_of<S, FEAT>() * 32, 1) forward_kernel(co
                 const int b = (int)(i / (unsigned)Ip), c = (int)(i - (unsigned)b * Ip);
                 const bool valid = c < n_in;
                 const float xv = valid ? run.x[((size_t)b * run.T_total + t_abs + 1) * n_in + c] : 0.0f;
-                emit_input(t + 1, valid, b, N + c, xv);
+                emit_input(t + 1, valid, b, Nsrc + c, xv);
             }
         }
+        if (PART) __threadfence_system();
         if (!bar.sync(ws.err)) return;
+        if (PART && emit_next && !exchange(t + 1)) return;
     }
 
     // The input of the last step completes the conductances the run leaves; resident
@@ -869,7 +933,8 @@ static cudaError_t launch_sf(const WtNet &net, const WtForward &run, const WtWor
 // and saving as given; no other feature); everything else runs the generic kernel.
 template <int S>
 static cudaError_t launch_s(const WtNet &net, const WtForward &run, const WtWorkspace &ws, cudaStream_t st) {
-    const int generic = WT_F_ADAPT | WT_F_MG_BLOCK | WT_F_SAMPLE | WT_F_GATED | WT_F_PROB | WT_F_TRACK | WT_F_SAVE_INPUT;
+    const int generic = WT_F_ADAPT | WT_F_MG_BLOCK | WT_F_SAMPLE | WT_F_GATED | WT_F_PROB | WT_F_TRACK | WT_F_SAVE_INPUT |
+                        WT_F_PARTITION;
     if (S > 4 || (run.flags & generic)) return launch_sf<S, kGeneric>(net, run, ws, st);
     const int feat = ((run.flags & WT_F_REFRACTORY) ? kRef : 0) | ((run.flags & WT_F_SAVE) ? kSave : 0);
     switch (feat) {

@@ -125,7 +125,7 @@ def check_device(err: torch.Tensor, what: str) -> None:
 
 
 def run_forward(plan, p, x, v, g, counter, g_a, gating, *, probabilities=False, track=False,
-                track_b=-1, save=None, noise=None, check=True):  # fmt: skip
+                track_b=-1, save=None, noise=None, check=True, part=None):  # fmt: skip
     """Launch the forward kernel over all of ``x``; returns the outputs (dict)."""
     device = plan.device
     B, T, n_in = x.shape
@@ -195,6 +195,9 @@ def run_forward(plan, p, x, v, g, counter, g_a, gating, *, probabilities=False, 
             flags |= _lib.F_SAVE_INPUT
             save["X"] = torch.empty((B, T, plan.ch.C, N), device=device)
             run.X_saved = save["X"].data_ptr()
+    if part is not None:  # one rank of a neuron-partitioned run (wiretorch_b200.partition)
+        flags |= _lib.F_PARTITION
+        part.fill(run)
     run.flags = flags
     ws, w = _workspace(plan, T, device)
     out["_ws"] = ws

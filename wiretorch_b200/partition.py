@@ -1,0 +1,180 @@
+"""Neuron-partitioned runs: the network's neurons cut into blocks, one block per rank
+(one process per GPU), every rank simulating its block for all trials.
+
+A rank holds the state of its neurons and every edge that ends on them (its sources are
+all ranks' neurons and the input columns). Each step the forward kernel of every rank
+writes the spike words of its neurons (32 neurons of one trial per 32-bit word) into the
+replicated spike words of every rank — peer stores over NVLink into buffers mapped with
+CUDA IPC, no collective call — then publishes its progress into every rank's progress
+slots; once all ranks have published the step, each rank emits the events of every
+source from the words into its own targets. The next step's scatter and update follow,
+so the exchange of step t + 1's spikes costs one wait per step (``WT_F_PARTITION``).
+
+Blocks are whole 32-neuron words. The inputs ``x`` are replicated on every rank. The
+run is forward only (no saving for a backward pass) and ungated. The fixed-point
+synaptic sums make a partitioned run's spikes identical to a one-GPU run's.
+"""
+
+from __future__ import annotations
+
+import copy
+
+import torch
+
+
+def blocks(N: int, P: int) -> list[tuple[int, int]]:
+    """The neurons ``[n0, n1)`` of each of P ranks: contiguous runs of whole 32-neuron
+    words, as even as the words allow."""
+    words = -(-N // 32)
+    if words < P:
+        raise ValueError(f"{N} neurons are fewer than one 32-neuron word for each of {P} ranks")
+    cuts = [words * r // P for r in range(P + 1)]
+    return [(cuts[r] * 32, min(N, cuts[r + 1] * 32)) for r in range(P)]
+
+
+def _restrict(W, n0: int, n1: int):
+    """The columns ``[n0, n1)`` of a pathway's weights (dense or ``SparseRows``), as
+    ``SparseRows`` with targets renumbered from 0."""
+    from wiretorch_b200.types import SparseRows
+
+    if isinstance(W, SparseRows):
+        cols = W.cols.long()
+        keep = (cols >= n0) & (cols < n1)
+        counts = torch.diff(W.row_ptr)
+        rows = torch.repeat_interleave(torch.arange(counts.numel(), device=cols.device), counts)
+        rows = rows[keep]
+        row_ptr = torch.zeros_like(W.row_ptr)
+        row_ptr[1:] = torch.cumsum(torch.bincount(rows, minlength=counts.numel()), 0)
+        return SparseRows(row_ptr, (cols[keep] - n0).to(torch.int32), W.values.detach()[keep].contiguous(), n1 - n0)
+    return W.detach()[:, n0:n1].contiguous()
+
+
+def local_network(drive, p, n0: int, n1: int):
+    """``(drive, p)`` of the rank holding neurons ``[n0, n1)``: every pathway's edges onto
+    those neurons (sources keep their global indices), the per-target scales and the
+    per-neuron physiology of the block."""
+    d = copy.copy(drive)
+    d.recurrent = [(rows, _restrict(W, n0, n1)) for rows, W in drive.recurrent]
+    d.feedforward = [(rows, _restrict(W, n0, n1)) for rows, W in drive.feedforward]
+    d.scale = drive.scale.detach()[:, n0:n1].contiguous()
+    q = copy.copy(p)
+    for name in ("theta", "U_reset", "E_L", "C_m", "beta", "n_ref", "adapt", "adapt_decay", "E_adapt"):
+        t = getattr(p, name, None)
+        if isinstance(t, torch.Tensor) and t.dim() == 1 and t.numel() == drive.scale.shape[1]:
+            setattr(q, name, t.detach()[n0:n1].contiguous())
+    return d, q
+
+
+def _cuda(result):
+    """The values of a cuda-python runtime call, raising on its error code."""
+    from cuda.bindings import runtime as rt
+
+    err, *vals = result
+    if err != rt.cudaError_t.cudaSuccess:
+        raise RuntimeError(f"CUDA runtime: {rt.cudaGetErrorString(err)[1].decode()}")
+    return vals[0] if len(vals) == 1 else vals
+
+
+class Partition:
+    """This rank's block and the buffers shared with the other ranks (``group``: a
+    ``torch.distributed`` group of one process per GPU, any backend; used on the host
+    only, to exchange the buffers' CUDA IPC handles). The shared buffers are a
+    ``cudaMalloc`` of their own, so that their IPC handle is their allocation's; call
+    ``close`` on every rank, after a barrier, when the runs are over."""
+
+    def __init__(self, N: int, B: int, group=None):
+        import torch.distributed as dist
+        from cuda.bindings import runtime as rt
+
+        self.group = group
+        self.P = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        if self.P > 8:
+            raise NotImplementedError("at most 8 ranks")
+        self.N, self.B = N, B
+        self.n0, self.n1 = blocks(N, self.P)[self.rank]
+        self.words_src = -(-N // 32)
+        words_bytes = -(-(2 * B * self.words_src * 4) // 256) * 256
+        total = words_bytes + 8 * 8
+        torch.cuda.synchronize()
+        self._base = _cuda(rt.cudaMalloc(total))
+        _cuda(rt.cudaMemset(self._base, 0, total))
+        _cuda(rt.cudaDeviceSynchronize())
+        handle = _cuda(rt.cudaIpcGetMemHandle(self._base))
+        handles = [None] * self.P
+        dist.all_gather_object(handles, bytes(handle.reserved), group=group)
+        self._opened = []
+        bases = []
+        for r, hb in enumerate(handles):
+            if r == self.rank:
+                bases.append(int(self._base))
+                continue
+            h = rt.cudaIpcMemHandle_t()
+            h.reserved = hb
+            peer = _cuda(rt.cudaIpcOpenMemHandle(h, rt.cudaIpcMemLazyEnablePeerAccess))
+            self._opened.append(peer)
+            bases.append(int(peer))
+        self.peer_words = bases
+        self.peer_progress = [b + words_bytes for b in bases]
+        self.words, self.progress = bases[self.rank], bases[self.rank] + words_bytes
+        self.epoch = 0
+        dist.barrier(group=group)
+
+    def fill(self, run) -> None:
+        """The partition's fields of a ``WtForward`` for the next call (a new epoch)."""
+        self.epoch += 1
+        run.words, run.progress = self.words, self.progress
+        for r in range(self.P):
+            run.peer_words[r] = self.peer_words[r]
+            run.peer_progress[r] = self.peer_progress[r]
+        run.n_ranks, run.rank, run.word0, run.epoch = self.P, self.rank, self.n0 // 32, self.epoch
+
+    def close(self) -> None:
+        from cuda.bindings import runtime as rt
+
+        for peer in self._opened:
+            _cuda(rt.cudaIpcCloseMemHandle(peer))
+        self._opened = []
+        if self._base is not None:
+            _cuda(rt.cudaFree(self._base))
+            self._base = None
+
+
+_LOCAL: dict = {}
+
+
+def simulate(part: Partition, v, g, x, drive, p, *, refractory=None, adaptation=None, pool=None):
+    """This rank's block of a neuron-partitioned forward run: ``engine.simulate`` for the
+    neurons ``[part.n0, part.n1)`` of the network ``(drive, p)`` (all ranks call it with
+    the full network and input, and the full state or their block's own, as a previous
+    call returned it). Returns the block's ``Run`` (spikes ``(B, T, n1 - n0)``, its
+    state). Synchronises the device and the ranks once per call."""
+    from wiretorch_b200 import engine, plan as _plan
+
+    if not x.is_cuda:
+        raise RuntimeError("wiretorch_b200 runs on CUDA tensors only (no CPU path)")
+    if drive.gates:
+        raise NotImplementedError("a partitioned run is ungated")
+    n0, n1 = part.n0, part.n1
+    key = (id(drive), id(p), part.rank, part.P, x.shape[0], x.shape[2])
+    cached = _LOCAL.get(key)
+    if cached is None:
+        d_loc, p_loc = local_network(drive, p, n0, n1)
+        pool_ = engine.POOL_SYNAPSES if pool is None else pool
+        plan = _plan.build(d_loc, p_loc, x.shape[0], x.shape[2], x.device, pool=pool_, n_src=part.N)
+        cached = _LOCAL[key] = (d_loc, p_loc, plan)
+    d_loc, p_loc, plan = cached
+    _plan.fold(plan, d_loc.scale)
+    local = v.shape[1] == n1 - n0 != part.N  # the block's own state (a previous call's Run)
+    cut = (lambda t: t) if local else (lambda t: None if t is None else t[:, n0:n1])  # noqa: E731
+    v_k, g_k, counter, g_a, _ = engine._prepare_state(plan, cut(v), cut(g), cut(refractory), None,
+                                                      cut(adaptation), p_loc)  # fmt: skip
+    # All ranks' kernels start together (their exchange waits are bounded), and none
+    # starts before every rank's previous call has finished reading the shared words.
+    import torch.distributed as dist
+
+    torch.cuda.synchronize()
+    dist.barrier(group=part.group)
+    with torch.no_grad():
+        out = engine.run_forward(plan, p_loc, x.detach().float(), v_k, g_k, counter, g_a, None, part=part)
+    return engine._run(plan, out, v_k, g_k, counter, g_a, None, p_loc, False, refractory)

@@ -187,6 +187,7 @@ class Plan:
     R_f: int = 0
     gated: bool = False
     gate_f_cols: list = field(default_factory=list)  # per pathway: saved-factor column, -1
+    N_src: int = 0  # neurons that are sources (N, or every rank's in a partitioned run)
 
     def net_for_fold(self) -> _lib.WtNet:
         """A ``WtNet`` with the structure only (enough for ``wt_fold_weights``)."""
@@ -198,6 +199,7 @@ class Plan:
         n.chunk_desc = t["chunk_desc"].data_ptr()
         n.edge_col = t["edge_col"].data_ptr()
         n.n_slots, n.n_chunks = self.n_slots, self.n_chunks
+        n.N_src = self.N_src or self.N
         one = t.setdefault("_one", torch.ones(1, device=self.device))
         n.theta = n.U_reset = n.E_L = n.C_m = n.beta = one.data_ptr()
         return n
@@ -249,13 +251,17 @@ class Plan:
             n.slot_gate, n.slot_row = t["slot_gate"].data_ptr(), t["slot_row"].data_ptr()
             n.gate_params, n.gate_cols = t["gate_params"].data_ptr(), t["gate_cols"].data_ptr()
         n.R, n.R_f = self.R, self.R_f
+        n.N_src = self.N_src or self.N
         return n
 
 
-def build(drive, p, B: int, n_in: int, device, pool: bool = False) -> Plan:
-    """Compile the structure of ``drive`` (weights are folded per call: ``fold``)."""
+def build(drive, p, B: int, n_in: int, device, pool: bool = False, n_src: int | None = None) -> Plan:
+    """Compile the structure of ``drive`` (weights are folded per call: ``fold``).
+    ``n_src``: the neurons that are sources, when they are not the N targets (one rank of
+    a neuron-partitioned run: its targets, every rank's neurons as sources)."""
     device = torch.device(device)
     N = int(drive.scale.shape[1])
+    N_src = N if n_src is None else int(n_src)
     pathways = [(r, W, True) for r, W in drive.recurrent]
     pathways += [(r, W, False) for r, W in drive.feedforward]
     K = len(pathways)
@@ -296,7 +302,7 @@ def build(drive, p, B: int, n_in: int, device, pool: bool = False) -> Plan:
     src_l, path_l, row_l = [], [], []
     for k, (rows, W, rec) in enumerate(pathways):
         rows = rows.to(device, torch.int64)
-        src_l.append(rows if rec else rows + N)
+        src_l.append(rows if rec else rows + N_src)
         path_l.append(torch.full_like(rows, k))
         row_l.append(torch.arange(rows.numel(), device=device))
     if src_l:
@@ -305,7 +311,8 @@ def build(drive, p, B: int, n_in: int, device, pool: bool = False) -> Plan:
         src = path = row = torch.zeros(0, dtype=torch.int64, device=device)
     order = torch.argsort(src * max(K, 1) + path)
     src, path, row = src[order], path[order], row[order]
-    n_src = N + n_in
+    plan.N_src = N_src
+    n_src = N_src + n_in
     src_slot = torch.zeros(n_src + 1, dtype=torch.int64, device=device)
     src_slot[1:] = torch.cumsum(torch.bincount(src, minlength=n_src), 0)
     plan.n_slots = int(src.numel())
