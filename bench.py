@@ -50,11 +50,11 @@ def parse():
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
-    ap.add_argument("--config", default="c2", choices=["c2", "c1", "c3", "c4"])
+    ap.add_argument("--config", default="c2", choices=["c2", "c1", "c3", "c4", "c5"])
     ap.add_argument("--chunk", type=int, default=None,
-                    help="c3 / c4: steps per engine call, the state carried over (default 250 / 1000)")
+                    help="c3 / c4 / c5: steps per engine call, the state carried over (default 250 / 1000 / 1000)")
     ap.add_argument("--partition", action="store_true",
-                    help="c2 / c4 forward: the network's neurons partitioned over the ranks (strong scaling)")
+                    help="c2 / c4 / c5 forward: the network's neurons partitioned over the ranks (strong scaling)")
     ap.add_argument("--recurrent-gradients", action="store_true",
                     help="c2: gradients through the recurrent spikes (Drive.recurrent_gradients)")
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
@@ -183,12 +183,15 @@ def build(args, rank, device):
         cfg = configs.c2(B=args.batch or 64, T=500, seed=0, device=device)
         engine.POOL_SYNAPSES = True  # 41 synapse types with 2 distinct dynamics
         cfg.drive.recurrent_gradients = args.recurrent_gradients
-    elif args.config in ("c3", "c4"):
+    elif args.config in ("c3", "c4", "c5"):
         if args.config == "c3":
             cfg = configs.c3(B=args.batch or 256, T=2000, seed=0, device=device)
-        else:
+        elif args.config == "c4":
             cfg = configs.c4(B=args.batch or 32, T=10000, seed=0, device=device)
             engine.POOL_SYNAPSES = True
+        else:
+            cfg = configs.c5(B=args.batch or 4, T=5000, seed=0, device=device)
+            engine.POOL_SYNAPSES = True  # the excitatory and the input AMPA share dynamics
         args.chunk = args.chunk or (250 if args.config == "c3" else 1000)
         cfg.extra["chunk"] = args.chunk
         return cfg, cfg.inputs(T=args.chunk, seed=1 + rank)  # one chunk of input, reused
@@ -203,16 +206,14 @@ def make_step(cfg, world, train: bool):
     from wiretorch_b200 import configs, engine, filtering
 
     v0, g0, kw0 = cfg.state()
-    if cfg.name in ("c3", "c4"):
+    if cfg.name in ("c3", "c4", "c5"):
         def forward_chunks(x, target=None):
             """The T steps as engine calls of x.shape[1] steps, the state carried over."""
             v, g, kw = v0, g0, kw0
             with torch.no_grad():
                 for _ in range(cfg.T // x.shape[1]):
                     run = engine.simulate(v, g, x, cfg.drive, cfg.p, **kw)
-                    v, g, kw = run.v, run.syn, {"refractory": run.refractory}
-                    if run.adaptation is not None:
-                        kw["adaptation"] = run.adaptation
+                    v, g, kw = run.v, run.syn, cfg.carried(run)
             return v.sum()
 
         return forward_chunks, None
@@ -260,15 +261,17 @@ def forward_bytes(cfg, plan, T, spikes_bits_saved: bool, fired_sources_edges: fl
     """Algorithmic bytes of one forward launch: per neuron-step the state read and written
     (v 8, conductances 16 per channel, refractory counter 2, adaptation 8), the spike bit,
     and with saving for the backward pass v 4, summed conductances 4 per channel and the
-    spike and refractory bits; the input read (4 per input-step); and 8 bytes (target,
-    weight) per edge of every source that fired in at least one trial of a step."""
+    spike and refractory bits; the input read (4 per input-step); 8 bytes (target,
+    weight) per edge of every source that fired in at least one trial of a step; and the
+    gating state (release probabilities, resources) read and written, 8 per column-step."""
     S = plan.ch.Sp
     per = 8 + 16 * S + 2 + 1 / 8
     if cfg.p.adapt is not None:
         per += 8
     if spikes_bits_saved:
         per += 4 + 4 * S + 2 / 8
-    return cfg.B * T * cfg.N * per + cfg.B * T * cfg.n_in * 4 + fired_sources_edges * 8
+    gating = cfg.B * T * cfg.extra["gating"].shape[1] * 8 if "gating" in cfg.extra else 0
+    return cfg.B * T * cfg.N * per + cfg.B * T * cfg.n_in * 4 + fired_sources_edges * 8 + gating
 
 
 def factorised_bytes(cfg, T):
@@ -341,6 +344,7 @@ def _to_cpu(cfg):
         if isinstance(val, torch.Tensor):
             setattr(p, name, val.detach().cpu())
     c.drive, c.p = d, p
+    c.extra = {k: (t.cpu() if isinstance(t, torch.Tensor) else t) for k, t in cfg.extra.items()}
     c.out_degree = cfg.out_degree.cpu()
     c.rates_in = cfg.rates_in.cpu()
     return c
@@ -378,8 +382,8 @@ def config_of(args, cfg, world):
         "workload": f"{cfg.name}: {cfg.N} neurons, {cfg.B} trials/GPU, {cfg.T} steps of 0.1 ms"
                     + (", forward + BPTT + van Rossum rate loss + SGD" if args.config == "c2" else ", forward")
                     + (f", factorised W = U V^T rank {cfg.extra.get('rank')}" if args.config == "c3" else "")
-                    + (f", {cfg.extra.get('edges')} edges" if args.config == "c4" else "")
-                    + (f", {args.chunk} steps per call" if args.config in ("c3", "c4") else "")
+                    + (f", {cfg.extra.get('edges')} edges" if args.config in ("c4", "c5") else "")
+                    + (f", {args.chunk} steps per call" if args.config in ("c3", "c4", "c5") else "")
                     + (", gradients through the recurrent spikes" if getattr(args, "recurrent_gradients", False) else ""),
         "global_batch": cfg.B * world, "seq_len": cfg.T, "parallelism": f"trial-batch x{world}",
         "l2": "inputs larger than L2 (spike input and state streams exceed 126 MB per step)",
@@ -388,7 +392,7 @@ def config_of(args, cfg, world):
 
 
 def main_partition(args, rank, world, local):
-    """``--partition``: one network (c2 or c4, forward only) with its neurons partitioned
+    """``--partition``: one network (c2, c4 or c5, forward only) with its neurons partitioned
     over the ranks, each step's spikes exchanged by peer stores inside the forward kernel.
     Total work is fixed as ranks are added (strong scaling)."""
     from wiretorch_b200 import _lib, partition
@@ -397,16 +401,14 @@ def main_partition(args, rank, world, local):
     torch.cuda.set_device(device)
     cfg, x = build(args, 0, device)  # every rank: the same network and input
     part = partition.Partition(cfg.N, cfg.B)
-    chunked = cfg.name == "c4"
+    chunked = cfg.name in ("c4", "c5")
 
     def step():
         v, g, kw = cfg.state()
         with torch.no_grad():
             for _ in range(cfg.T // x.shape[1] if chunked else 1):
                 run = partition.simulate(part, v, g, x, cfg.drive, cfg.p, **kw)
-                v, g, kw = run.v, run.syn, {"refractory": run.refractory}
-                if run.adaptation is not None:
-                    kw["adaptation"] = run.adaptation
+                v, g, kw = run.v, run.syn, cfg.carried(run)
         return run
 
     for _ in range(max(args.warmup, 3)):

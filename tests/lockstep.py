@@ -5,7 +5,8 @@ The oracle runs the whole input, recording its state every ``window`` steps; the
 restarts from each recorded state and runs the window. Spikes must match exactly, except
 a neuron whose voltage entering the step was within ``margin`` mV of threshold (either
 outcome is a legitimate rounding of the same equations; that trial's window is then
-excused); voltages and conductances must match to the tolerances given. This is the
+excused); voltages, conductances and the gating state (release probabilities and
+resources, within g_atol + g_rtol: they lie in [0, 1]) must match to the tolerances given. This is the
 reference suite's own definition of "the same simulator" (its tests/test_lockstep.py).
 """
 
@@ -73,6 +74,11 @@ def compare(engine_sim, net, drive, p, x, v, g, kw, window=10, margin=1e-3, v_at
         ref = states["g"][w + 1]
         err = np.abs(gk[ok] - ref[ok]) - (g_atol + g_rtol * np.abs(ref[ok]))
         assert err.max(initial=-1.0) <= 0, f"window {w}: conductances differ by {np.abs(gk[ok]-ref[ok]).max():.2e}"
+        if "gating" in kw and run.gating is not None:
+            gt = run.gating.detach().cpu().numpy()
+            ref = states["gating"][w + 1]
+            dgt = np.abs(gt[ok] - ref[ok]).max(initial=0.0)
+            assert dgt <= g_atol + g_rtol, f"window {w}: gating state differs by {dgt:.2e}"
         worst_dv = max(worst_dv, float(dv))
         worst_dg = max(worst_dg, float(np.abs(gk[ok] - ref[ok]).max(initial=0.0)))
     return excused, B * (x.shape[1] // window), worst_dv, worst_dg

@@ -46,3 +46,27 @@ def test_lockstep_against_oracle(N, B, feature, pool):
     net = oracle.Network(drive, p, B, x.shape[2])
     excused, windows, dv, dg = lockstep.compare(_sim(drive, p, pool), net, drive, p, x, v, g, kw)
     assert excused <= 0.01 * windows, f"{excused} near-threshold flips in {windows} trial-windows"
+
+
+def _c5_small():
+    """The C5 model (NMDA with Mg block, short-term depression on both recurrent
+    pathways, distance-dependent connectivity) at 4,000 neurons and ~390 edges each."""
+    from wiretorch_b200 import configs
+
+    return configs.c5(B=3, T=120, device="cuda", N=4000, mean_degree=400.0, lam=0.05 * 250 ** (1 / 3),
+                      w_e=3.0, w_in=30.0)  # fmt: skip
+
+
+@pytest.mark.parametrize("pool", [False, True], ids=["exact", "pooled"])
+def test_c5_model_lockstep_against_oracle(pool):
+    cfg = _c5_small()
+    x = cfg.inputs(seed=3)
+    v, g, kw = cfg.state()
+    net = oracle.Network(cfg.drive, cfg.p, cfg.B, cfg.n_in)
+    excused, windows, dv, dg = lockstep.compare(_sim(cfg.drive, cfg.p, pool), net, cfg.drive, cfg.p, x, v, g, kw)
+    assert excused <= 0.01 * windows, f"{excused} near-threshold flips in {windows} trial-windows"
+    with torch.no_grad():
+        run = engine.simulate(v, g, x, cfg.drive, cfg.p, **kw)
+    assert float(run.output.sum()) > 20  # the network is active
+    n_e = cfg.drive.gates[0].n
+    assert float(run.gating[:, n_e : 2 * n_e].min()) < 0.99  # and its excitatory synapses depress

@@ -43,7 +43,8 @@ class Config:
     extra: dict = field(default_factory=dict)
 
     def state(self):
-        """``(v, g, kw)`` at rest: voltages at reset, conductances zero."""
+        """``(v, g, kw)`` at rest: voltages at reset, conductances zero (and the gating
+        state of a gated network at its rest values)."""
         dev = self.drive.scale.device
         S = self.p.E_syn.shape[0]
         v = self.p.U_reset.expand(self.B, self.N).clone()
@@ -51,7 +52,18 @@ class Config:
         kw = {"refractory": torch.zeros((self.B, self.N), dtype=torch.int32, device=dev)}
         if self.p.adapt is not None:
             kw["adaptation"] = torch.zeros((self.B, self.N), device=dev)
+        if "gating" in self.extra:
+            kw["gating"] = self.extra["gating"].clone()
         return v, g, kw
+
+    def carried(self, run):
+        """The state keywords of the next engine call after ``run``."""
+        kw = {"refractory": run.refractory}
+        if run.adaptation is not None:
+            kw["adaptation"] = run.adaptation
+        if "gating" in self.extra:
+            kw["gating"] = run.gating
+        return kw
 
     def inputs(self, T=None, seed=1, generator_device=None):
         """Poisson input spikes ``(B, T, n_in)`` float32 (seeded)."""
@@ -71,7 +83,7 @@ def _kernel(tau_rise, tau_decay, g_bar):
 
 
 def _csr_from_edges(src, dst, w, n_rows, n_targets):
-    order = torch.argsort(src * n_targets + dst)
+    order = torch.argsort(src * n_targets + dst, stable=True)
     src, dst, w = src[order], dst[order], w[order]
     row_ptr = torch.zeros(n_rows + 1, dtype=torch.int64, device=src.device)
     row_ptr[1:] = torch.cumsum(torch.bincount(src, minlength=n_rows), 0)
@@ -328,4 +340,109 @@ def c4(B=32, T=10000, seed=0, device="cuda", N=139000, n_types=8000, mean_degree
     deg[N:] = 1
     cfg = Config("c4", drive, p, B, T, N, n_in, torch.full((n_in,), 15.0, device=dev), types, n_types, deg)
     cfg.extra["edges"] = int(src.numel())
+    return cfg
+
+
+def _distance_edges(gen, pos, mean_degree, lam, dev, batch=20000):
+    """Edges of a distance-dependent random graph on neurons at ``pos`` (N, 3) in the
+    unit cube: every source draws ~Poisson(mean_degree) targets at distances ~
+    Gamma(3, lam) (the law of 0.5 exp(-d / lam) p(d) over a uniform 3-d density) in
+    uniform directions; points outside the cube are reflected back at its faces (so the
+    mean out-degree stays ``mean_degree`` near the faces too), and each point picks a
+    random neuron of its grid cell (cells of ~4 neurons); empty cells and
+    self-connections are dropped."""
+    N = pos.shape[0]
+    G = max(1, round((N / 4.0) ** (1.0 / 3.0)))
+    cell = (pos * G).long().clamp(max=G - 1)
+    cid = (cell[:, 0] * G + cell[:, 1]) * G + cell[:, 2]
+    order = torch.argsort(cid, stable=True)
+    sorted_cid = cid[order]
+    starts = torch.searchsorted(sorted_cid, torch.arange(G**3, device=dev))
+    counts = torch.bincount(cid, minlength=G**3)
+    srcs, dsts = [], []
+    for j0 in range(0, N, batch):
+        j1 = min(N, j0 + batch)
+        k = torch.poisson(torch.full((j1 - j0,), float(mean_degree), device=dev), generator=gen).long()
+        src = torch.repeat_interleave(torch.arange(j0, j1, device=dev), k)
+        m = src.numel()
+        d = -lam * torch.log(torch.rand((m, 3), generator=gen, device=dev).clamp(min=1e-12)).sum(1)  # Gamma(3, lam)
+        u = torch.randn((m, 3), generator=gen, device=dev)
+        pt = pos[src] + u / u.norm(dim=1, keepdim=True).clamp(min=1e-12) * d[:, None]
+        pt = torch.remainder(pt, 2.0)
+        pt = torch.where(pt > 1.0, 2.0 - pt, pt)  # reflection at the faces
+        c = (pt * G).long().clamp(min=0, max=G - 1)
+        tc = (c[:, 0] * G + c[:, 1]) * G + c[:, 2]
+        n_in_cell = counts[tc]
+        ok = n_in_cell > 0
+        src, tc, n_in_cell = src[ok], tc[ok], n_in_cell[ok]
+        pick = (torch.rand(src.numel(), generator=gen, device=dev) * n_in_cell).long().clamp(max=n_in_cell - 1)
+        dst = order[starts[tc] + pick]
+        keep = dst != src
+        srcs.append(src[keep])
+        dsts.append(dst[keep])
+    return torch.cat(srcs), torch.cat(dsts)
+
+
+def c5(B=4, T=5000, seed=0, device="cuda", N=1_000_000, mean_degree=1000.0, lam=0.05, w_e=1.2, g_inh=12.0,
+       nmda=0.1, U=0.2, tau_rec=200.0, w_in=20.0):  # fmt: skip
+    """1,000,000-neuron synthetic connectome: neurons uniform in the unit cube, ~1B edges
+    from a distance-dependent model (connection probability 0.5 exp(-d / 0.05), out-degree
+    capped at a mean of 1,000: every source draws ~Poisson(1000) targets at distances ~
+    Gamma(3, 0.05), see ``_distance_edges``; the uncapped model would give
+    0.5 * 8 pi 0.05^3 * N ~ 1,570 edges per neuron), 80/20 E/I, log-normal weights (sigma 1,
+    mean ``w_e`` nS excitatory, ``g_inh`` times that inhibitory), conductance LIF with
+    AMPA + NMDA (Mg block, 1 mM; NMDA weight ``nmda`` of AMPA's) from excitatory sources
+    and GABA_A from inhibitory ones, short-term depression on both (U=0.2, tau_rec=200 ms,
+    no facilitation), refractoriness, dt=0.1 ms, T=5,000, batch 4, 15 Hz Poisson input to
+    5% of the neurons (weight ``w_in`` nS); forward only, made for the neuron partition.
+    Chosen here: the weights and the input (the specification leaves them open). At these
+    values the network fires at ~2 Hz in irregular population bursts (the oracle at
+    20,000 neurons with the same degree); ``w_e`` 0.6 with ``g_inh`` 3 runs away to
+    200 Hz."""
+    from wiretorch_b200.types import Gate
+
+    dev = torch.device(device)
+    gen = torch.Generator(device=dev).manual_seed(seed)
+    pos = torch.rand((N, 3), generator=gen, device=dev)
+    exc_n = torch.rand(N, generator=gen, device=dev) < 0.8
+    src, dst = _distance_edges(gen, pos, mean_degree, lam, dev)
+    w = torch.exp(math.log(w_e) - 0.5 + torch.randn(src.numel(), generator=gen, device=dev))
+    e = exc_n[src]
+    w = torch.where(e, w, w * g_inh)
+    rows_e, rows_i = torch.nonzero(exc_n).flatten(), torch.nonzero(~exc_n).flatten()
+    row_of = torch.empty(N, dtype=torch.int64, device=dev)
+    row_of[rows_e] = torch.arange(rows_e.numel(), device=dev)
+    row_of[rows_i] = torch.arange(rows_i.numel(), device=dev)
+    W_e = _csr_from_edges(row_of[src[e]], dst[e], w[e], rows_e.numel(), N)
+    W_i = _csr_from_edges(row_of[src[~e]], dst[~e], w[~e], rows_i.numel(), N)
+    n_edges = int(src.numel())
+    out_deg = torch.bincount(src, minlength=N)
+    del src, dst, w, e
+    n_in = max(1, int(round(0.05 * N)))
+    driven = torch.randperm(N, generator=gen, device=dev)[:n_in]
+    W_in = _csr_from_edges(torch.arange(n_in, device=dev), driven, torch.full((n_in,), w_in, device=dev), n_in, N)
+    # synapse types: 0 AMPA (E), 1 NMDA (E), 2 GABA_A (I), 3 AMPA (input)
+    S_params = [(0.0, 5.0, 0.0, 1.0), (2.0, 100.0, 0.0, nmda), (0.0, 10.0, -80.0, 1.0), (0.0, 5.0, 0.0, 1.0)]
+    made = torch.tensor([[1, 1, 0, 0], [0, 0, 1, 0], [0, 0, 0, 1]], dtype=torch.bool, device=dev)
+    d_D = math.exp(-0.1 / tau_rec)
+    params = torch.tensor([0.0, 0.0, U, d_D, 0.0], device=dev)
+    n_e, n_i = rows_e.numel(), rows_i.numel()
+    gates = [Gate(params, stp=True, saturates=False, start=0, n=n_e),
+             Gate(params, stp=True, saturates=False, start=2 * n_e, n=n_i), None]  # fmt: skip
+    drive = Drive(made=made, scale=torch.ones(3, N, device=dev), recurrent=[(rows_e, W_e), (rows_i, W_i)],
+                  feedforward=[(torch.arange(n_in, device=dev), W_in)], gates=gates)  # fmt: skip
+    p = _physiology(N, None, 0.1, S_params, dev)
+    p.mg_c = torch.tensor([0.0, 1.0 / 3.57, 0.0, 0.0], device=dev)
+    p.mg_a = torch.full((4,), 0.062, device=dev)
+    deg = torch.cat([out_deg, torch.ones(n_in, dtype=torch.int64, device=dev)])
+    cfg = Config("c5", drive, p, B, T, N, n_in, torch.full((n_in,), 15.0, device=dev),
+                 (~exc_n).long(), 2, deg)  # fmt: skip
+    cfg.extra["edges"] = n_edges
+    R = 2 * (n_e + n_i)
+    gating = torch.empty((B, R), device=dev)
+    gating[:, : n_e] = U
+    gating[:, n_e : 2 * n_e] = 1.0
+    gating[:, 2 * n_e : 2 * n_e + n_i] = U
+    gating[:, 2 * n_e + n_i :] = 1.0
+    cfg.extra["gating"] = gating  # release probabilities at U, resources full
     return cfg

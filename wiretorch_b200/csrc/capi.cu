@@ -124,8 +124,7 @@ int wt_forward(const WtNet *net, const WtForward *run, const WtWorkspace *ws, vo
     if (((uintptr_t)ws->X & 15) || ((uintptr_t)ws->ev & 15))
         return fail(WT_ERR_ARGS, "workspace X and ev must be 16-byte aligned%s");
     if (f & WT_F_PARTITION) {
-        if (f & (WT_F_SAVE | WT_F_GATED | WT_F_SAVE_INPUT))
-            return fail(WT_ERR_UNSUPPORTED, "a partitioned run is forward only and ungated%s");
+        if (f & (WT_F_SAVE | WT_F_SAVE_INPUT)) return fail(WT_ERR_UNSUPPORTED, "a partitioned run is forward only%s");
         if (run->n_ranks < 1 || run->n_ranks > 8 || run->rank < 0 || run->rank >= run->n_ranks || !run->words ||
             !run->progress)
             return fail(WT_ERR_ARGS, "bad partition%s");

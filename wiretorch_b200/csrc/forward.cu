@@ -431,6 +431,10 @@ __global__ void __launch_bounds__(warps_of<S, FEAT>() * 32, 1) forward_kernel(co
             const unsigned word = __ldcg(wsrc + it);  // written by the ranks: L2, not L1
             const int j = w * 32 + lane;
             const bool on = (word >> lane) & 1u;
+            if (gated) {  // every source's gates step, on every rank alike (replicated state)
+                emit(net, run, ws, step, j < Nsrc, b, j, on ? 1.0f : 0.0f, true, lane);
+                continue;
+            }
             int c0 = 0, cnt = 0;
             if (on) {
                 c0 = net.src_chunk[j];

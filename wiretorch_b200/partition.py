@@ -10,8 +10,9 @@ slots; once all ranks have published the step, each rank emits the events of eve
 source from the words into its own targets. The next step's scatter and update follow,
 so the exchange of step t + 1's spikes costs one wait per step (``WT_F_PARTITION``).
 
-Blocks are whole 32-neuron words. The inputs ``x`` are replicated on every rank. The
-run is forward only (no saving for a backward pass) and ungated. The fixed-point
+Blocks are whole 32-neuron words. The inputs ``x`` are replicated on every rank, and so
+is the gating state of gated pathways (every rank steps every source's gates alike from
+the words). The run is forward only (no saving for a backward pass). The fixed-point
 synaptic sums make a partitioned run's spikes identical to a one-GPU run's.
 """
 
@@ -143,7 +144,7 @@ class Partition:
 _LOCAL: dict = {}
 
 
-def simulate(part: Partition, v, g, x, drive, p, *, refractory=None, adaptation=None, pool=None):
+def simulate(part: Partition, v, g, x, drive, p, *, refractory=None, gating=None, adaptation=None, pool=None):
     """This rank's block of a neuron-partitioned forward run: ``engine.simulate`` for the
     neurons ``[part.n0, part.n1)`` of the network ``(drive, p)`` (all ranks call it with
     the full network and input, and the full state or their block's own, as a previous
@@ -153,8 +154,6 @@ def simulate(part: Partition, v, g, x, drive, p, *, refractory=None, adaptation=
 
     if not x.is_cuda:
         raise RuntimeError("wiretorch_b200 runs on CUDA tensors only (no CPU path)")
-    if drive.gates:
-        raise NotImplementedError("a partitioned run is ungated")
     n0, n1 = part.n0, part.n1
     key = (id(drive), id(p), part.rank, part.P, x.shape[0], x.shape[2])
     cached = _LOCAL.get(key)
@@ -167,8 +166,9 @@ def simulate(part: Partition, v, g, x, drive, p, *, refractory=None, adaptation=
     _plan.fold(plan, d_loc.scale)
     local = v.shape[1] == n1 - n0 != part.N  # the block's own state (a previous call's Run)
     cut = (lambda t: t) if local else (lambda t: None if t is None else t[:, n0:n1])  # noqa: E731
-    v_k, g_k, counter, g_a, _ = engine._prepare_state(plan, cut(v), cut(g), cut(refractory), None,
-                                                      cut(adaptation), p_loc)  # fmt: skip
+    # the gating state stays whole: every rank steps every source's gates alike
+    v_k, g_k, counter, g_a, gating_k = engine._prepare_state(plan, cut(v), cut(g), cut(refractory), gating,
+                                                             cut(adaptation), p_loc)  # fmt: skip
     # All ranks' kernels start together (their exchange waits are bounded), and none
     # starts before every rank's previous call has finished reading the shared words.
     import torch.distributed as dist
@@ -176,5 +176,5 @@ def simulate(part: Partition, v, g, x, drive, p, *, refractory=None, adaptation=
     torch.cuda.synchronize()
     dist.barrier(group=part.group)
     with torch.no_grad():
-        out = engine.run_forward(plan, p_loc, x.detach().float(), v_k, g_k, counter, g_a, None, part=part)
-    return engine._run(plan, out, v_k, g_k, counter, g_a, None, p_loc, False, refractory)
+        out = engine.run_forward(plan, p_loc, x.detach().float(), v_k, g_k, counter, g_a, gating_k, part=part)
+    return engine._run(plan, out, v_k, g_k, counter, g_a, gating_k, p_loc, False, refractory)
