@@ -76,8 +76,8 @@ def compare(engine_sim, net, drive, p, x, v, g, kw, window=10, margin=1e-3, v_at
         assert err.max(initial=-1.0) <= 0, f"window {w}: conductances differ by {np.abs(gk[ok]-ref[ok]).max():.2e}"
         if "gating" in kw and run.gating is not None:
             gt = run.gating.detach().cpu().numpy()
-            ref = states["gating"][w + 1]
-            dgt = np.abs(gt[ok] - ref[ok]).max(initial=0.0)
+            ref_gt = states["gating"][w + 1]
+            dgt = np.abs(gt[ok] - ref_gt[ok]).max(initial=0.0)
             assert dgt <= g_atol + g_rtol, f"window {w}: gating state differs by {dgt:.2e}"
         worst_dv = max(worst_dv, float(dv))
         worst_dg = max(worst_dg, float(np.abs(gk[ok] - ref[ok]).max(initial=0.0)))
