@@ -37,9 +37,19 @@ def oracle_windows(net, x, v, g, kw, window):
     return states, np.concatenate(spikes, 1), np.concatenate(v_track, 1)
 
 
+def _pooled(g, pools):
+    """``(B, N, 2, S)`` conductances summed over each pool's member types."""
+    if not pools:
+        return g
+    return np.stack([g[..., list(m)].sum(-1) for m in pools], -1)
+
+
 def compare(engine_sim, net, drive, p, x, v, g, kw, window=10, margin=1e-3, v_atol=2e-4,
-            g_rtol=1e-5, g_atol=1e-6):  # fmt: skip
+            g_rtol=1e-5, g_atol=1e-6, pools=None):  # fmt: skip
     """Lockstep of ``engine_sim(v, g, x_window, kw) -> Run`` against the oracle.
+
+    ``pools``: the engine's pooled channels (lists of synapse types), whose state holds
+    each pool's sum at its first member; the conductances are then compared pool by pool.
 
     Returns ``(excused, trial_windows, worst_dv, worst_dg)``; raises AssertionError on a
     flip away from threshold or a trace outside tolerance."""
@@ -70,8 +80,8 @@ def compare(engine_sim, net, drive, p, x, v, g, kw, window=10, margin=1e-3, v_at
         else:  # an engine without tracking: the voltages the window leaves
             dv = np.abs(run.v.detach().cpu().numpy()[ok] - states["v"][w + 1][ok]).max(initial=0.0)
         assert dv <= v_atol, f"window {w}: voltage differs by {dv:.2e} mV"
-        gk = run.syn.detach().cpu().numpy()
-        ref = states["g"][w + 1]
+        gk = _pooled(run.syn.detach().cpu().numpy(), pools)
+        ref = _pooled(states["g"][w + 1], pools)
         err = np.abs(gk[ok] - ref[ok]) - (g_atol + g_rtol * np.abs(ref[ok]))
         assert err.max(initial=-1.0) <= 0, f"window {w}: conductances differ by {np.abs(gk[ok]-ref[ok]).max():.2e}"
         if "gating" in kw and run.gating is not None:

@@ -63,7 +63,12 @@ def test_c5_model_lockstep_against_oracle(pool):
     x = cfg.inputs(seed=3)
     v, g, kw = cfg.state()
     net = oracle.Network(cfg.drive, cfg.p, cfg.B, cfg.n_in)
-    excused, windows, dv, dg = lockstep.compare(_sim(cfg.drive, cfg.p, pool), net, cfg.drive, cfg.p, x, v, g, kw)
+    # pooled: the excitatory and the input AMPA types share one channel
+    ch = engine.get_plan(cfg.drive, cfg.p, cfg.B, cfg.n_in, x.device, pool=pool).ch
+    assert ch.pooled == pool
+    pools = [list(m) for m in ch.member] if ch.pooled else None
+    excused, windows, dv, dg = lockstep.compare(_sim(cfg.drive, cfg.p, pool), net, cfg.drive, cfg.p, x, v, g, kw,
+                                                pools=pools)  # fmt: skip
     assert excused <= 0.01 * windows, f"{excused} near-threshold flips in {windows} trial-windows"
     with torch.no_grad():
         run = engine.simulate(v, g, x, cfg.drive, cfg.p, **kw)
