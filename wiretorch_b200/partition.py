@@ -157,12 +157,17 @@ def simulate(part: Partition, v, g, x, drive, p, *, refractory=None, gating=None
     n0, n1 = part.n0, part.n1
     key = (id(drive), id(p), part.rank, part.P, x.shape[0], x.shape[2])
     cached = _LOCAL.get(key)
-    if cached is None:
+    if cached is None or cached["drive"] is not drive or cached["p"] is not p:
         d_loc, p_loc = local_network(drive, p, n0, n1)
         pool_ = engine.POOL_SYNAPSES if pool is None else pool
         plan = _plan.build(d_loc, p_loc, x.shape[0], x.shape[2], x.device, pool=pool_, n_src=part.N)
-        cached = _LOCAL[key] = (d_loc, p_loc, plan)
-    d_loc, p_loc, plan = cached
+        # the network objects are held, so that their ids cannot pass to others
+        cached = _LOCAL[key] = {"drive": drive, "p": p, "local": (d_loc, p_loc, plan),
+                                "scale": drive.scale, "version": drive.scale._version}  # fmt: skip
+    d_loc, p_loc, plan = cached["local"]
+    if cached["scale"] is not drive.scale or cached["version"] != drive.scale._version:
+        d_loc.scale = drive.scale.detach()[:, n0:n1].contiguous()  # a new per-target scale
+        cached["scale"], cached["version"] = drive.scale, drive.scale._version
     _plan.fold(plan, d_loc.scale)
     local = v.shape[1] == n1 - n0 != part.N  # the block's own state (a previous call's Run)
     cut = (lambda t: t) if local else (lambda t: None if t is None else t[:, n0:n1])  # noqa: E731

@@ -437,6 +437,10 @@ def fold(plan: Plan, scale: torch.Tensor, p=None) -> None:
     word with the bits of ``w * scale[k, col] * jf[k, c] * 2^s_c`` — the
     ``wt_fold_weights`` kernel on CUDA (torch on the CPU, for the tests of the tables)."""
     t = plan.tensors
+    src = scale
+    if (p is None and "edge_cw" in t and t.get("_scale_src") is src
+            and t.get("_scale_version") == src._version):  # fmt: skip
+        return  # the same scale tensor, unchanged since the last fold: the edges hold it
     scale = scale.detach().to(plan.device, torch.float32).contiguous()
     if plan.fx_scale is None:
         _choose_fixed_point(plan, scale)
@@ -463,6 +467,9 @@ def fold(plan: Plan, scale: torch.Tensor, p=None) -> None:
     _lib.check(rc, "wt_fold_weights")
     _lib.count_launches(1)
     plan.tensors["_scale"] = scale  # alive until the kernel has read it
+    # held, so that its identity cannot pass to another tensor; its version counter
+    # shows an in-place change
+    t["_scale_src"], t["_scale_version"] = src, src._version
 
 
 def edge_weights(plan: Plan) -> torch.Tensor:

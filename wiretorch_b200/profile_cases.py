@@ -3,8 +3,9 @@
 ``python -m wiretorch_b200.profile_cases c2-active``: C2 (64 trials, pooled channels) run
 450 steps from rest, then one 20-step call from that state with saving for the backward
 pass, as in training. ``python -m wiretorch_b200.profile_cases c3-small``: C3 with 128
-trials, 200 steps, then one 10-step call from that state. In both the second launch is
-the one to capture (``-s 1 -c 1``).
+trials, 200 steps, then one 10-step call from that state. ``c5-small``: C5 at 250,000
+neurons (4 trials, gated, pooled), 300 steps from rest, then one 20-step call. In all
+the second launch of the kernel is the one to capture (``-s 1 -c 1``).
 """
 
 from __future__ import annotations
@@ -45,7 +46,22 @@ def c3_small():
     print(f"c3-small: {float(run2.output.sum()):.0f} spikes in 10 steps")
 
 
-CASES = {"c2-active": c2_active, "c3-small": c3_small}
+def c5_small():
+    from wiretorch_b200 import configs, engine
+
+    # C5 at a quarter of the neurons (same out-degree, ~250M edges, ~3 GB of tables)
+    cfg = configs.c5(B=4, T=320, device="cuda", N=250_000, lam=0.05 * 4 ** (1 / 3))
+    engine.POOL_SYNAPSES = True
+    x = cfg.inputs(T=320, seed=1)
+    v, g, kw = cfg.state()
+    with torch.no_grad():
+        run = engine.simulate(v, g, x[:, :300].contiguous(), cfg.drive, cfg.p, **kw)
+        run2 = engine.simulate(run.v, run.syn, x[:, 300:].contiguous(), cfg.drive, cfg.p, **cfg.carried(run))
+    torch.cuda.synchronize()
+    print(f"c5-small: {float(run2.output.sum()) / 20:.0f} spikes per step, {cfg.extra['edges']} edges")
+
+
+CASES = {"c2-active": c2_active, "c3-small": c3_small, "c5-small": c5_small}
 
 if __name__ == "__main__":
     CASES[sys.argv[1]]()
