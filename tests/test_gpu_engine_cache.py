@@ -34,3 +34,24 @@ def test_fold_is_kept_while_the_scale_is_unchanged():
         _lib.TIMER = None
     assert not torch.equal(r1.v, r3.v)  # the new scale took effect
     assert torch.equal(r3.output, r4.output) and torch.equal(r3.v, r4.v)
+
+
+def test_the_callers_state_is_not_written():
+    """The kernels write the state in place, into copies: the caller's tensors (here
+    ``(B, N, 2, S)`` views of ``(B, 2, S, N)`` storage, the kernel's own layout) keep
+    their values, and a second call from them repeats the first."""
+    from wiretorch_b200 import configs
+
+    cfg = configs.c5(B=2, T=80, device="cuda", N=2000, mean_degree=200.0, lam=0.05 * 500 ** (1 / 3),
+                     w_e=6.0, w_in=30.0)  # fmt: skip
+    x = cfg.inputs(seed=2)
+    v, g, kw = cfg.state()
+    g.add_(0.01)  # a non-trivial state in the kernel's layout
+    before = (v.clone(), g.clone(), {k: t.clone() for k, t in kw.items()})
+    with torch.no_grad():
+        r1 = engine.simulate(v, g, x, cfg.drive, cfg.p, **kw)
+        r2 = engine.simulate(v, g, x, cfg.drive, cfg.p, **kw)
+    assert torch.equal(v, before[0]) and torch.equal(g, before[1])
+    assert all(torch.equal(kw[k], before[2][k]) for k in kw)
+    assert float(r1.output.sum()) > 0
+    assert torch.equal(r1.output, r2.output) and torch.equal(r1.v, r2.v) and torch.equal(r1.gating, r2.gating)

@@ -83,7 +83,9 @@ def _internal_g(plan, g):
     if plan.ch.pooled:
         parts = [out[:, :, m].sum(2) for m in plan.ch.member]
         return torch.stack(parts, 2).contiguous()
-    return out.contiguous()
+    # always a copy: the kernel writes the state in place, and a caller's (B, N, 2, S)
+    # view of (B, 2, S, N) storage would otherwise be that very memory
+    return out.clone(memory_format=torch.contiguous_format)
 
 
 def _external_g(plan, g):

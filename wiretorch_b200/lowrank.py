@@ -198,7 +198,7 @@ def simulate(v, g, x, drive, p, *, refractory=None, gating=None, adaptation=None
     net.made = bits
 
     v_k = v.detach().to(dev, torch.float32).contiguous().clone()
-    g_k = g.detach().to(dev, torch.float32).permute(0, 2, 3, 1).contiguous()
+    g_k = g.detach().to(dev, torch.float32).permute(0, 2, 3, 1).clone(memory_format=torch.contiguous_format)
     counter = (torch.zeros((B, N), dtype=torch.int32, device=dev) if refractory is None
                else refractory.detach().to(dev, torch.int32).contiguous().clone())  # fmt: skip
     xs = x.detach().float().contiguous()
