@@ -420,16 +420,35 @@ def segments(plan: Plan) -> list:
 
 def edge_pathway(plan: Plan) -> torch.Tensor:
     """The pathway of every edge (int64)."""
+    e = torch.zeros(max(plan.n_edges, 1), dtype=torch.int64, device=plan.device)
+    for pos, path in _edge_runs(plan):
+        e[pos] = path
+    return e
+
+
+def _edge_runs(plan: Plan, max_edges: int = 1 << 26):
+    """``(positions, pathways)`` (int64) of the edges of consecutive runs of chunks, about
+    ``max_edges`` edges a run: bounded temporaries, whatever the network's size."""
     t = plan.tensors
-    if "edge_path" not in t:
-        e = torch.zeros(max(plan.n_edges, 1), dtype=torch.int64, device=plan.device)
-        if plan.n_chunks:
-            lens = t["chunk_len"].to(torch.int64)
-            idx = torch.repeat_interleave(torch.arange(plan.n_chunks, device=plan.device), lens)
-            within = torch.arange(idx.numel(), device=plan.device) - (torch.cumsum(lens, 0) - lens)[idx]
-            e[t["chunk_begin"][idx] + within] = t["chunk_path"][idx].to(torch.int64)
-        t["edge_path"] = e
-    return t["edge_path"]
+    if not plan.n_chunks:
+        return
+    lens_all = t["chunk_len"].to(torch.int64)
+    ends = torch.cumsum(lens_all, 0)
+    # chunk boundaries of the runs: every chunk holds at most WT_CHUNK_EDGES edges
+    cuts = torch.searchsorted(ends, torch.arange(max_edges, int(ends[-1]) + max_edges, max_edges,
+                                                 device=ends.device), right=True).tolist()  # fmt: skip
+    q0 = 0
+    for q1 in cuts:
+        q1 = min(max(q1, q0 + 1), plan.n_chunks)
+        if q1 <= q0:
+            continue
+        lens = lens_all[q0:q1]
+        idx = torch.repeat_interleave(torch.arange(q0, q1, device=plan.device), lens)
+        within = torch.arange(idx.numel(), device=plan.device) - (torch.cumsum(lens, 0) - lens)[idx - q0]
+        yield t["chunk_begin"][idx] + within, t["chunk_path"][idx].to(torch.int64)
+        q0 = q1
+        if q0 >= plan.n_chunks:
+            break
 
 
 def fold(plan: Plan, scale: torch.Tensor, p=None) -> None:
@@ -486,12 +505,12 @@ def _choose_fixed_point(plan: Plan, scale: torch.Tensor) -> None:
         plan.fx_exp = [0] * plan.ch.C
         plan.fx_scale = torch.ones(plan.ch.C, device=plan.device)
         return
-    k = edge_pathway(plan)
-    packed = t["edge_col"].to(torch.int64) & 0xFFFFFFFF
-    col, c = packed & 0x7FFFFFF, packed >> 27
-    w = t["w_raw"] * scale[k, col] * t["jf"][k, c]
     bound = torch.zeros(plan.ch.C * plan.N, device=plan.device, dtype=torch.float64)
-    bound.index_add_(0, c * plan.N + col, w.abs().double())
+    for pos, k in _edge_runs(plan):
+        packed = t["edge_col"][pos].to(torch.int64) & 0xFFFFFFFF
+        col, c = packed & 0x7FFFFFF, packed >> 27
+        w = t["w_raw"][pos] * scale[k, col] * t["jf"][k, c]
+        bound.index_add_(0, c * plan.N + col, w.abs().double())
     bound = bound.view(plan.ch.C, plan.N).amax(1).cpu()
     exps = []
     for b in bound.tolist():
