@@ -115,3 +115,21 @@ def test_chunks_split_long_rows():
     assert plan.n_chunks == -(-N // CHUNK_EDGES) + 1
     lens = t["chunk_len"][t["slot_chunk"][0] : t["slot_chunk"][1]]
     assert int(lens.sum()) == N and int(lens.max()) <= CHUNK_EDGES
+
+
+@pytest.mark.parametrize("max_edges", [1, 7, 200, 1 << 26])
+def test_edge_runs_cover_every_edge_once(max_edges):
+    """The bounded runs of edges (used for the fixed-point bounds) visit every edge once,
+    with its chunk's pathway, whatever the run size."""
+    drive, p, d, meta = golden_io.load("recurrent_frozen")
+    plan = P.build(drive, p, 2, d["in.x"].shape[2], "cpu", pool=False)
+    seen = torch.full((plan.n_edges,), -1, dtype=torch.int64)
+    count = torch.zeros(plan.n_edges, dtype=torch.int64)
+    for pos, path in P._edge_runs(plan, max_edges=max_edges):
+        seen[pos] = path
+        count.index_add_(0, pos, torch.ones_like(pos))
+    assert bool((count == 1).all())
+    t = plan.tensors
+    for q in range(plan.n_chunks):
+        b, n = int(t["chunk_begin"][q]), int(t["chunk_len"][q])
+        assert bool((seen[b : b + n] == int(t["chunk_path"][q])).all())
