@@ -522,12 +522,26 @@ __global__ void __launch_bounds__(warps_of<S, FEAT>() * 32, 1) forward_kernel(co
             if (++wr == D) wr = 0;
         }
 
+        // ---------------- the input columns of the next step ----------------
+        if (emit_next) {
+            for (long long base = warp0; base < itemsI; base += nthreads) {
+                const unsigned i = (unsigned)(base + lane);
+                const int b = (int)(i / (unsigned)Ip), c = (int)(i - (unsigned)b * Ip);
+                const bool valid = c < n_in;
+                const float xv = valid ? run.x[((size_t)b * run.T_total + t_abs + 1) * n_in + c] : 0.0f;
+                emit_input(t + 1, valid, b, Nsrc + c, xv);
+            }
+        }
+
         // ---------------- scatter the events of step t into X_t ----------------
         // Step t's events were emitted during step t - 1 and X_t's buffer emptied then.
         // The events go round the warps; a warp reads up to 32 of its events at once (one
         // per lane, from L2: other blocks wrote them), then walks them one by one, loading
         // the next event's edges before it issues the current one's reductions.
-        {
+        // Scatter and update of a step touch different buffers (X_t and the events of t;
+        // X_{t-1} and the events of t + 1), so half the warps of a block scatter before
+        // their items and half after: the reductions drain while the other half computes.
+        auto scatter = [&]() {
             const long long count = min((long long)*reinterpret_cast<volatile unsigned *>(&ws.ev_count[t]),
                                         (long long)ws.ev_cap);  // never above: one event per (trial, chunk)
             const WtEvent *evs = ws.ev + (size_t)(t & 1) * ws.ev_cap;
@@ -578,7 +592,9 @@ __global__ void __launch_bounds__(warps_of<S, FEAT>() * 32, 1) forward_kernel(co
                     }
                 }
             }
-        }
+        };
+        const bool scatter_late = (threadIdx.x >> 5) & 1;
+        if (!scatter_late) scatter();
 
         // ---------------- the neurons: step t, and the spikes of step t + 1 ----------------
         Cursor q = start;
@@ -754,16 +770,7 @@ __global__ void __launch_bounds__(warps_of<S, FEAT>() * 32, 1) forward_kernel(co
             rp += ks * 32;
         }
         cp_async_wait(0);  // the last (empty) groups
-        // ---------------- the input columns of the next step ----------------
-        if (emit_next) {
-            for (long long base = warp0; base < itemsI; base += nthreads) {
-                const unsigned i = (unsigned)(base + lane);
-                const int b = (int)(i / (unsigned)Ip), c = (int)(i - (unsigned)b * Ip);
-                const bool valid = c < n_in;
-                const float xv = valid ? run.x[((size_t)b * run.T_total + t_abs + 1) * n_in + c] : 0.0f;
-                emit_input(t + 1, valid, b, Nsrc + c, xv);
-            }
-        }
+        if (scatter_late) scatter();
         if (PART) __threadfence_system();
         if (!bar.sync(ws.err)) return;
         if (PART && emit_next && !exchange(t + 1)) return;
