@@ -95,6 +95,11 @@ typedef struct {
     /* sources that are neurons: N, or in a neuron-partitioned run every rank's neurons
      * (the N targets here are this rank's; input column i is source N_src + i) */
     int32_t N_src;
+    /* optional, gated runs (N_src + n_in, 2): per source its gate and row when it owns at
+     * most one slot (gate -1: that slot is ungated or there is none), gate -2 when it
+     * owns several. With it the forward kernel steps a source's gating state without
+     * walking its slots; NULL: every gated source walks its slots. */
+    const int32_t *src_gate;
 } WtNet;
 
 /* Buffers of one forward run of T steps (outputs indexed by step t0 + t of a chunk of

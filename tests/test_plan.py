@@ -133,3 +133,36 @@ def test_edge_runs_cover_every_edge_once(max_edges):
     for q in range(plan.n_chunks):
         b, n = int(t["chunk_begin"][q]), int(t["chunk_len"][q])
         assert bool((seen[b : b + n] == int(t["chunk_path"][q])).all())
+
+
+def test_source_gate_table_resolves_single_slots():
+    """``src_gate``: a source with one slot carries that slot's gate and row; a source
+    with several carries -2; one without slots, -1 (the C5 model at 2,000 neurons, and
+    the same with 100 of its excitatory sources in a second gated pathway)."""
+    from wiretorch_b200 import configs
+    from wiretorch_b200.types import Gate, SparseRows
+
+    cfg = configs.c5(B=2, T=10, device="cpu", N=2000, mean_degree=100.0, lam=0.2)
+    d = cfg.drive
+    rows_e, W_e = d.recurrent[0]
+    n = 100
+    end = int(W_e.row_ptr[n])
+    d.recurrent = [*d.recurrent, (rows_e[:n].clone(), SparseRows(W_e.row_ptr[: n + 1], W_e.cols[:end],
+                                                                 W_e.values[:end], W_e.n_targets))]  # fmt: skip
+    d.made = torch.cat([d.made[:2], d.made[:1], d.made[2:]])
+    d.scale = torch.cat([d.scale[:2], d.scale[:1], d.scale[2:]])
+    R0 = max(g.start + g.width for g in d.gates if g is not None)
+    d.gates = [d.gates[0], d.gates[1], Gate(d.gates[0].params, True, True, R0, n), None]
+    plan = P.build(d, cfg.p, cfg.B, cfg.n_in, "cpu")
+    t = plan.tensors
+    table = t["src_gate"].numpy()
+    src_slot, slot_gate, slot_row = t["src_slot"].numpy(), t["slot_gate"].numpy(), t["slot_row"].numpy()
+    assert table.shape == (cfg.N + cfg.n_in, 2)
+    for j in range(cfg.N + cfg.n_in):
+        s0, ns = src_slot[j], src_slot[j + 1] - src_slot[j]
+        if ns == 1:
+            assert tuple(table[j]) == (slot_gate[s0], slot_row[s0])
+        else:
+            assert table[j, 0] == (-2 if ns > 1 else -1)
+    assert (table[:, 0] == -2).sum() == n
+    assert (table[cfg.N :, 0] == -1).all()  # the input columns are ungated

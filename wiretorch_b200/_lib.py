@@ -48,6 +48,7 @@ class WtNet(C.Structure):
         ("n_slots", C.c_int32), ("n_chunks", C.c_int32), ("n_rec_edges", C.c_int64),
         ("slot_gate", P), ("slot_row", P), ("gate_params", P), ("gate_cols", P),
         ("R", C.c_int32), ("R_f", C.c_int32), ("N_src", C.c_int32),
+        ("src_gate", P),
     ]  # fmt: skip
 
 

@@ -79,36 +79,89 @@ __device__ __forceinline__ void cp_async_wait(int pending) {
     }
 }
 
-// Presynaptic gating of one slot for one trial (network.py:186-223): steps the state
-// with the source's spike (or input) `s` and returns the factor of its input.
-__device__ float gate_step(const WtNet &net, float *gating_b, int gate, int row, float s) {
-    const float *prm = net.gate_params + 5 * gate;
-    const int u_col = net.gate_cols[4 * gate + 0];
-    const int n = net.gate_cols[4 * gate + 1];
-    const int sat_col = net.gate_cols[4 * gate + 2];
+// One step of a slot's gating state for one trial (network.py:186-223) with the source's
+// spike (or input) `s`: release probability u and resources x (short-term plasticity,
+// `stp`), bound fraction a (receptor saturation, `sat`), in place. Returns the factor of
+// the source's input. prm: the gate's (c, d, U, d_D, d_F).
+__device__ __forceinline__ float gate_math(const float *prm, bool stp, bool sat, float &u, float &x, float &a,
+                                           float s) {
     float f = 1.0f;
-    bool have = false;
-    if (u_col >= 0) {
+    if (stp) {
         const float U = prm[2], d_D = prm[3], d_F = prm[4];
-        float u = gating_b[u_col + row], x = gating_b[u_col + n + row];
         x = 1.0f - (1.0f - x) * d_D;
         u = U + (u - U) * d_F;
         const float r = u * x;
         f = r / U;
-        have = true;
         x = x - s * r;
         u = u + s * U * (1.0f - u);
+    }
+    if (sat) {
+        const float c = prm[0], d = prm[1];
+        const float g = a * d;
+        const float closed = 1.0f - g;
+        f = stp ? fminf(c * f * closed, closed) : c * closed;
+        a = fminf(g + s * f, 1.0f);
+    }
+    return f;
+}
+
+// Presynaptic gating of one slot for one trial: steps the state in the trial's gating
+// row with `s` and returns the factor.
+__device__ float gate_step(const WtNet &net, float *gating_b, int gate, int row, float s) {
+    const int u_col = net.gate_cols[4 * gate + 0];
+    const int n = net.gate_cols[4 * gate + 1];
+    const int sat_col = net.gate_cols[4 * gate + 2];
+    float u = 0.0f, x = 0.0f, a = 0.0f;
+    if (u_col >= 0) {
+        u = gating_b[u_col + row];
+        x = gating_b[u_col + n + row];
+    }
+    if (sat_col >= 0) a = gating_b[sat_col + row];
+    const float f = gate_math(net.gate_params + 5 * gate, u_col >= 0, sat_col >= 0, u, x, a, s);
+    if (u_col >= 0) {
         gating_b[u_col + row] = u;
         gating_b[u_col + n + row] = x;
     }
-    if (sat_col >= 0) {
-        const float c = prm[0], d = prm[1];
-        const float g = gating_b[sat_col + row] * d;
-        const float closed = 1.0f - g;
-        f = have ? fminf(c * f * closed, closed) : c * closed;
-        gating_b[sat_col + row] = fminf(g + s * f, 1.0f);
-    }
+    if (sat_col >= 0) gating_b[sat_col + row] = a;
     return f;
+}
+
+// The gating of a source that owns at most one slot (WtNet.src_gate), resolved once:
+// its gate (-1: none, -2: several slots, walked by `emit`), the columns of its state in
+// a trial's gating row (-1: not kept) and of its saved factor, the gate's parameters.
+struct SrcGate {
+    int gate, u_off, x_off, a_off, f_off;
+    float prm[5];
+};
+
+__device__ __forceinline__ SrcGate src_gate_of(const WtNet &net, int j) {
+    SrcGate G;
+    const int2 gr = reinterpret_cast<const int2 *>(net.src_gate)[j];
+    G.gate = gr.x;
+    G.u_off = G.x_off = G.a_off = G.f_off = -1;
+#pragma unroll
+    for (int i = 0; i < 5; i++) G.prm[i] = 0.0f;
+    if (gr.x >= 0) {
+        const int4 cl = reinterpret_cast<const int4 *>(net.gate_cols)[gr.x];
+        if (cl.x >= 0) {
+            G.u_off = cl.x + gr.y;
+            G.x_off = cl.x + cl.y + gr.y;
+        }
+        if (cl.z >= 0) G.a_off = cl.z + gr.y;
+        G.f_off = cl.w + gr.y;
+#pragma unroll
+        for (int i = 0; i < 5; i++) G.prm[i] = net.gate_params[5 * gr.x + i];
+    }
+    return G;
+}
+
+__device__ __forceinline__ SrcGate no_gate() {
+    SrcGate G;
+    G.gate = -1;
+    G.u_off = G.x_off = G.a_off = G.f_off = -1;
+#pragma unroll
+    for (int i = 0; i < 5; i++) G.prm[i] = 0.0f;
+    return G;
 }
 
 // All 32 lanes call this together. Lane proposes source `j` of trial `b` whose spike
@@ -378,8 +431,46 @@ __global__ void __launch_bounds__(warps_of<S, FEAT>() * 32, 1) forward_kernel(co
         else
             emit_fast(net, ws, step, valid && value != 0.0f, b, k.c0, k.cnt, value, lane);
     };
+    // A gated source j through its resolved gating (src_gate): the state of its one slot
+    // stepped in place, then its events emitted with the factor; a source with several
+    // slots in the warp sends the warp through `emit`.
+    auto emit_src = [&](int step, bool valid, int b, int j, float value) {
+        const SrcGate G = valid ? src_gate_of(net, j) : no_gate();
+        if (__any_sync(kFull, G.gate == -2)) {
+            emit(net, run, ws, step, valid, b, j, value, true, lane);
+            return;
+        }
+        float amp = value;
+        if (valid && G.gate >= 0) {
+            float *gb = run.gating + (size_t)b * net.R;
+            float u = 0.0f, x = 0.0f, a = 0.0f;
+            if (G.u_off >= 0) {
+                u = gb[G.u_off];
+                x = gb[G.x_off];
+            }
+            if (G.a_off >= 0) a = gb[G.a_off];
+            const float f = gate_math(G.prm, G.u_off >= 0, G.a_off >= 0, u, x, a, value);
+            if (G.u_off >= 0) {
+                gb[G.u_off] = u;
+                gb[G.x_off] = x;
+            }
+            if (G.a_off >= 0) gb[G.a_off] = a;
+            if (SAVE) run.f_saved[((size_t)b * run.T_total + run.t0 + step) * net.R_f + G.f_off] = f;
+            amp = value * f;
+        }
+        const bool on = valid && value != 0.0f;
+        int c0 = 0, cnt = 0;
+        if (on) {
+            c0 = net.src_chunk[j];
+            cnt = net.src_chunk[j + 1] - c0;
+        }
+        emit_fast(net, ws, step, on, b, c0, cnt, amp, lane);
+    };
+    const bool GSRC = gated && net.src_gate != nullptr;
     auto emit_input = [&](int step, bool valid, int b, int j, float value) {
-        if (gated) {
+        if (GSRC) {
+            emit_src(step, valid, b, j, value);
+        } else if (gated) {
             emit(net, run, ws, step, valid, b, j, value, true, lane);
         } else {
             const bool on = valid && value != 0.0f;
@@ -432,7 +523,10 @@ __global__ void __launch_bounds__(warps_of<S, FEAT>() * 32, 1) forward_kernel(co
             const int j = w * 32 + lane;
             const bool on = (word >> lane) & 1u;
             if (gated) {  // every source's gates step, on every rank alike (replicated state)
-                emit(net, run, ws, step, j < Nsrc, b, j, on ? 1.0f : 0.0f, true, lane);
+                if (GSRC)
+                    emit_src(step, j < Nsrc, b, j, on ? 1.0f : 0.0f);
+                else
+                    emit(net, run, ws, step, j < Nsrc, b, j, on ? 1.0f : 0.0f, true, lane);
                 continue;
             }
             int c0 = 0, cnt = 0;
@@ -600,6 +694,11 @@ __global__ void __launch_bounds__(warps_of<S, FEAT>() * 32, 1) forward_kernel(co
         Cursor q = start;
         int g_k = -1, rd = 0;
         NeuronConsts k{};
+        // gated runs with resolved gating: the group's sources' gates (kg), and whether
+        // one of them owns several slots (then the warp walks them in `emit`)
+        const bool GN = GSRC && !PART;
+        SrcGate kg = no_gate();
+        bool gmulti = false;
         float *rp = wsm + lane;
         const size_t tN = (size_t)t_abs * N;
         for (int j = 0; j < nitems; j++) {
@@ -609,6 +708,10 @@ __global__ void __launch_bounds__(warps_of<S, FEAT>() * 32, 1) forward_kernel(co
             if (q.g != g_k) {
                 k = consts_of(n);
                 g_k = q.g;
+                if (GN) {
+                    kg = valid ? src_gate_of(net, n) : no_gate();
+                    gmulti = __any_sync(kFull, kg.gate == -2);
+                }
             }
             // item j's slot: wait for its copies (this lane's, then the warp's)
             cp_async_wait(D - 1);
@@ -637,6 +740,18 @@ __global__ void __launch_bounds__(warps_of<S, FEAT>() * 32, 1) forward_kernel(co
             qi.next(B, N, Np, TN);
             if (++wr == D) wr = 0;
             if (++rd == D) rd = 0;
+            // the gating state the spike of step t + 1 steps: loaded now, used after the
+            // membrane update
+            const bool gstep = GN && emit_next && !gmulti && valid && kg.gate >= 0;
+            float *gb = run.gating + (size_t)b * net.R;
+            float gu = 0.0f, gx = 0.0f, gsa = 0.0f;
+            if (gstep) {
+                if (kg.u_off >= 0) {
+                    gu = gb[kg.u_off];
+                    gx = gb[kg.x_off];
+                }
+                if (kg.a_off >= 0) gsa = gb[kg.a_off];
+            }
 
             const size_t o = q.bN + n;
             const size_t out = q.bTN + tN + n;
@@ -761,10 +876,24 @@ __global__ void __launch_bounds__(warps_of<S, FEAT>() * 32, 1) forward_kernel(co
                 }
             }
             if (emit_next) {
-                if (PART)
+                if (PART) {
                     publish(t + 1, b, q.g, s_next);
-                else
+                } else if (GN && !gmulti) {
+                    float amp = s_next;
+                    if (gstep) {
+                        const float f = gate_math(kg.prm, kg.u_off >= 0, kg.a_off >= 0, gu, gx, gsa, s_next);
+                        if (kg.u_off >= 0) {
+                            gb[kg.u_off] = gu;
+                            gb[kg.x_off] = gx;
+                        }
+                        if (kg.a_off >= 0) gb[kg.a_off] = gsa;
+                        if (SAVE) run.f_saved[((size_t)b * run.T_total + t_abs + 1) * net.R_f + kg.f_off] = f;
+                        amp = s_next * f;
+                    }
+                    emit_fast(net, ws, t + 1, valid && s_next != 0.0f, b, k.c0, k.cnt, amp, lane);
+                } else {
                     emit_neuron(t + 1, valid, b, n, k, s_next);
+                }
             }
             q.next(B, N, Np, TN);
             rp += ks * 32;

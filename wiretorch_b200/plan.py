@@ -250,6 +250,8 @@ class Plan:
         if self.gated:
             n.slot_gate, n.slot_row = t["slot_gate"].data_ptr(), t["slot_row"].data_ptr()
             n.gate_params, n.gate_cols = t["gate_params"].data_ptr(), t["gate_cols"].data_ptr()
+            if "src_gate" in t:  # without it the kernel walks every gated source's slots
+                n.src_gate = t["src_gate"].data_ptr()
         n.R, n.R_f = self.R, self.R_f
         n.N_src = self.N_src or self.N
         return n
@@ -384,6 +386,16 @@ def build(drive, p, B: int, n_in: int, device, pool: bool = False, n_src: int | 
         t["gate_params"] = torch.stack(params).contiguous()
         t["gate_cols"] = torch.tensor(cols, dtype=torch.int32, device=device).contiguous()
         plan.R = max(g.start + g.width for g in gates if g is not None)
+        # per source: (gate, row) of its one slot, gate -1 when ungated or slotless,
+        # -2 when it owns several slots
+        n_slots_of = src_slot[1:] - src_slot[:-1]
+        src_gate = torch.full((n_src, 2), -1, dtype=torch.int32, device=device)
+        one = (n_slots_of == 1).nonzero().flatten()
+        first = src_slot[:-1][one]
+        src_gate[one, 0] = t["slot_gate"][first]
+        src_gate[one, 1] = t["slot_row"][first]
+        src_gate[n_slots_of > 1, 0] = -2
+        t["src_gate"] = src_gate.contiguous()
 
     t["src_slot"] = src_slot.to(torch.int32).contiguous()
     t["slot_chunk"] = slot_chunk.to(torch.int32).contiguous()
