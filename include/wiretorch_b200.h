@@ -136,6 +136,14 @@ typedef struct {
     unsigned long long *peer_progress[8];
     int32_t n_ranks, rank, word0;
     uint32_t epoch;
+    /* optional, WT_F_PARTITION with WT_F_GATED when every neuron owns at most one slot
+     * (WtNet.src_gate never -2): the factors of each step's spikes, (2, B,
+     * ceil(N_src / 32) * 32) floats here and on the n_ranks ranks, written by the rank
+     * that owns the neuron (it alone steps that neuron's gating state; the other ranks'
+     * copies of those columns are left as they were). NULL: every rank steps every
+     * source's gates from the spike words. */
+    float *amps;
+    float *peer_amps[8];
 } WtForward;
 
 /* One scatter work item: a chunk of a source's edges, for one trial. */

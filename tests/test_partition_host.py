@@ -82,3 +82,45 @@ def test_sparse_rows_restriction():
     r = torch.repeat_interleave(torch.arange(counts.numel()), counts)
     loc[r, W_loc.cols.long()] = W_loc.values
     assert torch.equal(loc, dense[:, n0:n1])
+
+
+def _gating_rank_main(rank, world, port, result):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        from types import SimpleNamespace
+
+        from wiretorch_b200 import configs
+        from wiretorch_b200 import plan as P
+
+        cfg = configs.c5(B=2, T=4, device="cpu", N=2000, mean_degree=100.0, lam=0.2)
+        n0, n1 = partition.blocks(cfg.N, world)[rank]
+        d_loc, p_loc = partition.local_network(cfg.drive, cfg.p, n0, n1)
+        plan = P.build(d_loc, p_loc, cfg.B, cfg.n_in, "cpu", n_src=cfg.N)
+        assert partition.owner_gates(plan)
+        owner = partition.gating_owners(plan, world)
+        # each depressing synapse's columns (u, then x) belong to the rank of its neuron
+        cuts = [b[0] for b in partition.blocks(cfg.N, world)]
+        for (rows, _), gate in zip(cfg.drive.recurrent, cfg.drive.gates):
+            want = torch.tensor([sum(int(j) >= c for c in cuts[1:]) for j in rows])
+            assert torch.equal(owner[gate.start : gate.start + gate.n], want)
+            assert torch.equal(owner[gate.start + gate.n : gate.start + 2 * gate.n], want)
+        assert int((owner >= 0).sum()) == plan.R
+        # the gathered state takes every column from its owner
+        truth = torch.arange(cfg.B * plan.R, dtype=torch.float32).reshape(cfg.B, plan.R)
+        mine = torch.where(owner == rank, truth, torch.full_like(truth, -1.0))
+        partition._gather_gating(SimpleNamespace(group=None, P=world, rank=rank), plan, mine)
+        result[rank] = bool(torch.equal(mine, truth))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_owner_stepped_gating_gathered_from_the_owners():
+    """Owner-stepped gates (every neuron of the C5 model owns one depressing slot): the
+    column owners follow the blocks, and the gathered state is each owner's."""
+    world = 2
+    ctx = mp.get_context("spawn")
+    manager = ctx.Manager()
+    result = manager.dict()
+    mp.start_processes(_gating_rank_main, args=(world, _free_port(), result), nprocs=world, start_method="spawn")
+    assert dict(result) == {0: True, 1: True}

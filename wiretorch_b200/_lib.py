@@ -63,6 +63,7 @@ class WtForward(C.Structure):
         ("track_b", C.c_int32),
         ("words", P), ("peer_words", P * 8), ("progress", P), ("peer_progress", P * 8),
         ("n_ranks", C.c_int32), ("rank", C.c_int32), ("word0", C.c_int32), ("epoch", C.c_uint32),
+        ("amps", P), ("peer_amps", P * 8),
     ]  # fmt: skip
 
 

@@ -130,6 +130,11 @@ int wt_forward(const WtNet *net, const WtForward *run, const WtWorkspace *ws, vo
             return fail(WT_ERR_ARGS, "bad partition%s");
         for (int r = 0; r < run->n_ranks; r++)
             if (!run->peer_words[r] || !run->peer_progress[r]) return fail(WT_ERR_ARGS, "missing peer buffers%s");
+        if (run->amps) {  // owner-stepped gates
+            if (!(f & WT_F_GATED) || !net->src_gate) return fail(WT_ERR_ARGS, "amplitudes need a gated net with src_gate%s");
+            for (int r = 0; r < run->n_ranks; r++)
+                if (!run->peer_amps[r]) return fail(WT_ERR_ARGS, "missing peer amplitude buffers%s");
+        }
         const int n_src = net->N_src ? net->N_src : net->N;
         if (run->word0 < 0 || (long long)run->word0 * 32 + net->N > ((long long)n_src + 31) / 32 * 32)
             return fail(WT_ERR_ARGS, "this rank's neurons lie outside the sources%s");

@@ -270,16 +270,22 @@ __device__ __forceinline__ float spike_of(float v, float theta, int counter, flo
 }
 
 static_assert(WT_CHUNK_EDGES <= 128, "a chunk's edges take at most four per lane");
-// Feature bits of a specialised kernel: the refractory period and saving for the backward
-// pass known at compile time; everything else (adaptation, Mg block, escape noise,
-// gating, probabilities, tracking, saved input) in the generic variant, tested at run time.
-constexpr int kRef = 1, kSave = 2, kGeneric = 4;
+// Feature bits of a specialised kernel: the refractory period, saving for the backward
+// pass, the Mg block and presynaptic gating known at compile time; everything else
+// (adaptation, escape noise, probabilities, tracking, saved input, partitions) in the
+// generic variant, tested at run time.
+constexpr int kRef = 1, kSave = 2, kGeneric = 4, kMg = 8, kGate = 16;
 
 // Warps per block of the forward kernel (one block per SM): 24 for the specialised
-// kernels of up to four channels (80 registers a thread, as good as no spill), 16 for
-// the others (up to 128 registers).
+// kernels of up to four channels (80 registers a thread, as good as no spill), WT_GATE_WARPS
+// for those with the Mg block or gating, 16 for the others (up to 128 registers).
+#ifndef WT_GATE_WARPS
+#define WT_GATE_WARPS 20
+#endif
 template <int S, int FEAT>
-constexpr int warps_of() { return ((FEAT & kGeneric) == 0 && S <= 4) ? 24 : 16; }
+constexpr int warps_of() {
+    return ((FEAT & kGeneric) == 0 && S <= 4) ? ((FEAT & (kMg | kGate)) ? WT_GATE_WARPS : 24) : 16;
+}
 constexpr int kMaxRing = 4;               // deepest ring of staged items
 
 
@@ -318,9 +324,9 @@ __global__ void __launch_bounds__(warps_of<S, FEAT>() * 32, 1) forward_kernel(co
     const bool REF = GEN ? (flags & WT_F_REFRACTORY) != 0 : (FEAT & kRef) != 0;
     const bool SAVE = GEN ? (flags & WT_F_SAVE) != 0 : (FEAT & kSave) != 0;
     const bool ADAPT = GEN && (flags & WT_F_ADAPT);
-    const bool MG = GEN && (flags & WT_F_MG_BLOCK);
+    const bool MG = GEN ? (flags & WT_F_MG_BLOCK) != 0 : (FEAT & kMg) != 0;
     const bool SAMPLE = GEN && (flags & WT_F_SAMPLE);
-    const bool gated = GEN && (flags & WT_F_GATED);
+    const bool gated = GEN ? (flags & WT_F_GATED) != 0 : (FEAT & kGate) != 0;
     const bool PROB = GEN && (flags & WT_F_PROB);
     const bool TRACK = GEN && (flags & WT_F_TRACK);
     const bool SAVE_IN = GEN && (flags & WT_F_SAVE_INPUT);
@@ -434,6 +440,25 @@ __global__ void __launch_bounds__(warps_of<S, FEAT>() * 32, 1) forward_kernel(co
     // A gated source j through its resolved gating (src_gate): the state of its one slot
     // stepped in place, then its events emitted with the factor; a source with several
     // slots in the warp sends the warp through `emit`.
+    // One step of a resolved gate G (G.gate >= 0) for trial b with the source's value of
+    // `step`; returns the factor.
+    auto step_gate = [&](const SrcGate &G, int step, int b, float value) -> float {
+        float *gb = run.gating + (size_t)b * net.R;
+        float u = 0.0f, x = 0.0f, a = 0.0f;
+        if (G.u_off >= 0) {
+            u = gb[G.u_off];
+            x = gb[G.x_off];
+        }
+        if (G.a_off >= 0) a = gb[G.a_off];
+        const float f = gate_math(G.prm, G.u_off >= 0, G.a_off >= 0, u, x, a, value);
+        if (G.u_off >= 0) {
+            gb[G.u_off] = u;
+            gb[G.x_off] = x;
+        }
+        if (G.a_off >= 0) gb[G.a_off] = a;
+        if (SAVE) run.f_saved[((size_t)b * run.T_total + run.t0 + step) * net.R_f + G.f_off] = f;
+        return f;
+    };
     auto emit_src = [&](int step, bool valid, int b, int j, float value) {
         const SrcGate G = valid ? src_gate_of(net, j) : no_gate();
         if (__any_sync(kFull, G.gate == -2)) {
@@ -441,23 +466,7 @@ __global__ void __launch_bounds__(warps_of<S, FEAT>() * 32, 1) forward_kernel(co
             return;
         }
         float amp = value;
-        if (valid && G.gate >= 0) {
-            float *gb = run.gating + (size_t)b * net.R;
-            float u = 0.0f, x = 0.0f, a = 0.0f;
-            if (G.u_off >= 0) {
-                u = gb[G.u_off];
-                x = gb[G.x_off];
-            }
-            if (G.a_off >= 0) a = gb[G.a_off];
-            const float f = gate_math(G.prm, G.u_off >= 0, G.a_off >= 0, u, x, a, value);
-            if (G.u_off >= 0) {
-                gb[G.u_off] = u;
-                gb[G.x_off] = x;
-            }
-            if (G.a_off >= 0) gb[G.a_off] = a;
-            if (SAVE) run.f_saved[((size_t)b * run.T_total + run.t0 + step) * net.R_f + G.f_off] = f;
-            amp = value * f;
-        }
+        if (valid && G.gate >= 0) amp = value * step_gate(G, step, b, value);
         const bool on = valid && value != 0.0f;
         int c0 = 0, cnt = 0;
         if (on) {
@@ -467,6 +476,19 @@ __global__ void __launch_bounds__(warps_of<S, FEAT>() * 32, 1) forward_kernel(co
         emit_fast(net, ws, step, on, b, c0, cnt, amp, lane);
     };
     const bool GSRC = gated && net.src_gate != nullptr;
+    // Owner-stepped gates: a partitioned gated run whose neurons each own at most one slot
+    // (the host checks, and passes the amplitude buffers only then). The rank that owns a
+    // neuron alone steps its gate and writes its spike's factor into every rank's replica
+    // of the amplitudes (2, B, words_src * 32), beside the spike words; the exchange reads
+    // the factors back instead of stepping every source's gates on every rank.
+    const bool OG = PART && GSRC && run.amps != nullptr;
+    const size_t amp_row = (size_t)words_src * 32;
+    auto publish_amp = [&](int step, int b, int jg, bool on, float amp) {
+        if (on) {
+            const size_t ai = ((size_t)(step & 1) * B + b) * amp_row + jg;
+            for (int r = 0; r < run.n_ranks; r++) run.peer_amps[r][ai] = amp;
+        }
+    };
     auto emit_input = [&](int step, bool valid, int b, int j, float value) {
         if (GSRC) {
             emit_src(step, valid, b, j, value);
@@ -517,24 +539,37 @@ __global__ void __launch_bounds__(warps_of<S, FEAT>() * 32, 1) forward_kernel(co
         }
         if (!bar.sync(ws.err)) return false;
         const uint32_t *wsrc = run.words + (size_t)(step & 1) * B * words_src;
-        for (long long it = gwarp; it < (long long)B * words_src; it += nwarps) {
-            const int b = (int)(it / words_src), w = (int)(it % words_src);
-            const unsigned word = __ldcg(wsrc + it);  // written by the ranks: L2, not L1
-            const int j = w * 32 + lane;
-            const bool on = (word >> lane) & 1u;
-            if (gated) {  // every source's gates step, on every rank alike (replicated state)
-                if (GSRC)
-                    emit_src(step, j < Nsrc, b, j, on ? 1.0f : 0.0f);
-                else
-                    emit(net, run, ws, step, j < Nsrc, b, j, on ? 1.0f : 0.0f, true, lane);
-                continue;
+        const long long n_words = (long long)B * words_src;
+        // a warp takes 32 words at once (one per lane) and walks the ones with a spike;
+        // with replicated gates it walks them all (every source's gates step)
+        for (long long base = gwarp * 32; base < n_words; base += nwarps * 32) {
+            const long long mine = base + lane;
+            const unsigned my_word = mine < n_words ? __ldcg(wsrc + mine) : 0u;  // written by the ranks: L2
+            unsigned todo = __ballot_sync(kFull, (gated && !OG) ? mine < n_words : my_word != 0u);
+            while (todo) {
+                const int l = __ffs(todo) - 1;
+                todo &= todo - 1;
+                const long long it = base + l;
+                const unsigned word = __shfl_sync(kFull, my_word, l);
+                const int b = (int)(it / words_src), w = (int)(it % words_src);
+                const int j = w * 32 + lane;
+                const bool on = (word >> lane) & 1u;
+                if (gated && !OG) {  // every source's gates step, on every rank alike (replicated state)
+                    if (GSRC)
+                        emit_src(step, j < Nsrc, b, j, on ? 1.0f : 0.0f);
+                    else
+                        emit(net, run, ws, step, j < Nsrc, b, j, on ? 1.0f : 0.0f, true, lane);
+                    continue;
+                }
+                int c0 = 0, cnt = 0;
+                float amp = 1.0f;
+                if (on) {
+                    c0 = net.src_chunk[j];
+                    cnt = net.src_chunk[j + 1] - c0;
+                    if (OG) amp = __ldcg(run.amps + ((size_t)(step & 1) * B + b) * amp_row + j);  // the owner's factor
+                }
+                emit_fast(net, ws, step, on, b, c0, cnt, amp, lane);
             }
-            int c0 = 0, cnt = 0;
-            if (on) {
-                c0 = net.src_chunk[j];
-                cnt = net.src_chunk[j + 1] - c0;
-            }
-            emit_fast(net, ws, step, on, b, c0, cnt, 1.0f, lane);
         }
         return bar.sync(ws.err);
     };
@@ -585,10 +620,19 @@ __global__ void __launch_bounds__(warps_of<S, FEAT>() * 32, 1) forward_kernel(co
                 float held;
                 s = spike_of(v, k.theta, cnt, u01, sflags, ksur, held);
             }
-            if (PART)
+            if (PART) {
+                if (OG) {
+                    const int jg = run.word0 * 32 + n;
+                    const SrcGate G = valid ? src_gate_of(net, jg) : no_gate();
+                    if (G.gate == -2) set_error(ws.err, WT_ERR_UNSUPPORTED);
+                    float amp = s;
+                    if (valid && G.gate >= 0) amp = s * step_gate(G, 0, q.b, s);
+                    publish_amp(0, q.b, jg, valid && s != 0.0f, amp);
+                }
                 publish(0, q.b, q.g, s);
-            else
+            } else {
                 emit_neuron(0, valid, q.b, n, k, s);
+            }
         }
     }
     for (long long base = warp0; base < itemsI; base += nthreads) {
@@ -696,7 +740,7 @@ __global__ void __launch_bounds__(warps_of<S, FEAT>() * 32, 1) forward_kernel(co
         NeuronConsts k{};
         // gated runs with resolved gating: the group's sources' gates (kg), and whether
         // one of them owns several slots (then the warp walks them in `emit`)
-        const bool GN = GSRC && !PART;
+        const bool GN = GSRC && (!PART || OG);
         SrcGate kg = no_gate();
         bool gmulti = false;
         float *rp = wsm + lane;
@@ -709,8 +753,9 @@ __global__ void __launch_bounds__(warps_of<S, FEAT>() * 32, 1) forward_kernel(co
                 k = consts_of(n);
                 g_k = q.g;
                 if (GN) {
-                    kg = valid ? src_gate_of(net, n) : no_gate();
+                    kg = valid ? src_gate_of(net, PART ? run.word0 * 32 + n : n) : no_gate();
                     gmulti = __any_sync(kFull, kg.gate == -2);
+                    if (OG && gmulti && lane == 0) set_error(ws.err, WT_ERR_UNSUPPORTED);
                 }
             }
             // item j's slot: wait for its copies (this lane's, then the warp's)
@@ -796,7 +841,8 @@ __global__ void __launch_bounds__(warps_of<S, FEAT>() * 32, 1) forward_kernel(co
                 for (int c = 0; c < S; c++) {
                     float gs = gr[c] + gd[c];
                     gs = fminf(fmaxf(gs, 0.0f), net.g_clip[c]);
-                    if (MG) gs = gs * sigmoid(net.mg_a[c] * v - net.mg_lc[c]);
+                    // a channel without the block (mg_lc -inf) multiplies by sigmoid(+inf) = 1
+                    if (MG && net.mg_lc[c] != -INFINITY) gs = gs * sigmoid(net.mg_a[c] * v - net.mg_lc[c]);
                     Gt[c] = gs;
                 }
 #pragma unroll
@@ -877,11 +923,24 @@ __global__ void __launch_bounds__(warps_of<S, FEAT>() * 32, 1) forward_kernel(co
             }
             if (emit_next) {
                 if (PART) {
+                    if (OG) {
+                        float amp = s_next;
+                        if (gstep) {
+                            const float f = gate_math(net.gate_params + 5 * kg.gate, kg.u_off >= 0, kg.a_off >= 0, gu, gx, gsa, s_next);
+                            if (kg.u_off >= 0) {
+                                gb[kg.u_off] = gu;
+                                gb[kg.x_off] = gx;
+                            }
+                            if (kg.a_off >= 0) gb[kg.a_off] = gsa;
+                            amp = s_next * f;
+                        }
+                        publish_amp(t + 1, b, run.word0 * 32 + n, valid && s_next != 0.0f, amp);
+                    }
                     publish(t + 1, b, q.g, s_next);
                 } else if (GN && !gmulti) {
                     float amp = s_next;
                     if (gstep) {
-                        const float f = gate_math(kg.prm, kg.u_off >= 0, kg.a_off >= 0, gu, gx, gsa, s_next);
+                        const float f = gate_math(net.gate_params + 5 * kg.gate, kg.u_off >= 0, kg.a_off >= 0, gu, gx, gsa, s_next);
                         if (kg.u_off >= 0) {
                             gb[kg.u_off] = gu;
                             gb[kg.x_off] = gx;
@@ -1073,15 +1132,22 @@ static cudaError_t launch_sf(const WtNet &net, const WtForward &run, const WtWor
 // and saving as given; no other feature); everything else runs the generic kernel.
 template <int S>
 static cudaError_t launch_s(const WtNet &net, const WtForward &run, const WtWorkspace &ws, cudaStream_t st) {
-    const int generic = WT_F_ADAPT | WT_F_MG_BLOCK | WT_F_SAMPLE | WT_F_GATED | WT_F_PROB | WT_F_TRACK | WT_F_SAVE_INPUT |
-                        WT_F_PARTITION;
-    if (S > 4 || (run.flags & generic)) return launch_sf<S, kGeneric>(net, run, ws, st);
-    const int feat = ((run.flags & WT_F_REFRACTORY) ? kRef : 0) | ((run.flags & WT_F_SAVE) ? kSave : 0);
+    const int generic = WT_F_ADAPT | WT_F_SAMPLE | WT_F_PROB | WT_F_TRACK | WT_F_SAVE_INPUT | WT_F_PARTITION;
+    const int feat = ((run.flags & WT_F_REFRACTORY) ? kRef : 0) | ((run.flags & WT_F_SAVE) ? kSave : 0) |
+                     ((run.flags & WT_F_MG_BLOCK) ? kMg : 0) | ((run.flags & WT_F_GATED) ? kGate : 0);
+    // the Mg block and gating are specialised for forward runs with a refractory period
+    // (the large simulations' case); other combinations with them run the generic kernel
+    const bool mg_gate = feat & (kMg | kGate);
+    if (S > 4 || (run.flags & generic) || (mg_gate && (feat & (kRef | kSave)) != kRef))
+        return launch_sf<S, kGeneric>(net, run, ws, st);
     switch (feat) {
         case 0: return launch_sf<S, 0>(net, run, ws, st);
         case kRef: return launch_sf<S, kRef>(net, run, ws, st);
         case kSave: return launch_sf<S, kSave>(net, run, ws, st);
-        default: return launch_sf<S, kRef | kSave>(net, run, ws, st);
+        case kRef | kSave: return launch_sf<S, kRef | kSave>(net, run, ws, st);
+        case kRef | kMg: return launch_sf<S, kRef | kMg>(net, run, ws, st);
+        case kRef | kGate: return launch_sf<S, kRef | kGate>(net, run, ws, st);
+        default: return launch_sf<S, kRef | kMg | kGate>(net, run, ws, st);
     }
 }
 

@@ -199,7 +199,7 @@ def run_forward(plan, p, x, v, g, counter, g_a, gating, *, probabilities=False, 
             run.X_saved = save["X"].data_ptr()
     if part is not None:  # one rank of a neuron-partitioned run (wiretorch_b200.partition)
         flags |= _lib.F_PARTITION
-        part.fill(run)
+        part.fill(run, plan)
     run.flags = flags
     ws, w = _workspace(plan, T, device)
     out["_ws"] = ws

@@ -11,9 +11,14 @@ source from the words into its own targets. The next step's scatter and update f
 so the exchange of step t + 1's spikes costs one wait per step (``WT_F_PARTITION``).
 
 Blocks are whole 32-neuron words. The inputs ``x`` are replicated on every rank, and so
-is the gating state of gated pathways (every rank steps every source's gates alike from
-the words). The run is forward only (no saving for a backward pass). The fixed-point
-synaptic sums make a partitioned run's spikes identical to a one-GPU run's.
+is the gating state of gated pathways. When every neuron owns at most one slot (one
+pathway), a neuron's gate is stepped by the rank that owns the neuron alone, which
+writes the factor of each of its spikes beside the spike words (``amps``, peer stores
+like the words); after the call the ranks gather the gating state, each column from the
+rank that stepped it (``_gather_gating``). Otherwise every rank steps every source's
+gates alike from the words. Input columns' gates are stepped on every rank (the inputs
+are replicated). The run is forward only (no saving for a backward pass). The
+fixed-point synaptic sums make a partitioned run's spikes identical to a one-GPU run's.
 """
 
 from __future__ import annotations
@@ -96,7 +101,8 @@ class Partition:
         self.n0, self.n1 = blocks(N, self.P)[self.rank]
         self.words_src = -(-N // 32)
         words_bytes = -(-(2 * B * self.words_src * 4) // 256) * 256
-        total = words_bytes + 8 * 8
+        amps_off = words_bytes + 256  # after the progress slots (8 x 8 bytes)
+        total = amps_off + 2 * B * self.words_src * 32 * 4
         torch.cuda.synchronize()
         self._base = _cuda(rt.cudaMalloc(total))
         _cuda(rt.cudaMemset(self._base, 0, total))
@@ -117,18 +123,24 @@ class Partition:
             bases.append(int(peer))
         self.peer_words = bases
         self.peer_progress = [b + words_bytes for b in bases]
+        self.peer_amps = [b + amps_off for b in bases]
         self.words, self.progress = bases[self.rank], bases[self.rank] + words_bytes
         self.epoch = 0
         dist.barrier(group=group)
 
-    def fill(self, run) -> None:
-        """The partition's fields of a ``WtForward`` for the next call (a new epoch)."""
+    def fill(self, run, plan=None) -> None:
+        """The partition's fields of a ``WtForward`` for the next call (a new epoch); the
+        amplitude buffers too when ``plan``'s gates are stepped by their owners."""
         self.epoch += 1
         run.words, run.progress = self.words, self.progress
         for r in range(self.P):
             run.peer_words[r] = self.peer_words[r]
             run.peer_progress[r] = self.peer_progress[r]
         run.n_ranks, run.rank, run.word0, run.epoch = self.P, self.rank, self.n0 // 32, self.epoch
+        if plan is not None and owner_gates(plan):
+            run.amps = self.peer_amps[self.rank]
+            for r in range(self.P):
+                run.peer_amps[r] = self.peer_amps[r]
 
     def close(self) -> None:
         from cuda.bindings import runtime as rt
@@ -139,6 +151,59 @@ class Partition:
         if self._base is not None:
             _cuda(rt.cudaFree(self._base))
             self._base = None
+
+
+def owner_gates(plan) -> bool:
+    """Whether each neuron's gate can be stepped by the rank that owns the neuron alone:
+    a gated network with the per-source gate table in which no neuron owns several
+    slots (a spike then carries one factor)."""
+    t = plan.tensors
+    if not plan.gated or "src_gate" not in t:
+        return False
+    if "_owner_gates" not in t:
+        t["_owner_gates"] = not bool((t["src_gate"][: plan.N_src, 0] == -2).any())
+    return t["_owner_gates"]
+
+
+def gating_owners(plan, P: int) -> torch.Tensor:
+    """``(R,)`` int64: per column of the gating state, the rank that steps it in an
+    owner-stepped run (the rank holding the column's source neuron), or -1 for the
+    columns every rank steps alike (input columns' gates, unused columns)."""
+    t = plan.tensors
+    if "_gating_owners" not in t:
+        R = plan.R
+        owner = torch.full((R,), -1, dtype=torch.int64, device=plan.device)
+        sg = t["src_gate"][: plan.N_src].long()
+        j = (sg[:, 0] >= 0).nonzero().flatten()
+        if j.numel():
+            gate, row = sg[j, 0], sg[j, 1]
+            cols = t["gate_cols"].long()[gate]  # (k, 4): u column, rows, saturation column, -
+            cuts = torch.tensor([b[0] for b in blocks(plan.N_src, P)[1:]], device=plan.device)
+            rank = torch.bucketize(j, cuts, right=True)
+            stp, sat = cols[:, 0] >= 0, cols[:, 2] >= 0
+            owner[(cols[:, 0] + row)[stp]] = rank[stp]
+            owner[(cols[:, 0] + cols[:, 1] + row)[stp]] = rank[stp]
+            owner[(cols[:, 2] + row)[sat]] = rank[sat]
+        t["_gating_owners"] = owner
+    return t["_gating_owners"]
+
+
+def _gather_gating(part, plan, gating) -> None:
+    """After an owner-stepped run: every rank's gating state made whole, in place — each
+    column taken from the rank that stepped it (the others' copies of it are stale)."""
+    import torch.distributed as dist
+
+    owner = gating_owners(plan, part.P)
+    if owner.numel() < gating.shape[1]:  # columns past the gates' own: nobody's
+        owner = torch.cat([owner, owner.new_full((gating.shape[1] - owner.numel(),), -1)])
+    on_gpu = dist.get_backend(part.group) == "nccl"
+    mine = gating if on_gpu else gating.cpu()
+    parts = [torch.empty_like(mine) for _ in range(part.P)]
+    dist.all_gather(parts, mine.contiguous(), group=part.group)
+    stacked = torch.stack(parts)  # (P, B, R)
+    src = torch.where(owner < 0, part.rank, owner).to(stacked.device)
+    whole = stacked[src, :, torch.arange(owner.numel(), device=stacked.device)]  # (R, B)
+    gating.copy_(whole.t())
 
 
 _LOCAL: dict = {}
@@ -171,7 +236,7 @@ def simulate(part: Partition, v, g, x, drive, p, *, refractory=None, gating=None
     _plan.fold(plan, d_loc.scale)
     local = v.shape[1] == n1 - n0 != part.N  # the block's own state (a previous call's Run)
     cut = (lambda t: t) if local else (lambda t: None if t is None else t[:, n0:n1])  # noqa: E731
-    # the gating state stays whole: every rank steps every source's gates alike
+    # the gating state is whole on every rank (owner-stepped columns gathered after the run)
     v_k, g_k, counter, g_a, gating_k = engine._prepare_state(plan, cut(v), cut(g), cut(refractory), gating,
                                                              cut(adaptation), p_loc)  # fmt: skip
     # All ranks' kernels start together (their exchange waits are bounded), and none
@@ -182,4 +247,6 @@ def simulate(part: Partition, v, g, x, drive, p, *, refractory=None, gating=None
     dist.barrier(group=part.group)
     with torch.no_grad():
         out = engine.run_forward(plan, p_loc, x.detach().float(), v_k, g_k, counter, g_a, gating_k, part=part)
+    if gating_k is not None and owner_gates(plan):
+        _gather_gating(part, plan, gating_k)
     return engine._run(plan, out, v_k, g_k, counter, g_a, gating_k, p_loc, False, refractory)
