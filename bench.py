@@ -19,7 +19,8 @@ recurrent spikes per second (counted on the device over one extra, untimed step 
 multiplied by the steps timed), input events separately.
 ``roofline``: the dominant kernel's algorithmic bytes per launch / its CUDA-event
 duration against the measured HBM copy bandwidth. ``e2e``: the same step fed from pinned
-host memory (spike input as bytes, target rates), with the loss and gradient read back.
+host memory (spike input as bytes, target rates), with the loss and gradient read back;
+each step's input is copied on a second stream while the previous step computes.
 ``cpu_baseline``: the oracle (the C restatement of the reference's time loop) on a
 bounded sample of the same network on the host cores. ``--impl reference`` times that
 CPU implementation alone.
@@ -560,23 +561,46 @@ def main():
         h2d = x_host.numel() + (tgt_host.numel() * 4 if train else 0)
         d2h = out_host.numel() * 4
 
-        def e2e_step():
-            xd = x_host.to(device, non_blocking=True).float()
+        # Each step's input crosses from pinned host memory on a copy stream while the
+        # previous step computes (the copy of step k + 1 overlaps step k); every copy lies
+        # inside the timed region, between its two events.
+        copy_stream = torch.cuda.Stream(device)
+        main = torch.cuda.current_stream(device)
+
+        def fetch(after):
+            copy_stream.wait_event(after)
+            with torch.cuda.stream(copy_stream):
+                xd = x_host.to(device, non_blocking=True).float()
+                r = tgt_host.to(device, non_blocking=True) * (DT / 1000.0) if train else None
+                ready = torch.cuda.Event()
+                ready.record(copy_stream)
+            return xd, r, ready
+
+        def e2e_step(inputs):
+            xd, r, ready = inputs
+            main.wait_event(ready)
+            xd.record_stream(main)
             if train:
-                r = tgt_host.to(device, non_blocking=True) * (DT / 1000.0)
+                r.record_stream(main)
                 loss = step(xd, r[:, None, :].expand(cfg.B, cfg.T, cfg.N))
                 res = torch.cat([loss.detach().reshape(1), log_sf.detach().reshape(-1)])
             else:
                 res = step(xd).reshape(1).float()
             out_host.copy_(res, non_blocking=True)
 
-        e2e_step()
+        first = torch.cuda.Event()
+        first.record(main)
+        e2e_step(fetch(first))
         torch.cuda.synchronize()
         barrier(world)
         s2, e2 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         s2.record()
-        for _ in range(K):
-            e2e_step()
+        pending = fetch(s2)
+        for k in range(K):
+            inputs = pending
+            if k + 1 < K:
+                pending = fetch(inputs[2])  # the next step's input, behind this one's copy
+            e2e_step(inputs)
         e2.record()
         torch.cuda.synchronize()
         e2e_el = max_over_ranks(s2.elapsed_time(e2) / 1000.0, world)
