@@ -103,22 +103,3 @@ def test_resolved_gating_gradients_match():
     assert g_fast is not None and float(g_fast.abs().sum()) > 0
     torch.testing.assert_close(g_fast, g_slow, rtol=1e-5, atol=1e-6 * float(g_slow.abs().max()))
 
-
-@pytest.mark.parametrize("pool", [False, True], ids=["exact", "pooled"])
-def test_specialised_kernel_matches_generic(pool):
-    """Forward runs with a refractory period and the Mg block or gating take a kernel with
-    those features compiled in; tracking sends the same run through the generic kernel.
-    Both give identical spikes and state."""
-    cfg = _doubled(_c5_small())
-    x = cfg.inputs(seed=7)
-    engine.POOL_SYNAPSES = pool
-    try:
-        v, g, kw = cfg.state()
-        with torch.no_grad():
-            fast = engine.simulate(v, g, x, cfg.drive, cfg.p, **kw)
-            generic = engine.simulate(v, g, x, cfg.drive, cfg.p, **kw, track=True)
-    finally:
-        engine.POOL_SYNAPSES = False
-    assert float(fast.output.sum()) > 20
-    for name in ("output", "v", "syn", "gating", "refractory"):
-        assert torch.equal(getattr(fast, name), getattr(generic, name)), name

@@ -271,20 +271,21 @@ __device__ __forceinline__ float spike_of(float v, float theta, int counter, flo
 
 static_assert(WT_CHUNK_EDGES <= 128, "a chunk's edges take at most four per lane");
 // Feature bits of a specialised kernel: the refractory period, saving for the backward
-// pass, the Mg block and presynaptic gating known at compile time; everything else
-// (adaptation, escape noise, probabilities, tracking, saved input, partitions) in the
-// generic variant, tested at run time.
-constexpr int kRef = 1, kSave = 2, kGeneric = 4, kMg = 8, kGate = 16;
+// pass, the Mg block, presynaptic gating and adaptation known at compile time;
+// everything else (escape noise, probabilities, tracking, saved input, partitions) in
+// the generic variant, tested at run time.
+constexpr int kRef = 1, kSave = 2, kGeneric = 4, kMg = 8, kGate = 16, kAdapt = 32;
 
 // Warps per block of the forward kernel (one block per SM): 24 for the specialised
 // kernels of up to four channels (80 registers a thread, as good as no spill), WT_GATE_WARPS
-// for those with the Mg block or gating, 16 for the others (up to 128 registers).
+// for those with the Mg block, gating or adaptation, 16 for the others (up to 128
+// registers).
 #ifndef WT_GATE_WARPS
 #define WT_GATE_WARPS 20
 #endif
 template <int S, int FEAT>
 constexpr int warps_of() {
-    return ((FEAT & kGeneric) == 0 && S <= 4) ? ((FEAT & (kMg | kGate)) ? WT_GATE_WARPS : 24) : 16;
+    return ((FEAT & kGeneric) == 0 && S <= 4) ? ((FEAT & (kMg | kGate | kAdapt)) ? WT_GATE_WARPS : 24) : 16;
 }
 constexpr int kMaxRing = 4;               // deepest ring of staged items
 
@@ -323,7 +324,7 @@ __global__ void __launch_bounds__(warps_of<S, FEAT>() * 32, 1) forward_kernel(co
     const int flags = run.flags;
     const bool REF = GEN ? (flags & WT_F_REFRACTORY) != 0 : (FEAT & kRef) != 0;
     const bool SAVE = GEN ? (flags & WT_F_SAVE) != 0 : (FEAT & kSave) != 0;
-    const bool ADAPT = GEN && (flags & WT_F_ADAPT);
+    const bool ADAPT = GEN ? (flags & WT_F_ADAPT) != 0 : (FEAT & kAdapt) != 0;
     const bool MG = GEN ? (flags & WT_F_MG_BLOCK) != 0 : (FEAT & kMg) != 0;
     const bool SAMPLE = GEN && (flags & WT_F_SAMPLE);
     const bool gated = GEN ? (flags & WT_F_GATED) != 0 : (FEAT & kGate) != 0;
@@ -1132,13 +1133,17 @@ static cudaError_t launch_sf(const WtNet &net, const WtForward &run, const WtWor
 // and saving as given; no other feature); everything else runs the generic kernel.
 template <int S>
 static cudaError_t launch_s(const WtNet &net, const WtForward &run, const WtWorkspace &ws, cudaStream_t st) {
-    const int generic = WT_F_ADAPT | WT_F_SAMPLE | WT_F_PROB | WT_F_TRACK | WT_F_SAVE_INPUT | WT_F_PARTITION;
+    const int generic = WT_F_SAMPLE | WT_F_PROB | WT_F_TRACK | WT_F_SAVE_INPUT | WT_F_PARTITION;
     const int feat = ((run.flags & WT_F_REFRACTORY) ? kRef : 0) | ((run.flags & WT_F_SAVE) ? kSave : 0) |
-                     ((run.flags & WT_F_MG_BLOCK) ? kMg : 0) | ((run.flags & WT_F_GATED) ? kGate : 0);
-    // the Mg block and gating are specialised for forward runs with a refractory period
-    // (the large simulations' case); other combinations with them run the generic kernel
-    const bool mg_gate = feat & (kMg | kGate);
-    if (S > 4 || (run.flags & generic) || (mg_gate && (feat & (kRef | kSave)) != kRef))
+                     ((run.flags & WT_F_MG_BLOCK) ? kMg : 0) | ((run.flags & WT_F_GATED) ? kGate : 0) |
+                     ((run.flags & WT_F_ADAPT) ? kAdapt : 0);
+    // the Mg block, gating and adaptation are specialised for forward runs with a
+    // refractory period (the large simulations' cases: Mg block and gating in any
+    // combination, or adaptation alone); other combinations with them run the generic
+    // kernel
+    const int extra = feat & (kMg | kGate | kAdapt);
+    if (S > 4 || (run.flags & generic) || (extra && (feat & (kRef | kSave)) != kRef) ||
+        ((extra & kAdapt) && extra != kAdapt))
         return launch_sf<S, kGeneric>(net, run, ws, st);
     switch (feat) {
         case 0: return launch_sf<S, 0>(net, run, ws, st);
@@ -1147,6 +1152,7 @@ static cudaError_t launch_s(const WtNet &net, const WtForward &run, const WtWork
         case kRef | kSave: return launch_sf<S, kRef | kSave>(net, run, ws, st);
         case kRef | kMg: return launch_sf<S, kRef | kMg>(net, run, ws, st);
         case kRef | kGate: return launch_sf<S, kRef | kGate>(net, run, ws, st);
+        case kRef | kAdapt: return launch_sf<S, kRef | kAdapt>(net, run, ws, st);
         default: return launch_sf<S, kRef | kMg | kGate>(net, run, ws, st);
     }
 }
