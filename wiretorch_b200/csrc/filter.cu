@@ -173,6 +173,8 @@ __global__ void filter_grad_chunked(const WtFilterGradArgs f) {
 // The van Rossum rate loss (training_utils/losses.py:140-194) in one pass per column:
 // both filters, the difference saved, its square summed in double (per thread, then
 // over the block: one partial per block, summed by the caller in a fixed order).
+constexpr int kVrAhead = 8;  // steps of input the van Rossum scans load at once
+
 __global__ void __launch_bounds__(256) van_rossum_fwd(const WtVanRossumArgs a) {
     __shared__ double part[8];
     const long long cols = (long long)a.B * a.N;
@@ -187,13 +189,11 @@ __global__ void __launch_bounds__(256) van_rossum_fwd(const WtVanRossumArgs a) {
             rt = a.carry[2 * cols + i];
             st = a.carry[3 * cols + i];
         }
-        const float *x = a.x + b * a.x_bstride + n;
-        const float *y = a.y + b * a.y_bstride + n;
-        float *e = a.err + (size_t)b * a.T * a.N + n;
-#pragma unroll 4
-        for (int t = 0; t < a.T; t++) {
-            const float xt = x[t * a.x_tstride], yt = y[t * a.y_tstride];
-            // the carried state enters undecayed at t = 0 (filtering.py:112-117)
+        const float *__restrict__ x = a.x + b * a.x_bstride + n;
+        const float *__restrict__ y = a.y + b * a.y_bstride + n;
+        float *__restrict__ e = a.err + (size_t)b * a.T * a.N + n;
+        // one step (the carried state enters undecayed at t = 0: filtering.py:112-117)
+        auto step = [&](int t, float xt, float yt) {
             ro = (t == 0 ? ro : a.a_rise * ro) + xt;
             so = (t == 0 ? so : a.a_decay * so) + ro;
             rt = (t == 0 ? rt : a.a_rise * rt) + yt;
@@ -201,7 +201,19 @@ __global__ void __launch_bounds__(256) van_rossum_fwd(const WtVanRossumArgs a) {
             const float d = so - st;
             e[(size_t)t * a.N] = d;
             sq += (double)d * (double)d;
+        };
+        int t = 0;
+        for (; t + kVrAhead <= a.T; t += kVrAhead) {  // kVrAhead steps' loads issued together
+            float xs[kVrAhead], ys[kVrAhead];
+#pragma unroll
+            for (int k = 0; k < kVrAhead; k++) {
+                xs[k] = x[(t + k) * a.x_tstride];
+                ys[k] = y[(t + k) * a.y_tstride];
+            }
+#pragma unroll
+            for (int k = 0; k < kVrAhead; k++) step(t + k, xs[k], ys[k]);
         }
+        for (; t < a.T; t++) step(t, x[t * a.x_tstride], y[t * a.y_tstride]);
         if (a.T > 0) {
             a.last[i] = ro;
             a.last[cols + i] = so;
@@ -226,13 +238,23 @@ __global__ void van_rossum_bwd(const WtVanRossumGradArgs a) {
     const int b = (int)(i / a.N), n = (int)(i % a.N);
     const float c = a.scale * *a.grad_loss;
     const size_t base = (size_t)b * a.T * a.N + n;
+    const float *__restrict__ err = a.err + base;
+    float *__restrict__ grad_x = a.grad_x + base;
     float gs = 0.0f, gx = 0.0f;
-    for (int t = a.T - 1; t >= 0; t--) {
-        const size_t o = base + (size_t)t * a.N;
-        gs = a.err[o] * c + a.a_decay * gs;
+    auto step = [&](int t, float et) {
+        gs = et * c + a.a_decay * gs;
         gx = gs + a.a_rise * gx;
-        a.grad_x[o] = gx;
+        grad_x[(size_t)t * a.N] = gx;
+    };
+    int t = a.T - 1;
+    for (; t + 1 >= kVrAhead; t -= kVrAhead) {  // kVrAhead steps' loads issued together
+        float es[kVrAhead];
+#pragma unroll
+        for (int k = 0; k < kVrAhead; k++) es[k] = err[(size_t)(t - k) * a.N];
+#pragma unroll
+        for (int k = 0; k < kVrAhead; k++) step(t - k, es[k]);
     }
+    for (; t >= 0; t--) step(t, err[(size_t)t * a.N]);
 }
 
 // Columns below which the parallel-over-T kernels run (148 SMs x 2048 threads would
