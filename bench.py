@@ -466,6 +466,9 @@ def main():
         return
     from wiretorch_b200 import _lib, engine
 
+    # the forward's device error word is read behind the launches (no host
+    # synchronisation per step); every run's word is checked before the results print
+    engine.DEFER_CHECKS = True
     device = torch.device("cuda", local)
     torch.cuda.set_device(device)
     cfg, x = build(args, rank, device)
@@ -608,6 +611,7 @@ def main():
                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                "ms_per_step": e2e_el / K * 1000.0}  # fmt: skip
 
+    engine.check_errors()  # every deferred device error check of the runs above
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu and not factorised:
         rate, cores, sample = cpu_baseline(cfg)

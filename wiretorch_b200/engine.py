@@ -126,9 +126,43 @@ def check_device(err: torch.Tensor, what: str) -> None:
         raise RuntimeError(f"{what}: {_lib.ERRORS.get(code, code)}")
 
 
+#: When True, a forward launch's device error word is not read at once (a host
+#: synchronisation per call) but copied to pinned host memory behind the launch, on its
+#: stream, and checked by the next engine call or by ``check_errors()`` — the first
+#: error raises there. For loops that keep the GPU fed (training, benchmarks); the
+#: default reads the word before the call returns.
+DEFER_CHECKS = False
+_PENDING: list = []
+
+
+def _defer_check(err: torch.Tensor, what: str) -> None:
+    host = torch.empty(1, dtype=torch.int32, pin_memory=True)
+    host.copy_(err, non_blocking=True)
+    done = torch.cuda.Event()
+    done.record(torch.cuda.current_stream(err.device))
+    _PENDING.append((done, host, what))
+
+
+def check_errors(block: bool = True) -> None:
+    """Raise for the first device error recorded by a deferred check (``DEFER_CHECKS``);
+    ``block``: wait for the launches still running, else check only finished ones."""
+    while _PENDING:
+        done, host, what = _PENDING[0]
+        if not block and not done.query():
+            return
+        done.synchronize()
+        _PENDING.pop(0)
+        code = int(host[0])
+        if code:
+            _PENDING.clear()
+            raise RuntimeError(f"{what}: {_lib.ERRORS.get(code, code)}")
+
+
 def run_forward(plan, p, x, v, g, counter, g_a, gating, *, probabilities=False, track=False,
                 track_b=-1, save=None, noise=None, check=True, part=None):  # fmt: skip
     """Launch the forward kernel over all of ``x``; returns the outputs (dict)."""
+    if _PENDING:
+        check_errors(block=False)  # earlier deferred checks that have finished
     device = plan.device
     B, T, n_in = x.shape
     N, Sp = plan.N, plan.ch.Sp
@@ -208,7 +242,9 @@ def run_forward(plan, p, x, v, g, counter, g_a, gating, *, probabilities=False, 
                                    _lib.C.c_void_p(_lib.stream_of(device)))  # fmt: skip
     _lib.check(rc, "wt_forward")
     _lib.count_launches(1)
-    if check:
+    if check and DEFER_CHECKS:
+        _defer_check(ws["err"], "wt_forward")
+    elif check:
         check_device(ws["err"], "wt_forward")
     return out
 
