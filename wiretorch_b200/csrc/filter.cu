@@ -20,21 +20,32 @@
 namespace wt {
 namespace {
 
+constexpr int kVrAhead = 8;  // steps of a column the sequential scans load at once
+
 __global__ void filter_seq(const WtFilterArgs f) {
     const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= (long long)f.B * f.N) return;
     const int b = (int)(i / f.N), n = (int)(i % f.N);
     float r = f.carry_rise ? f.carry_rise[i] : 0.0f;
     float s = f.carry_smooth ? f.carry_smooth[i] : 0.0f;
-    const float *x = f.x + b * f.x_bstride + n;
-    for (int t = 0; t < f.T; t++) {
-        const float xt = x[t * f.x_tstride];
+    const float *__restrict__ x = f.x + b * f.x_bstride + n;
+    float *__restrict__ rise = f.rise, *__restrict__ smooth = f.smooth;
+    auto step = [&](int t, float xt) {
         r = (t == 0 ? r : f.a_rise * r) + xt;
         s = (t == 0 ? s : f.a_decay * s) + r;
         const size_t o = ((size_t)b * f.T + t) * f.N + n;
-        if (f.rise) f.rise[o] = r;
-        if (f.smooth) f.smooth[o] = s;
+        if (rise) rise[o] = r;
+        if (smooth) smooth[o] = s;
+    };
+    int t = 0;
+    for (; t + kVrAhead <= f.T; t += kVrAhead) {  // kVrAhead steps' loads issued together
+        float xs[kVrAhead];
+#pragma unroll
+        for (int k = 0; k < kVrAhead; k++) xs[k] = x[(t + k) * f.x_tstride];
+#pragma unroll
+        for (int k = 0; k < kVrAhead; k++) step(t + k, xs[k]);
     }
+    for (; t < f.T; t++) step(t, x[t * f.x_tstride]);
     if (f.last_rise) f.last_rise[i] = r;
     if (f.last_smooth) f.last_smooth[i] = s;
 }
@@ -123,13 +134,24 @@ __global__ void filter_grad_seq(const WtFilterGradArgs f) {
     const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= (long long)f.B * f.N) return;
     const int b = (int)(i / f.N), n = (int)(i % f.N);
+    const size_t base = (size_t)b * f.T * f.N + n;
+    const float *__restrict__ gsm = f.grad_smooth + base;
+    float *__restrict__ gx = f.grad_x + base;
     float gs = 0.0f, gr = 0.0f;
-    for (int t = f.T - 1; t >= 0; t--) {
-        const size_t o = ((size_t)b * f.T + t) * f.N + n;
-        gs = f.grad_smooth[o] * f.grad_scale + f.a_decay * gs;
+    auto step = [&](int t, float g) {
+        gs = g * f.grad_scale + f.a_decay * gs;
         gr = gs + f.a_rise * gr;
-        f.grad_x[o] = gr;
+        gx[(size_t)t * f.N] = gr;
+    };
+    int t = f.T - 1;
+    for (; t + 1 >= kVrAhead; t -= kVrAhead) {  // kVrAhead steps' loads issued together
+        float g8[kVrAhead];
+#pragma unroll
+        for (int k = 0; k < kVrAhead; k++) g8[k] = gsm[(size_t)(t - k) * f.N];
+#pragma unroll
+        for (int k = 0; k < kVrAhead; k++) step(t - k, g8[k]);
     }
+    for (; t >= 0; t--) step(t, gsm[(size_t)t * f.N]);
 }
 
 // The reverse recursion as a chunked parallel scan (state (g_s, g_x), map M^T).
@@ -173,8 +195,6 @@ __global__ void filter_grad_chunked(const WtFilterGradArgs f) {
 // The van Rossum rate loss (training_utils/losses.py:140-194) in one pass per column:
 // both filters, the difference saved, its square summed in double (per thread, then
 // over the block: one partial per block, summed by the caller in a fixed order).
-constexpr int kVrAhead = 8;  // steps of input the van Rossum scans load at once
-
 __global__ void __launch_bounds__(256) van_rossum_fwd(const WtVanRossumArgs a) {
     __shared__ double part[8];
     const long long cols = (long long)a.B * a.N;
