@@ -18,7 +18,7 @@
  *
  * The reference (rory-bedford/wiretorch) is pure Python with Triton kernels and binds
  * no foreign functions; each entry point names the Python/Triton function of the
- * reference whose work it replaces, and INTEGRATION.md shows the ctypes binding.
+ * reference whose work it replaces.
  */
 #ifndef WIRETORCH_B200_H
 #define WIRETORCH_B200_H
@@ -191,11 +191,15 @@ int wt_forward(const WtNet *net, const WtForward *run, const WtWorkspace *ws, vo
  * with PyTorch on every call). For callers that cannot allocate device memory on this
  * path. The first call on a device looks up the array (do it before any stream capture);
  * calls overlapping in time share the array and race, so a caller serialises them. The
- * run's device error code is read with wt_noalloc_error. Allocates nothing. */
+ * address looked up belongs to the device's context: after cudaDeviceReset this entry
+ * point must not be called again in the process. A call rejected by the argument checks
+ * launches nothing and keeps the previous run's device error code. The run's device
+ * error code is read with wt_noalloc_error. Allocates nothing. */
 int wt_forward_noalloc(const WtNet *net, const WtForward *run, void *stream);
 
 /* The device error code (0: none) of the last wt_forward_noalloc on the current device,
- * after waiting for `stream`. No counterpart in the reference. */
+ * after waiting for `stream`, which must be the stream that run was enqueued on (a read
+ * on another stream may come before the run ends). No counterpart in the reference. */
 int wt_noalloc_error(void *stream, int32_t *code);
 
 /* Gradients wanted by a backward pass (WtBackward.wants): the physiology, in the order

@@ -1,8 +1,8 @@
 """Short, representative launches of the engine's kernels for profiling (ncu captures).
 
-``python -m wiretorch_b200.profile_cases c2-active``: C2 (64 trials, pooled channels) run
+``python tests/profile_cases.py c2-active``: C2 (64 trials, pooled channels) run
 450 steps from rest, then one 20-step call from that state with saving for the backward
-pass, as in training. ``python -m wiretorch_b200.profile_cases c3-small``: C3 with 128
+pass, as in training. ``python tests/profile_cases.py c3-small``: C3 with 128
 trials, 200 steps, then one 10-step call from that state. ``c5-small``: C5 at 250,000
 neurons (4 trials, gated, pooled), 300 steps from rest, then one 20-step call. In all
 the second launch of the kernel is the one to capture (``-s 1 -c 1``).
@@ -11,8 +11,11 @@ the second launch of the kernel is the one to capture (``-s 1 -c 1``).
 from __future__ import annotations
 
 import sys
+from pathlib import Path
 
-import torch
+sys.path.insert(0, str(Path(__file__).resolve().parents[1]))
+
+import torch  # noqa: E402
 
 
 def c2_active():

@@ -92,7 +92,12 @@ int wt_fold_weights(const WtNet *net, const float *w_raw, const int32_t *chunk_p
                          "fold");
 }
 
-int wt_forward(const WtNet *net, const WtForward *run, const WtWorkspace *ws, void *stream) {
+}  // extern "C"
+
+namespace wt {
+// Every argument check of wt_forward, with no device work: WT_OK if wt_forward would
+// launch (or return at once for T = 0), else its error code with wt_last_error set.
+int check_forward(const WtNet *net, const WtForward *run, const WtWorkspace *ws) {
     int rc = check_net(net);
     if (rc) return rc;
     if (!run || !ws) return fail(WT_ERR_ARGS, "run or workspace is null%s");
@@ -141,6 +146,15 @@ int wt_forward(const WtNet *net, const WtForward *run, const WtWorkspace *ws, vo
     } else if (net->N_src && net->N_src != net->N) {
         return fail(WT_ERR_ARGS, "a net with other neurons' sources needs WT_F_PARTITION%s");
     }
+    return WT_OK;
+}
+}  // namespace wt
+
+extern "C" {
+
+int wt_forward(const WtNet *net, const WtForward *run, const WtWorkspace *ws, void *stream) {
+    const int rc = wt::check_forward(net, run, ws);
+    if (rc) return rc;
     if (run->T == 0) return WT_OK;
     cudaStream_t st = (cudaStream_t)stream;
     cudaError_t e = cudaMemsetAsync(ws->barrier, 0, 64 * 4, st);

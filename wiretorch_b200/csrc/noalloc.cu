@@ -11,7 +11,12 @@
 //
 // Set-up: the first call on a device (with that device current) looks up the array's
 // address with cudaGetSymbolAddress and keeps it; later calls on that device reuse it,
-// so the first call should come before any stream capture. Runs whose workspace
+// so the first call should come before any stream capture. The kept address belongs to
+// the device's current context: after cudaDeviceReset (or anything else that destroys
+// that context) it is stale, and this entry point must not be called again in the
+// process. A call that fails its argument checks launches nothing and leaves the
+// previous run's device error code in place; wt_noalloc_error waits on the stream it is
+// given, which must be the stream of the run whose code is wanted. Runs whose workspace
 // (wt_workspace_bytes) does not fit are rejected with WT_ERR_ARGS before any device
 // work. Calls share the one array per device: two calls that overlap in time, on any
 // streams, race on it and corrupt each other's results, so a caller serialises them.
@@ -22,6 +27,7 @@
 
 namespace wt {
 int set_last_error(int code, const char *message);
+int check_forward(const WtNet *net, const WtForward *run, const WtWorkspace *ws);
 }
 
 namespace {
@@ -81,8 +87,12 @@ int wt_forward_noalloc(const WtNet *net, const WtForward *run, void *stream) {
     ws.err = reinterpret_cast<int32_t *>(base + off[4]);
     ws.ev_cap = (long long)net->B * (net->n_chunks > 0 ? net->n_chunks : 1);
     ws.edges = nullptr;
-    // The error word must start at zero (wt_forward clears the barrier; the kernel clears
-    // the accumulators and event counts itself).
+    // Every check of wt_forward first: a call it rejects leaves the device error code of
+    // the previous run in place. Then the error word must start at zero (wt_forward
+    // clears the barrier; the kernel clears the accumulators and event counts itself).
+    const int checked = wt::check_forward(net, run, &ws);
+    if (checked) return checked;
+    if (run->T == 0) return WT_OK;
     e = cudaMemsetAsync(ws.err, 0, sizeof(int32_t), (cudaStream_t)stream);
     if (e != cudaSuccess) return wt::set_last_error(WT_ERR_LAUNCH, cudaGetErrorString(e));
     return wt_forward(net, run, &ws, stream);
