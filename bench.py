@@ -1,29 +1,40 @@
 #!/usr/bin/env python
 """Benchmark of the conductance-LIF simulation hot path on B200.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--config c2] [--impl ours|reference]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config c5] [--impl ours|reference]
 
 For N > 1 run one process per GPU (``torch.distributed.run``); ranks talk over NCCL.
 
-Workload (``--config c2``, the default): BASELINE configuration 2 — 20,000 conductance
-LIF neurons in 40 cell types, learnt per-type-pair scales, batch 64 per GPU, T=500 steps
-of 0.1 ms, Poisson input. One step is one training step: the forward simulation through
-the engine (``wiretorch_b200.engine.simulate``), the van Rossum rate loss (20 ms-filtered
-output against filtered target rates), backpropagation through time to the 41x40 scales,
-the gradients' all-reduce across ranks and an SGD update (gradient norm clipped at 1). Every rank simulates its own 64
-trials (trial-batch sharding, weak scaling). Inputs are larger than L2.
+Workload (``--config c5``, the default: the largest configuration): BASELINE
+configuration 5 — 1,000,000 conductance-LIF neurons with ~1B edges from a
+distance-dependent model, AMPA + NMDA (Mg block) + GABA_A, short-term depression,
+refractoriness, 4 trials, T=5,000 steps of 0.1 ms, forward, run as engine calls of 1,000
+steps with the state carried. One step is one such 5,000-step simulation. At N = 1 it
+runs on one GPU; at N > 1 the network's neurons are partitioned over the ranks (each
+holds a block of neurons and every edge onto them) and every step's spikes cross between
+the GPUs by peer stores inside the forward kernel: total work is fixed (strong scaling).
 
-``value``: neuron-steps per second of the whole job (trials x neurons x time steps of all
-ranks / the slowest rank's device time). ``synaptic_events_per_s``: edges traversed by
-recurrent spikes per second (counted on the device over one extra, untimed step and
-multiplied by the steps timed), input events separately.
+``--config c2``: configuration 2's training step — 20,000 neurons in 40 cell types,
+learnt per-type-pair scales, 64 trials per GPU, T=500: forward through the engine
+(``wiretorch_b200.engine.simulate``), the van Rossum rate loss (20 ms-filtered output
+against filtered target rates), backpropagation through time to the 41x40 scales, the
+gradients' all-reduce across ranks and an SGD update (gradient norm clipped at 1); every
+rank simulates its own 64 trials (trial-batch sharding, weak scaling). ``--config c1 /
+c3 / c4``: the other configurations, forward.
+
+``value``: neuron-steps per second of the whole job (trials x neurons x time steps of
+the work all ranks did / the slowest rank's device time). ``synaptic_events_per_s``:
+edges traversed by recurrent spikes per second (counted on the device over one extra,
+untimed step and multiplied by the steps timed), input events separately.
 ``roofline``: the dominant kernel's algorithmic bytes per launch / its CUDA-event
-duration against the measured HBM copy bandwidth. ``e2e``: the same step fed from pinned
-host memory (spike input as bytes, target rates), with the loss and gradient read back;
-each step's input is copied on a second stream while the previous step computes.
-``cpu_baseline``: the oracle (the C restatement of the reference's time loop) on a
-bounded sample of the same network on the host cores. ``--impl reference`` times that
-CPU implementation alone.
+duration against the measured HBM copy bandwidth. ``e2e``: the same step through the
+public API fed from pinned host memory (the spike input as bytes, and the target rates
+for c2), each step's (or engine call's) input copied on a second stream while the
+previous one computes, and its result (spike count, or loss and learnt parameters)
+read back. ``cpu_baseline``: the oracle (the C restatement of the reference's time
+loop) on a bounded sample of the same network on the host cores. ``--impl reference``
+times that CPU implementation alone (and, for c1 / c2 where the reference's package is
+installed under ``baseline/_ref``, the reference's own ``dynamics.simulate``).
 """
 
 from __future__ import annotations
@@ -51,11 +62,12 @@ def parse():
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
-    ap.add_argument("--config", default="c2", choices=["c2", "c1", "c3", "c4", "c5"])
+    ap.add_argument("--config", default="c5", choices=["c5", "c2", "c1", "c3", "c4"])
     ap.add_argument("--chunk", type=int, default=None,
                     help="c3 / c4 / c5: steps per engine call, the state carried over (default 250 / 1000 / 1000)")
     ap.add_argument("--partition", action="store_true",
-                    help="c2 / c4 / c5 forward: the network's neurons partitioned over the ranks (strong scaling)")
+                    help="the network's neurons partitioned over the ranks (strong scaling; "
+                         "the default for c4 / c5 at N > 1)")
     ap.add_argument("--recurrent-gradients", action="store_true",
                     help="c2: gradients through the recurrent spikes (Drive.recurrent_gradients)")
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
@@ -203,26 +215,35 @@ def build(args, rank, device):
 
 
 def make_step(cfg, world, train: bool):
-    """``step(x, target) -> loss`` (or the spike count for a forward-only config)."""
+    """``step(x, target) -> result``: the loss (c2), or the final membrane state of a
+    forward-only configuration (the state a caller would carry to the next run)."""
     from wiretorch_b200 import configs, engine, filtering
 
     v0, g0, kw0 = cfg.state()
     if cfg.name in ("c3", "c4", "c5"):
-        def forward_chunks(x, target=None):
-            """The T steps as engine calls of x.shape[1] steps, the state carried over."""
+        def forward_chunks(x, target=None, fetch=None):
+            """The T steps as engine calls of x.shape[1] steps, the state carried over;
+            ``fetch`` (a ``Prefetcher``) gives each call's input (default: ``x`` for
+            every call)."""
             v, g, kw = v0, g0, kw0
             with torch.no_grad():
-                for _ in range(cfg.T // x.shape[1]):
-                    run = engine.simulate(v, g, x, cfg.drive, cfg.p, **kw)
+                for i in range(cfg.T // x.shape[1]):
+                    xi = x if fetch is None else fetch.get()
+                    if fetch is not None:
+                        fetch.prefetch()  # the next call's input, copied while this one runs
+                    run = engine.simulate(v, g, xi, cfg.drive, cfg.p, **kw)
                     v, g, kw = run.v, run.syn, cfg.carried(run)
-            return v.sum()
+            return v
 
         return forward_chunks, None
     if not train:
-        def forward(x, target=None):
+        def forward(x, target=None, fetch=None):
+            xi = x if fetch is None else fetch.get()
+            if fetch is not None:
+                fetch.prefetch()
             with torch.no_grad():
-                run = engine.simulate(v0, g0, x, cfg.drive, cfg.p, **kw0)
-            return run.output.sum()
+                run = engine.simulate(v0, g0, xi, cfg.drive, cfg.p, **kw0)
+            return run.v
 
         return forward, None
     log_sf = torch.zeros(cfg.extra["log_sf_shape"], device=x_device(cfg), requires_grad=True)
@@ -246,6 +267,46 @@ def make_step(cfg, world, train: bool):
         return loss
 
     return step, log_sf
+
+
+class Prefetcher:
+    """Inputs of successive engine calls copied from pinned host memory on a copy stream,
+    one call ahead: ``get()`` returns the next call's device input (its copy ordered
+    before the current stream's use of it) and starts the copy of the one after, so that
+    it overlaps the call about to be launched."""
+
+    def __init__(self, host_chunks, device, convert):
+        self.host = host_chunks  # list of pinned host tensors, used in turn
+        self.device = device
+        self.convert = convert
+        self.stream = torch.cuda.Stream(device)
+        self.i = 0
+        self.pending = None
+
+    def _fetch(self):
+        host = self.host[self.i % len(self.host)]
+        self.i += 1
+        with torch.cuda.stream(self.stream):  # into a fresh buffer: no wait on the compute
+            dev = self.convert(host.to(self.device, non_blocking=True))
+            ready = torch.cuda.Event()
+            ready.record(self.stream)
+        return dev, ready
+
+    def start(self):
+        self.pending = self._fetch()
+
+    def get(self):
+        dev, ready = self.pending
+        main = torch.cuda.current_stream(self.device)
+        main.wait_event(ready)
+        dev.record_stream(main)
+        self.pending = None
+        return dev
+
+    def prefetch(self):
+        """Start the next copy (it runs beside the call that uses the current input)."""
+        if self.pending is None:
+            self.pending = self._fetch()
 
 
 def x_device(cfg):
@@ -302,10 +363,12 @@ def cpu_baseline(cfg, seconds_target=15.0, threads=None):
 
     threads = threads or os.cpu_count() or 1
     oracle.set_threads(threads)
-    cpu = _to_cpu(cfg)
     B = min(cfg.B, threads)
+    if _CPU_NET.get("cfg") is not cfg:  # the network on the host, built once per run
+        cpu = _to_cpu(cfg)
+        _CPU_NET.update(cfg=cfg, cpu=cpu, net=oracle.Network(cpu.drive, cpu.p, B, cfg.n_in))
+    cpu, net = _CPU_NET["cpu"], _CPU_NET["net"]
     T = 20
-    net = oracle.Network(cpu.drive, cpu.p, B, cfg.n_in)
     x = cfg.inputs(T=T, seed=99)[:B].cpu()
     v, g, kw = cpu.state()
     v, g = v[:B], g[:B]
@@ -320,7 +383,11 @@ def cpu_baseline(cfg, seconds_target=15.0, threads=None):
     net.simulate(x, v, g, **kw, track=False)
     el = time.perf_counter() - t0
     rate = B * T2 * cfg.N / el
-    return rate, threads, f"{B} trials x {T2} steps of the {cfg.name} network, forward only ({el:.1f} s)"
+    used = min(threads, B)  # the oracle runs its trials in parallel, one thread each
+    return rate, used, f"{B} trials x {T2} steps of the {cfg.name} network, forward only ({el:.1f} s)"
+
+
+_CPU_NET: dict = {}
 
 
 def _to_cpu(cfg):
@@ -352,30 +419,93 @@ def _to_cpu(cfg):
 
 
 def run_reference(args, rank, world):
-    """``--impl reference``: the CPU implementation (the oracle port of the reference's
-    time loop) on the host cores; rank 0 only."""
+    """``--impl reference``: the CPU implementation of the path on the host cores, rank 0
+    only: the oracle (the C restatement of the reference's time loop, forward only), each
+    step a bounded sample of the configuration's trials and steps; for c1 / c2 also the
+    reference's own ``dynamics.simulate`` when its package is installed under
+    ``baseline/_ref`` (a bounded sample too)."""
     if rank != 0:
         return
     device = "cuda" if torch.cuda.is_available() else "cpu"
     cfg, _ = build(args, 0, device)
-    for _ in range(max(args.warmup, 0)):
-        pass
-    rates = []
+    per_step = max(5.0, 60.0 / max(args.steps, 1))
+    for _ in range(max(args.warmup, 0)):  # warm-up: a short sample of the same run
+        cpu_baseline(cfg, seconds_target=1.0)
+    rates, cores, sample = [], 1, ""
     for _ in range(max(args.steps, 1)):
-        rate, cores, sample = cpu_baseline(cfg, seconds_target=max(5.0, 60.0 / max(args.steps, 1)))
+        rate, cores, sample = cpu_baseline(cfg, seconds_target=per_step)
         rates.append(rate)
     value = statistics.median(rates)
     line = {
         "impl": "reference", "metric": "neuron-steps/s", "value": value, "unit": "neuron-steps/s",
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
-        "data": "synthetic", "config": config_of(args, cfg, world=1),
+        "data": "synthetic", "config": {**config_of(args, cfg, world=1),
+                                        "workload": f"{cfg.name}: CPU forward simulation, sample: {sample}"},
         "cpu_baseline": {"value": value, "unit": "neuron-steps/s", "cores": cores,
                          "kind": "port", "sample": sample},
         "e2e": {"value": value, "unit": "neuron-steps/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
     }  # fmt: skip
+    ref = reference_dynamics_baseline(args, cfg)
+    if ref is not None:
+        line["reference_dynamics"] = ref
     print(json.dumps(line))
+
+
+def reference_dynamics_baseline(args, cfg):
+    """The reference's own CPU path, ``conductance/dynamics.py:146-237`` ``simulate``,
+    imported from ``baseline/_ref`` (its package installed there), on a bounded sample
+    of the configuration with dense weights, as its networks hand them over; forward
+    only. None where it does not apply; a note where it cannot run."""
+    if cfg.name in ("c3", "c4", "c5"):
+        dense = {"c3": "10 GB", "c4": "77 GB", "c5": "4 TB"}[cfg.name]
+        return {"unavailable": f"the reference's dense weights for {cfg.name} ({dense}) do not fit on the host"}
+    ref_dir = ROOT / "baseline" / "_ref"
+    if not ref_dir.exists():
+        return {"unavailable": "the reference package is not installed under baseline/_ref"}
+    sys.path.insert(0, str(ref_dir))
+    try:
+        from wiretorch.network_simulators import network as ref_net
+        from wiretorch.network_simulators.conductance import dynamics as ref_dyn
+    except Exception as e:  # noqa: BLE001
+        return {"unavailable": f"importing the reference failed: {type(e).__name__}: {e}"}
+    cpu = _to_cpu(cfg)
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+
+    def dense_of(W):
+        if not hasattr(W, "row_ptr"):
+            return W
+        n_rows, N = W.shape
+        out = torch.zeros(n_rows, N)
+        rows = torch.repeat_interleave(torch.arange(n_rows), W.row_ptr[1:] - W.row_ptr[:-1])
+        out.index_put_((rows, W.cols.long()), W.values, accumulate=True)
+        return out
+
+    drive = ref_net.Drive(made=cpu.drive.made, scale=cpu.drive.scale,
+                          recurrent=[(r, dense_of(W)) for r, W in cpu.drive.recurrent],
+                          feedforward=[(r, dense_of(W)) for r, W in cpu.drive.feedforward])  # fmt: skip
+    fields = ("theta", "U_reset", "E_L", "C_m", "beta", "E_syn", "g_clip", "decay", "jump", "dt",
+              "surr_scale", "n_ref", "mg_c", "mg_a", "adapt", "adapt_decay", "E_adapt")  # fmt: skip
+    p = ref_dyn.Physiology(**{f: getattr(cpu.p, f) for f in fields}, spike_mode=cpu.p.spike_mode)
+    v, g, kw = cpu.state()
+
+    def timed(T):
+        x = cfg.inputs(T=T, seed=99).cpu()
+        t0 = time.perf_counter()
+        with torch.no_grad():
+            ref_dyn.simulate(v, g, x, drive, p, **kw)
+        return time.perf_counter() - t0
+
+    timed(2)  # warm-up
+    T = 5
+    el = timed(T)
+    T = int(min(cfg.T, max(T, T * 15.0 / max(el, 1e-3))))
+    el = timed(T)
+    return {"value": cfg.B * cfg.N * T / el, "unit": "neuron-steps/s", "cores": threads,
+            "kind": "reference", "sample": f"{cfg.B} trials x {T} steps of the {cfg.name} network, forward only, "
+                                            f"dense weights ({el:.1f} s)"}  # fmt: skip
 
 
 def config_of(args, cfg, world):
@@ -392,30 +522,51 @@ def config_of(args, cfg, world):
     return c
 
 
-def main_partition(args, rank, world, local):
-    """``--partition``: one network (c2, c4 or c5, forward only) with its neurons partitioned
-    over the ranks, each step's spikes exchanged by peer stores inside the forward kernel.
-    Total work is fixed as ranks are added (strong scaling)."""
-    from wiretorch_b200 import _lib, partition
+def local_out_degree(d_loc, n_src, n_in, device):
+    """Per source (neurons, then input columns) its edges onto this rank's block."""
+    deg = torch.zeros(n_src + n_in, dtype=torch.float64, device=device)
+    for side, off in ((d_loc.recurrent, 0), (d_loc.feedforward, n_src)):
+        for rows, W in side:
+            deg.index_add_(0, rows.to(device) + off, torch.diff(W.row_ptr).double().to(device))
+    return deg
 
+
+def main_partition(args, rank, world, local):
+    """The network's neurons partitioned over the ranks (c4 / c5 by default at N > 1, or
+    ``--partition``), forward only, each step's spikes exchanged by peer stores inside
+    the forward kernel. Total work is fixed as ranks are added (strong scaling)."""
+    from wiretorch_b200 import _lib, engine, partition
+
+    engine.DEFER_CHECKS = True
     device = torch.device("cuda", local)
     torch.cuda.set_device(device)
     cfg, x = build(args, 0, device)  # every rank: the same network and input
     part = partition.Partition(cfg.N, cfg.B)
     chunked = cfg.name in ("c4", "c5")
+    calls = cfg.T // x.shape[1] if chunked else 1
 
-    def step():
+    def step(fetch=None):
         v, g, kw = cfg.state()
         with torch.no_grad():
-            for _ in range(cfg.T // x.shape[1] if chunked else 1):
-                run = partition.simulate(part, v, g, x, cfg.drive, cfg.p, **kw)
+            for _ in range(calls):
+                xi = x if fetch is None else fetch.get()
+                run = partition.simulate(part, v, g, xi, cfg.drive, cfg.p, **kw)
+                if fetch is not None:  # after the launch: the copy runs beside this call
+                    fetch.prefetch()
                 v, g, kw = run.v, run.syn, cfg.carried(run)
         return run
 
     for _ in range(max(args.warmup, 3)):
         step()
     torch.cuda.synchronize()
+    # synaptic events of one untimed step, counted on the device (edges onto this block)
+    edges = torch.zeros(2, dtype=torch.int64, device=device)
+    engine.EDGE_COUNTER = edges
+    step()
+    torch.cuda.synchronize()
+    engine.EDGE_COUNTER = None
     _lib.TIMER = {}
+    launches0 = _lib.LAUNCHES
     barrier(world)
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with Clocks(local) as clocks:
@@ -425,23 +576,73 @@ def main_partition(args, rank, world, local):
         end.record()
         torch.cuda.synchronize()
     barrier(world)
+    launches = _lib.LAUNCHES - launches0
     timer, _lib.TIMER = _lib.TIMER, None
     elapsed_max = max_over_ranks(start.elapsed_time(end) / 1000.0, world)
     kernel = {k: sum(a.elapsed_time(b) for a, b in v) / len(v) for k, v in timer.items()}
-    neuron_steps = cfg.B * cfg.N * cfg.T * args.steps  # the one network, whatever the ranks
+    K = args.steps
+    neuron_steps = cfg.B * cfg.N * cfg.T * K  # the one network, whatever the ranks
     spikes = sum_over_ranks(float(run.output.sum()), world)
+    rec_edges = sum_over_ranks(float(edges[0]) * K, world)
+    in_edges = sum_over_ranks(float(edges[1]) * K, world)
+
+    # ---- roofline of this rank's forward launch (its block's share of the bytes) ----
+    key = next(k for k in partition._LOCAL if k[2] == part.rank)
+    d_loc, p_loc, plan = partition._LOCAL[key]["local"]
+    n_b = part.n1 - part.n0
+    T = x.shape[1]
+    per = 8 + 16 * plan.ch.Sp + 2 + 1 / 8 + (8 if cfg.p.adapt is not None else 0)
+    gating = cfg.B * T * cfg.extra["gating"].shape[1] * 8 / world if "gating" in cfg.extra else 0
+    edge_bytes = float(edges[0] + edges[1]) / calls * 8  # this block's edges, per trial-event
+    fwd_bytes = cfg.B * T * n_b * per + cfg.B * T * cfg.n_in * 4 + edge_bytes + gating
+    peak, peak_kind = measured_peak()
+    launch_ms = max_over_ranks(kernel["wt_forward"], world)
+    roofline = {
+        "kernel": f"wt_forward (persistent forward step kernel, one of {world} neuron blocks)",
+        "bound": "hbm", "achieved": fwd_bytes / (launch_ms / 1000) / 1e9, "peak": peak, "unit": "GB/s",
+        "frac": fwd_bytes / (launch_ms / 1000) / 1e9 / peak, "peak_kind": peak_kind, "traffic": None,
+        "algorithmic_bytes_per_launch": fwd_bytes, "launch_ms": launch_ms,
+        "edges_counted": "per trial-event onto this rank's block (at C5's rates a source rarely fires in "
+                         "two trials at one step)",
+    }  # fmt: skip
+
+    # ---- end to end: each call's input from pinned host memory, the block's state read back ----
+    e2e = None
+    if not args.no_e2e:
+        x_host = [(x.cpu() != 0).to(torch.uint8).pin_memory()]
+        out_host = torch.empty((cfg.B, n_b), pin_memory=True)
+        fetch = Prefetcher(x_host, device, lambda t: t.float())
+        fetch.start()
+        out_host.copy_(step(fetch).v, non_blocking=True)
+        torch.cuda.synchronize()
+        barrier(world)
+        s2, e2 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s2.record()
+        for _ in range(K):
+            out_host.copy_(step(fetch).v, non_blocking=True)
+        e2.record()
+        torch.cuda.synchronize()
+        e2e_el = max_over_ranks(s2.elapsed_time(e2) / 1000.0, world)
+        e2e = {"value": neuron_steps / e2e_el, "unit": "neuron-steps/s",
+               "h2d_bytes_per_step": calls * x_host[0].numel(), "d2h_bytes_per_step": out_host.numel() * 4,
+               "ms_per_step": e2e_el / K * 1000.0,
+               "note": "every rank copies the replicated input; bytes are per rank"}  # fmt: skip
+    engine.check_errors()
     if rank == 0:
         print(json.dumps({
             "metric": "neuron-steps/s", "value": neuron_steps / elapsed_max, "unit": "neuron-steps/s",
-            "n_gpus": world, "steps": args.steps, "warmup": max(args.warmup, 3),
-            "ms_per_step": elapsed_max / args.steps * 1000.0, "higher_is_better": True, "scaling": "strong",
+            "n_gpus": world, "steps": K, "warmup": max(args.warmup, 3),
+            "ms_per_step": elapsed_max / K * 1000.0, "higher_is_better": True, "scaling": "strong",
             "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded Poisson input, seeded connectome)",
             "config": {**config_of(args, cfg, world), "parallelism": f"neuron-partition x{world}",
                        "global_batch": cfg.B,
                        "workload": f"{cfg.name}: {cfg.N} neurons ({world} blocks), {cfg.B} trials, {cfg.T} steps "
-                                   f"of 0.1 ms, forward, spikes exchanged each step by peer stores"},
+                                   f"of 0.1 ms, forward, {calls} calls of {x.shape[1]} steps, "
+                                   f"spikes exchanged each step by peer stores"},
+            "synaptic_events_per_s": rec_edges / elapsed_max, "input_events_per_s": in_edges / elapsed_max,
             "mean_rate_hz": spikes / (cfg.B * cfg.N * x.shape[1]) / (DT / 1000.0),
-            "kernel_ms": kernel, "clocks": clocks.summary(),
+            "roofline": roofline, "kernel_ms": kernel, "gpu_launches": launches,
+            "clocks": clocks.summary(), "e2e": e2e, "cpu_baseline": None,
         }))  # fmt: skip
     barrier(world)
     part.close()
@@ -450,20 +651,22 @@ def main_partition(args, rank, world, local):
 def main():
     args = parse()
     rank, world, local = dist_setup(args)
-    if args.partition and args.impl != "reference":
-        main_partition(args, rank, world, local)
+    try:
+        if args.impl == "reference":
+            run_reference(args, rank, world)
+        elif args.partition or (world > 1 and args.config in ("c4", "c5")):
+            main_partition(args, rank, world, local)
+        else:
+            main_single(args, rank, world, local)
+    finally:
         if world > 1:
             import torch.distributed as dist
 
             dist.destroy_process_group()
-        return
-    if args.impl == "reference":
-        run_reference(args, rank, world)
-        if world > 1:
-            import torch.distributed as dist
 
-            dist.destroy_process_group()
-        return
+
+def main_single(args, rank, world, local):
+    """One GPU per rank, each rank its own trials (weak scaling at N > 1)."""
     from wiretorch_b200 import _lib, engine
 
     # the forward's device error word is read behind the launches (no host
@@ -522,13 +725,9 @@ def main():
 
     # ---- the dominant kernel's roofline ----
     kernel_ms = {k: sum(s.elapsed_time(e) for s, e in v) / len(v) for k, v in timer.items()}
-    kernel_total = {k: sum(s.elapsed_time(e) for s, e in v) for k, v in timer.items()}
-    dominant = max(kernel_total, key=kernel_total.get)
     with torch.no_grad():
-        from wiretorch_b200 import engine as eng
-
         v0, g0, kw0 = cfg.state()
-        run = eng.simulate(v0, g0, x, cfg.drive, cfg.p, **kw0)
+        run = engine.simulate(v0, g0, x, cfg.drive, cfg.p, **kw0)
     if factorised:
         kname = "wt_lowrank_forward"
         fwd_bytes = factorised_bytes(cfg, x.shape[1])
@@ -537,6 +736,8 @@ def main():
         kname = "wt_forward"
         fwd_bytes = forward_bytes(cfg, plan, x.shape[1], train, fired_edges_once(cfg, run.output, x))
         kdesc = "wt_forward (persistent forward step kernel)"
+    mean_rate = float(run.output.mean()) / (DT / 1000.0)
+    del run
     peak, peak_kind = measured_peak()
     fwd_s = kernel_ms[kname] / 1000.0
     roofline = {
@@ -558,58 +759,27 @@ def main():
     # ---- end to end from host buffers ----
     e2e = None
     if not args.no_e2e:
-        x_host = (x.cpu() != 0).to(torch.uint8).pin_memory()
-        tgt_host = cfg.extra["target_rates"].cpu().pin_memory() if train else None
-        out_host = torch.empty(1 + (log_sf.numel() if train else 0), pin_memory=True)
-        h2d = x_host.numel() + (tgt_host.numel() * 4 if train else 0)
-        d2h = out_host.numel() * 4
-
-        # Each step's input crosses from pinned host memory on a copy stream while the
-        # previous step computes (the copy of step k + 1 overlaps step k); every copy lies
-        # inside the timed region, between its two events.
-        copy_stream = torch.cuda.Stream(device)
-        main = torch.cuda.current_stream(device)
-
-        def fetch(after):
-            copy_stream.wait_event(after)
-            with torch.cuda.stream(copy_stream):
-                xd = x_host.to(device, non_blocking=True).float()
-                r = tgt_host.to(device, non_blocking=True) * (DT / 1000.0) if train else None
-                ready = torch.cuda.Event()
-                ready.record(copy_stream)
-            return xd, r, ready
-
-        def e2e_step(inputs):
-            xd, r, ready = inputs
-            main.wait_event(ready)
-            xd.record_stream(main)
-            if train:
-                r.record_stream(main)
-                loss = step(xd, r[:, None, :].expand(cfg.B, cfg.T, cfg.N))
-                res = torch.cat([loss.detach().reshape(1), log_sf.detach().reshape(-1)])
-            else:
-                res = step(xd).reshape(1).float()
-            out_host.copy_(res, non_blocking=True)
-
-        first = torch.cuda.Event()
-        first.record(main)
-        e2e_step(fetch(first))
-        torch.cuda.synchronize()
-        barrier(world)
-        s2, e2 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        s2.record()
-        pending = fetch(s2)
-        for k in range(K):
-            inputs = pending
-            if k + 1 < K:
-                pending = fetch(inputs[2])  # the next step's input, behind this one's copy
-            e2e_step(inputs)
-        e2.record()
-        torch.cuda.synchronize()
-        e2e_el = max_over_ranks(s2.elapsed_time(e2) / 1000.0, world)
-        e2e = {"value": neuron_steps / e2e_el, "unit": "neuron-steps/s",
-               "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-               "ms_per_step": e2e_el / K * 1000.0}  # fmt: skip
+        x_host = [(x.cpu() != 0).to(torch.uint8).pin_memory()]
+        calls = cfg.T // x.shape[1] if cfg.name in ("c3", "c4", "c5") else 1
+        if train:
+            e2e = e2e_training(cfg, step, log_sf, x_host[0], device, world, K, neuron_steps)
+        else:
+            fetch = Prefetcher(x_host, device, lambda t: t.float())
+            out_host = torch.empty((cfg.B, cfg.N), pin_memory=True)
+            fetch.start()
+            out_host.copy_(step(x, fetch=fetch), non_blocking=True)
+            torch.cuda.synchronize()
+            barrier(world)
+            s2, e2 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s2.record()
+            for _ in range(K):  # the final membrane state of every step read back
+                out_host.copy_(step(x, fetch=fetch), non_blocking=True)
+            e2.record()
+            torch.cuda.synchronize()
+            e2e_el = max_over_ranks(s2.elapsed_time(e2) / 1000.0, world)
+            e2e = {"value": neuron_steps / e2e_el, "unit": "neuron-steps/s",
+                   "h2d_bytes_per_step": calls * x_host[0].numel(), "d2h_bytes_per_step": out_host.numel() * 4,
+                   "ms_per_step": e2e_el / K * 1000.0}  # fmt: skip
 
     engine.check_errors()  # every deferred device error check of the runs above
     cpu = None
@@ -626,15 +796,45 @@ def main():
             "config": config_of(args, cfg, world),
             "synaptic_events_per_s": rec_edges_all / elapsed_max,
             "input_events_per_s": in_edges_all / elapsed_max,
-            "mean_rate_hz": float(run.output.mean()) / (DT / 1000.0),
+            "mean_rate_hz": mean_rate,
             "roofline": roofline, "kernel_ms": kernel_ms, "gpu_launches": launches,
             "clocks": clock, "e2e": e2e, "cpu_baseline": cpu,
         }  # fmt: skip
         print(json.dumps(line))
-    if world > 1:
-        import torch.distributed as dist
 
-        dist.destroy_process_group()
+
+def e2e_training(cfg, step, log_sf, x_host, device, world, K, neuron_steps):
+    """The c2 training step fed from pinned host memory (spike input as bytes, target
+    rates), the loss and the learnt scales read back every step; each step's input
+    copied on a second stream while the previous step computes."""
+    tgt_host = cfg.extra["target_rates"].cpu().pin_memory()
+    out_host = torch.empty(1 + log_sf.numel(), pin_memory=True)
+    h2d = x_host.numel() + tgt_host.numel() * 4
+    d2h = out_host.numel() * 4
+    fetch_x = Prefetcher([x_host], device, lambda t: t.float())
+    fetch_t = Prefetcher([tgt_host], device, lambda t: t * (DT / 1000.0))
+
+    def e2e_step():
+        xd, r = fetch_x.get(), fetch_t.get()
+        fetch_x.prefetch()
+        fetch_t.prefetch()
+        loss = step(xd, r[:, None, :].expand(cfg.B, cfg.T, cfg.N))
+        out_host.copy_(torch.cat([loss.detach().reshape(1), log_sf.detach().reshape(-1)]), non_blocking=True)
+
+    fetch_x.start()
+    fetch_t.start()
+    e2e_step()
+    torch.cuda.synchronize()
+    barrier(world)
+    s2, e2 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s2.record()
+    for _ in range(K):
+        e2e_step()
+    e2.record()
+    torch.cuda.synchronize()
+    e2e_el = max_over_ranks(s2.elapsed_time(e2) / 1000.0, world)
+    return {"value": neuron_steps / e2e_el, "unit": "neuron-steps/s", "h2d_bytes_per_step": h2d,
+            "d2h_bytes_per_step": d2h, "ms_per_step": e2e_el / K * 1000.0}
 
 
 if __name__ == "__main__":

@@ -9,6 +9,11 @@ every differentiable input of the engine. Cases that come from a recording of th
 reference's own test suite also carry that recording (``rec.*``): its spike raster,
 voltages and the state at every window start.
 
+The configuration (``config_*``) and statistics (``statistics_*``) cases store their
+weights as CSR rows (``SparseRows``) and their 0/1 inputs bit-packed (``x_bits``), and
+record voltages every ``snap`` steps instead of every step. The loss cases
+(``loss_*``) are plain arrays, read with ``numpy.load``.
+
 ``make_golden.py`` writes them; the tests read them with ``load``.
 """
 
@@ -20,7 +25,7 @@ from pathlib import Path
 import numpy as np
 import torch
 
-from wiretorch_b200.types import Drive, Gate, Physiology
+from wiretorch_b200.types import Drive, Gate, Physiology, SparseRows
 
 GOLDEN = Path(__file__).parent / "golden"
 
@@ -51,8 +56,14 @@ def save(path: Path, *, drive, p, inputs: dict, outputs: dict, grads: dict,
 
     def source(W):
         if id(W) not in sources:
-            sources[id(W)] = len(sources)
-            arrays[f"net.W.{sources[id(W)]}"] = _np(W).astype(np.float32)
+            i = sources[id(W)] = len(sources)
+            if isinstance(W, SparseRows):  # CSR rows: the configuration-sized networks
+                arrays[f"net.Wcsr.{i}.row_ptr"] = _np(W.row_ptr).astype(np.int64)
+                arrays[f"net.Wcsr.{i}.cols"] = _np(W.cols).astype(np.int32)
+                arrays[f"net.Wcsr.{i}.values"] = _np(W.values).astype(np.float32)
+                arrays[f"net.Wcsr.{i}.n_targets"] = np.int64(W.n_targets)
+            else:
+                arrays[f"net.W.{i}"] = _np(W).astype(np.float32)
         return sources[id(W)]
 
     meta = dict(meta)
@@ -84,7 +95,12 @@ def save(path: Path, *, drive, p, inputs: dict, outputs: dict, grads: dict,
         for key, value in group.items():
             if value is None:
                 continue
-            if key.endswith("spikes"):
+            if key.startswith("x") and meta.get("x_bits"):  # 0/1 input trains, bit-packed
+                a = _np(value)
+                assert np.isin(a, (0.0, 1.0)).all()
+                arrays[f"{prefix}.{key}.xbits"] = pack(a)
+                arrays[f"{prefix}.{key}.xshape"] = np.array(a.shape, np.int64)
+            elif key.endswith("spikes"):
                 arrays[f"{prefix}.{key}.bits"] = pack(_np(value))
             else:
                 arrays[f"{prefix}.{key}"] = _np(value)
@@ -108,7 +124,12 @@ def load(name: str, device="cpu"):
 
     def W(i):
         if i not in weights:
-            weights[i] = t(arrays[f"net.W.{i}"])
+            if f"net.Wcsr.{i}.row_ptr" in arrays:
+                weights[i] = SparseRows(t(arrays[f"net.Wcsr.{i}.row_ptr"]), t(arrays[f"net.Wcsr.{i}.cols"]),
+                                        t(arrays[f"net.Wcsr.{i}.values"]),
+                                        int(arrays[f"net.Wcsr.{i}.n_targets"]))  # fmt: skip
+            else:
+                weights[i] = t(arrays[f"net.W.{i}"])
         return weights[i]
 
     recurrent = [(t(arrays[f"net.rec_rows.{k}"]), W(i)) for k, i in enumerate(meta["rec"])]
@@ -131,14 +152,43 @@ def load(name: str, device="cpu"):
     p = Physiology(**phys, spike_mode=meta["spike_mode"])
     data = {}
     for key, value in arrays.items():
-        if key.startswith(("net.", "phys.")) or key.endswith(".shape"):
+        if key.startswith(("net.", "phys.")) or key.endswith((".shape", ".xshape")):
             continue
-        if key.endswith(".bits"):
+        if key.endswith(".xbits"):
+            shape = tuple(arrays[key.removesuffix(".xbits") + ".xshape"])
+            data[key.removesuffix(".xbits")] = unpack(value, shape[-1]).astype(np.float32)
+        elif key.endswith(".bits"):
             data[key.removesuffix(".bits")] = unpack(value, N)
         else:
             data[key] = value
     return drive, p, data, meta
 
 
+KINDS = ("config_", "statistics_", "loss_")
+
+
 def cases() -> list[str]:
-    return sorted(p.stem for p in GOLDEN.glob("*.npz"))
+    """The scenario cases (one engine call of a reference test network each)."""
+    return sorted(p.stem for p in GOLDEN.glob("*.npz") if not p.stem.startswith(KINDS))
+
+
+def config_cases() -> list[str]:
+    """The benchmark configurations' networks run by the reference (``config_c*``)."""
+    return sorted(p.stem for p in GOLDEN.glob("config_*.npz"))
+
+
+def statistics_cases() -> list[str]:
+    """The reference's at-scale statistics networks (``statistics_*``)."""
+    return sorted(p.stem for p in GOLDEN.glob("statistics_*.npz"))
+
+
+def first_divergence(a, b) -> int:
+    """The first step (axis 1) at which two ``(B, T, N)`` rasters differ (T if none)."""
+    diff = (np.asarray(a) != np.asarray(b)).any(axis=(0, 2))
+    return int(np.argmax(diff)) if diff.any() else diff.shape[0]
+
+
+def population_rates(spikes, types, dt_ms) -> np.ndarray:
+    """Mean firing rate (Hz) of each cell type over trials, steps and its neurons."""
+    rates = np.asarray(spikes, np.float64).mean(axis=(0, 1)) / (dt_ms / 1000.0)
+    return np.array([rates[types == t].mean() for t in np.unique(types)])

@@ -45,15 +45,16 @@ def _pooled(g, pools):
 
 
 def compare(engine_sim, net, drive, p, x, v, g, kw, window=10, margin=1e-3, v_atol=2e-4,
-            g_rtol=1e-5, g_atol=1e-6, pools=None):  # fmt: skip
+            g_rtol=1e-5, g_atol=1e-6, pools=None, oracle=None):  # fmt: skip
     """Lockstep of ``engine_sim(v, g, x_window, kw) -> Run`` against the oracle.
 
     ``pools``: the engine's pooled channels (lists of synapse types), whose state holds
     each pool's sum at its first member; the conductances are then compared pool by pool.
+    ``oracle``: the result of ``oracle_windows`` for these inputs, if already run.
 
     Returns ``(excused, trial_windows, worst_dv, worst_dg)``; raises AssertionError on a
     flip away from threshold or a trace outside tolerance."""
-    states, spikes, v_track = oracle_windows(net, x, v, g, kw, window)
+    states, spikes, v_track = oracle if oracle is not None else oracle_windows(net, x, v, g, kw, window)
     theta = p.theta.detach().cpu().numpy()
     dev = x.device
     B = x.shape[0]

@@ -157,7 +157,7 @@ def c1(B=8, T=1000, seed=0, device="cuda", w_in=15.0, g_L=10.0):
 
 
 def c2(B=64, T=500, seed=0, device="cuda", n_in=2000, p_in=0.05, w_mu=-1.0, w_mu_i=0.6,
-       w_in_mu=-0.5, g_L=10.0, n_types=40, frac_e_types=0.75):  # fmt: skip
+       w_in_mu=-0.5, g_L=10.0, n_types=40, frac_e_types=0.75, N=20000, p_max=0.05):  # fmt: skip
     """N=20,000 neurons in 40 synthetic cell types (type sizes multinomial; 75% of the types
     excitatory), per-type-pair connection probability ~U(0, 0.05), log-normal per-synapse
     weights (sigma=1, nS; mu=w_mu from excitatory types, w_mu_i = w_mu + ln 5 from
@@ -170,15 +170,17 @@ def c2(B=64, T=500, seed=0, device="cuda", n_in=2000, p_in=0.05, w_mu=-1.0, w_mu
     Every cell type makes its own synapse type, as the reference's synapse registry does
     (one per source cell type and synapse name): 30 AMPA-like (tau 5 ms, E 0 mV), 10
     GABA-like (tau 10 ms, E -80 mV), and the inputs' AMPA. ``extra["log_sf_shape"]``:
-    the learnt per-pair log scale, (41 source types, 40 target types)."""
+    the learnt per-pair log scale, (41 source types, 40 target types).
+
+    ``N`` and ``p_max`` (pair probabilities ~ U(0, p_max)) make smaller networks of the
+    same construction, for tests."""
     dev = torch.device(device)
     gen = torch.Generator(device=dev).manual_seed(seed)
     rng = np.random.default_rng(seed)
-    N = 20000
     sizes = rng.multinomial(N, np.full(n_types, 1.0 / n_types))
     starts = np.concatenate([[0], np.cumsum(sizes)])
     n_e_types = int(round(frac_e_types * n_types))
-    p_pair = rng.uniform(0.0, 0.05, (n_types, n_types))
+    p_pair = rng.uniform(0.0, p_max, (n_types, n_types))
     rows_l, pathways = [], []
     srcs, dsts = [], []
     for a in range(n_types):
