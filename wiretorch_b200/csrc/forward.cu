@@ -271,21 +271,21 @@ __device__ __forceinline__ float spike_of(float v, float theta, int counter, flo
 
 static_assert(WT_CHUNK_EDGES <= 128, "a chunk's edges take at most four per lane");
 // Feature bits of a specialised kernel: the refractory period, saving for the backward
-// pass, the Mg block, presynaptic gating and adaptation known at compile time;
-// everything else (escape noise, probabilities, tracking, saved input, partitions) in
-// the generic variant, tested at run time.
-constexpr int kRef = 1, kSave = 2, kGeneric = 4, kMg = 8, kGate = 16, kAdapt = 32;
+// pass, the Mg block, presynaptic gating, adaptation and one rank of a neuron partition
+// known at compile time; everything else (escape noise, probabilities, tracking, saved
+// input) in the generic variant, tested at run time.
+constexpr int kRef = 1, kSave = 2, kGeneric = 4, kMg = 8, kGate = 16, kAdapt = 32, kPart = 64;
 
 // Warps per block of the forward kernel (one block per SM): 24 for the specialised
 // kernels of up to four channels (80 registers a thread, as good as no spill), WT_GATE_WARPS
-// for those with the Mg block, gating or adaptation, 16 for the others (up to 128
-// registers).
+// for those with the Mg block, gating, adaptation or a partition, 16 for the others (up
+// to 128 registers).
 #ifndef WT_GATE_WARPS
 #define WT_GATE_WARPS 20
 #endif
 template <int S, int FEAT>
 constexpr int warps_of() {
-    return ((FEAT & kGeneric) == 0 && S <= 4) ? ((FEAT & (kMg | kGate | kAdapt)) ? WT_GATE_WARPS : 24) : 16;
+    return ((FEAT & kGeneric) == 0 && S <= 4) ? ((FEAT & (kMg | kGate | kAdapt | kPart)) ? WT_GATE_WARPS : 24) : 16;
 }
 constexpr int kMaxRing = 4;               // deepest ring of staged items
 
@@ -331,7 +331,7 @@ __global__ void __launch_bounds__(warps_of<S, FEAT>() * 32, 1) forward_kernel(co
     const bool PROB = GEN && (flags & WT_F_PROB);
     const bool TRACK = GEN && (flags & WT_F_TRACK);
     const bool SAVE_IN = GEN && (flags & WT_F_SAVE_INPUT);
-    const bool PART = GEN && (flags & WT_F_PARTITION);
+    const bool PART = GEN ? (flags & WT_F_PARTITION) != 0 : (FEAT & kPart) != 0;
 
     const int B = net.B, N = net.N, n_in = net.n_in, C = net.C, T = run.T, Np = geo.Np;
     const int Nsrc = net.N_src > 0 ? net.N_src : N;  // neuron sources (all ranks' when partitioned)
@@ -1133,18 +1133,26 @@ static cudaError_t launch_sf(const WtNet &net, const WtForward &run, const WtWor
 // and saving as given; no other feature); everything else runs the generic kernel.
 template <int S>
 static cudaError_t launch_s(const WtNet &net, const WtForward &run, const WtWorkspace &ws, cudaStream_t st) {
-    const int generic = WT_F_SAMPLE | WT_F_PROB | WT_F_TRACK | WT_F_SAVE_INPUT | WT_F_PARTITION;
+    const int generic = WT_F_SAMPLE | WT_F_PROB | WT_F_TRACK | WT_F_SAVE_INPUT;
     const int feat = ((run.flags & WT_F_REFRACTORY) ? kRef : 0) | ((run.flags & WT_F_SAVE) ? kSave : 0) |
                      ((run.flags & WT_F_MG_BLOCK) ? kMg : 0) | ((run.flags & WT_F_GATED) ? kGate : 0) |
-                     ((run.flags & WT_F_ADAPT) ? kAdapt : 0);
+                     ((run.flags & WT_F_ADAPT) ? kAdapt : 0) | ((run.flags & WT_F_PARTITION) ? kPart : 0);
     // the Mg block, gating and adaptation are specialised for forward runs with a
     // refractory period (the large simulations' cases: Mg block and gating in any
-    // combination, or adaptation alone); other combinations with them run the generic
-    // kernel
-    const int extra = feat & (kMg | kGate | kAdapt);
+    // combination, or adaptation alone), and so are the ranks of a neuron partition;
+    // other combinations with them run the generic kernel
+    const int extra = feat & (kMg | kGate | kAdapt | kPart);
     if (S > 4 || (run.flags & generic) || (extra && (feat & (kRef | kSave)) != kRef) ||
-        ((extra & kAdapt) && extra != kAdapt))
+        ((extra & kAdapt) && (extra & ~kPart) != kAdapt))
         return launch_sf<S, kGeneric>(net, run, ws, st);
+    if (feat & kPart) {
+        switch (feat) {
+            case kRef | kPart: return launch_sf<S, kRef | kPart>(net, run, ws, st);
+            case kRef | kAdapt | kPart: return launch_sf<S, kRef | kAdapt | kPart>(net, run, ws, st);
+            case kRef | kMg | kGate | kPart: return launch_sf<S, kRef | kMg | kGate | kPart>(net, run, ws, st);
+            default: return launch_sf<S, kGeneric>(net, run, ws, st);
+        }
+    }
     switch (feat) {
         case 0: return launch_sf<S, 0>(net, run, ws, st);
         case kRef: return launch_sf<S, kRef>(net, run, ws, st);
