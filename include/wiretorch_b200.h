@@ -144,7 +144,19 @@ typedef struct {
      * source's gates from the spike words. */
     float *amps;
     float *peer_amps[8];
+    /* optional, instrumented runs: per step and warp of the grid, the global timer (ns)
+     * at the ends of the step's phases, (T, phase_warps, WT_PHASES); warps of the grid
+     * beyond phase_warps record nothing. NULL: no record. */
+    unsigned long long *phases;
+    int32_t phase_warps;
 } WtForward;
+
+/* The phases of a forward step that WtForward.phases records, in order: the step's
+ * start; the next step's input columns emitted; the early scatter done (the even warps
+ * of a block scatter before their items); the warp's items done (membrane update and
+ * spike emission); the late scatter done (the odd warps); the grid barrier passed; the
+ * spike exchange of a partitioned run done (its progress wait, barrier and emission). */
+#define WT_PHASES 7
 
 /* One scatter work item: a chunk of a source's edges, for one trial. */
 typedef struct {

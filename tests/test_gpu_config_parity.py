@@ -118,7 +118,7 @@ def test_config_c2_rate_loss_gradient_matches_the_reference(pool):
     finally:
         engine.POOL_SYNAPSES = False
     assert float(run.output.detach().sum()) == float(d["grad.spikes_sum"])
-    np.testing.assert_allclose(float(loss), float(d["grad.loss"]), rtol=1e-5)
+    np.testing.assert_allclose(float(loss.detach()), float(d["grad.loss"]), rtol=1e-5)
     ref = d["grad.log_sf"]
     got = log_sf.grad.cpu().numpy()
     assert np.abs(ref).max() > 0
@@ -299,4 +299,6 @@ def test_van_rossum_rate_loss_matches_the_reference_over_carried_chunks():
         assert np.abs(g - ref).max() <= 1e-4 * np.abs(ref).max()
         carried = torch.stack([loss_fn.prev_output_rise, loss_fn.prev_output_smooth, loss_fn.prev_target_rise,
                                loss_fn.prev_target_smooth]).cpu().numpy()  # fmt: skip
-        np.testing.assert_allclose(carried, d[f"carried.{c}"], rtol=1e-5, atol=1e-7)
+        # the state after up to 300 steps of a float32 recursion, against the reference's
+        # Toeplitz products: the same sums rounded in another order
+        np.testing.assert_allclose(carried, d[f"carried.{c}"], rtol=3e-5, atol=1e-7)

@@ -16,6 +16,7 @@ CHUNK_EDGES = 128
 EVENT_BYTES = 16  # sizeof(WtEvent)
 
 OK, ERR_ARGS, ERR_LAUNCH, ERR_BARRIER, ERR_EVENTS, ERR_FIXED_POINT, ERR_UNSUPPORTED = range(7)
+PHASES = 7  # WT_PHASES: the phases of a forward step that WtForward.phases records
 ERRORS = {
     ERR_ARGS: "inconsistent arguments",
     ERR_LAUNCH: "kernel launch failed",
@@ -64,6 +65,7 @@ class WtForward(C.Structure):
         ("words", P), ("peer_words", P * 8), ("progress", P), ("peer_progress", P * 8),
         ("n_ranks", C.c_int32), ("rank", C.c_int32), ("word0", C.c_int32), ("epoch", C.c_uint32),
         ("amps", P), ("peer_amps", P * 8),
+        ("phases", P), ("phase_warps", C.c_int32),
     ]  # fmt: skip
 
 

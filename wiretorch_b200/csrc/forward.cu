@@ -351,6 +351,17 @@ __global__ void __launch_bounds__(warps_of<S, FEAT>() * 32, 1) forward_kernel(co
     const int D = geo.D, ks = geo.ks, w_cnt = geo.w_cnt, w_ga = geo.w_ga, w_gd = geo.w_gd;
     const int slot_words = geo.slot_rows * 32;
     GridBarrier bar(ws.barrier, gridDim.x);
+    // instrumented runs: lane 0 of each warp stamps the end of each phase of a step
+    unsigned long long *const phases =
+        (run.phases && gwarp < run.phase_warps) ? run.phases + (size_t)gwarp * WT_PHASES : nullptr;
+    const size_t phase_row = (size_t)run.phase_warps * WT_PHASES;
+    auto stamp = [&](int t, int k) {
+        if (phases && lane == 0) {
+            unsigned long long g;
+            asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(g));
+            phases[(size_t)t * phase_row + k] = g;
+        }
+    };
 
     // Per channel: the input channel feeding it, that input's fixed-point scale, and the
     // state word of its rise component (-1: it does not decay and keeps none).
@@ -652,6 +663,7 @@ __global__ void __launch_bounds__(warps_of<S, FEAT>() * 32, 1) forward_kernel(co
         const bool emit_next = t + 1 < T;
         const bool has_x = t > 0;
         unsigned long long *Xprev = ws.X + (size_t)((t + 1) & 1) * C * BNp;  // X_{t-1}
+        stamp(t, 0);
         // The first D items' copies go out now and land while the warp scatters.
         Cursor qi = start;
         int wr = 0;
@@ -732,8 +744,10 @@ __global__ void __launch_bounds__(warps_of<S, FEAT>() * 32, 1) forward_kernel(co
                 }
             }
         };
+        stamp(t, 1);
         const bool scatter_late = (threadIdx.x >> 5) & 1;
         if (!scatter_late) scatter();
+        stamp(t, 2);
 
         // ---------------- the neurons: step t, and the spikes of step t + 1 ----------------
         Cursor q = start;
@@ -959,10 +973,14 @@ __global__ void __launch_bounds__(warps_of<S, FEAT>() * 32, 1) forward_kernel(co
             rp += ks * 32;
         }
         cp_async_wait(0);  // the last (empty) groups
+        stamp(t, 3);
         if (scatter_late) scatter();
+        stamp(t, 4);
         if (PART) __threadfence_system();
         if (!bar.sync(ws.err)) return;
+        stamp(t, 5);
         if (PART && emit_next && !exchange(t + 1)) return;
+        stamp(t, 6);
     }
 
     // The input of the last step completes the conductances the run leaves; resident

@@ -37,6 +37,11 @@ _PLANS: dict = {}
 #: traverses (recurrent, input): the synaptic events of the run, counted on the device.
 EDGE_COUNTER = None
 
+#: If set to a list, every forward launch appends to it a (T, warps, WT_PHASES) int64
+#: tensor: per step and warp of the grid the global timer (ns) at the end of each phase
+#: of the step (instrumented runs; see ``WT_PHASES`` in the C header).
+PHASE_RECORD = None
+
 
 def _key(drive, p, B, n_in, device, pool):
     pathways = list(drive.recurrent) + list(drive.feedforward)
@@ -234,6 +239,11 @@ def run_forward(plan, p, x, v, g, counter, g_a, gating, *, probabilities=False, 
     if part is not None:  # one rank of a neuron-partitioned run (wiretorch_b200.partition)
         flags |= _lib.F_PARTITION
         part.fill(run, plan)
+    if PHASE_RECORD is not None:  # instrumented run: every warp's phase stamps, every step
+        warps = torch.cuda.get_device_properties(device).multi_processor_count * 32
+        stamps = torch.zeros((T, warps, _lib.PHASES), dtype=torch.int64, device=device)
+        run.phases, run.phase_warps = stamps.data_ptr(), warps
+        PHASE_RECORD.append(stamps)
     run.flags = flags
     ws, w = _workspace(plan, T, device)
     out["_ws"] = ws
