@@ -247,6 +247,10 @@ typedef struct {
     int32_t t_lo, t_hi;
     float *adj;
     const float *R;
+    /* optional, a whole scan (no adj, t_lo 0, t_hi T): the same adjoints target-major,
+     * QT (C, N, B, Tp) with Tp = T rounded up to a multiple of 8 (entries past T are
+     * zero), for the edge gradients' target-by-target pass; with QT, Q may be NULL. */
+    float *QT;
 } WtBackward;
 
 /* Gradients carried along the connectome's edges, from the adjoints Q of a reverse scan:
@@ -271,10 +275,31 @@ typedef struct {
      * wt_edge_grads_scratch_words(net, T) words, and a work counter (1 word) */
     uint32_t *fired;
     uint32_t *work;
+    /* optional: g_scale and g_w target by target from QT (WtBackward.QT, Tp = T rounded
+     * up to 8) instead of source by source from Q: a block per target stages the
+     * target's adjoints of a slice of trials in shared memory (wt_edge_grads_slice_trials
+     * trials at a time) and sums every in-edge's events from there, so each adjoint is
+     * read from HBM once. The in-edges of each target, by pathway then edge (in_ptr
+     * (N + 1), and per in-edge its edge, its source and its pathway, (E_in) each; in_fcol
+     * its gating factor's column of f_saved, -1 ungated, or NULL when nothing is gated);
+     * scratch: ev_start ((N + n_in) (slices + 1)) and ev (ev_cap) for each source's events
+     * (b Tp + t) and where each slice of trials starts among them, in_acc (E_in) floats,
+     * and err: WT_ERR_EVENTS when the run's events exceed ev_cap (below 2^31). */
+    const float *QT;
+    const int32_t *in_ptr, *in_edge, *in_src, *in_path, *in_fcol;
+    int32_t *ev_start, *ev;
+    long long ev_cap;
+    float *in_acc;
+    int32_t *err;
 } WtEdgeGrads;
 
 /* 32-bit words of WtEdgeGrads.fired for a run of T steps. */
 int64_t wt_edge_grads_scratch_words(const WtNet *net, int32_t T);
+
+/* Trials per slice of the target-by-target edge gradients (WtEdgeGrads.QT) for a run of
+ * T steps; 0 when even one trial's adjoints of a target do not fit in shared memory (use
+ * Q, source by source). */
+int32_t wt_edge_grads_slice_trials(const WtNet *net, int32_t T);
 
 /* The reverse scan. Replaces `scan_backward` (conductance/kernels.py:382-568, driven by
  * conductance/engine.py:358-383 `_backward`). */

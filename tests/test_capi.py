@@ -14,7 +14,7 @@ HEADER = Path(__file__).parents[1] / "include" / "wiretorch_b200.h"
 
 def declared() -> list[str]:
     text = HEADER.read_text()
-    return sorted(set(re.findall(r"^\s*(?:int|const char \*)\s*(wt_\w+)\(", text, re.M)))
+    return sorted(set(re.findall(r"^\s*(?:int|int32_t|int64_t|const char \*)\s*(wt_\w+)\(", text, re.M)))
 
 
 @pytest.fixture(scope="module")

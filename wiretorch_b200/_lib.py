@@ -91,6 +91,7 @@ def lib() -> C.CDLL:
         _lib = C.CDLL(str(LIB))
         _lib.wt_last_error.restype = C.c_char_p
         _lib.wt_edge_grads_scratch_words.restype = C.c_int64
+        _lib.wt_edge_grads_slice_trials.restype = C.c_int32
         for name in ("wt_forward", "wt_fold_weights", "wt_workspace_bytes", "wt_abi_version",
                      "wt_backward", "wt_edge_grads", "wt_filter_forward", "wt_filter_backward",
                      "wt_forward_noalloc", "wt_noalloc_error", "wt_van_rossum_forward",

@@ -42,6 +42,7 @@ class _BackwardArgs(_lib.C.Structure):
         ("g_beta", _lib.P), ("g_E_syn", _lib.P), ("g_decay", _lib.P), ("g_jump", _lib.P),
         ("g_adapt", _lib.P), ("g_adapt_decay", _lib.P), ("g_E_adapt", _lib.P),
         ("t_lo", _lib.C.c_int32), ("t_hi", _lib.C.c_int32), ("adj", _lib.P), ("R", _lib.P),
+        ("QT", _lib.P),
     ]  # fmt: skip
 
 
@@ -58,6 +59,9 @@ class _EdgeArgs(_lib.C.Structure):
         ("Q", _lib.P), ("w_raw", _lib.P), ("scale", _lib.P), ("jf", _lib.P),
         ("chunk_path", _lib.P), ("g_scale", _lib.P), ("g_w", _lib.P), ("g_x", _lib.P),
         ("fired", _lib.P), ("work", _lib.P),
+        ("QT", _lib.P), ("in_ptr", _lib.P), ("in_edge", _lib.P), ("in_src", _lib.P), ("in_path", _lib.P),
+        ("in_fcol", _lib.P), ("ev_start", _lib.P), ("ev", _lib.P), ("ev_cap", _lib.C.c_longlong),
+        ("in_acc", _lib.P), ("err", _lib.P),
     ]  # fmt: skip
 
 
@@ -145,8 +149,23 @@ class _Simulate(torch.autograd.Function):
         bw.X_saved = _lib.ptr(save.get("X"))
         g_init = ctx.g_init
         bw.g_init = _lib.ptr(g_init)
-        Q = torch.empty((B, T, C, N), device=device)
-        bw.Q = Q.data_ptr()
+        n_weights = ctx.n_weights
+        need_scale = ctx.needs_input_grad[1]
+        need_x = ctx.needs_input_grad[2] and plan.n_in > 0
+        need_w = any(ctx.needs_input_grad[4 : 4 + n_weights])
+        # the scale and weight gradients target by target (the adjoints written
+        # target-major, each read once) wherever a target's slice of them fits on chip
+        lib = _lib.lib()
+        slice_trials = lib.wt_edge_grads_slice_trials(_lib.C.byref(net), T) if (need_scale or need_w) else 0
+        target_major = slice_trials > 0 and not cx.recurrent and plan.n_edges > 0
+        Q = QT = None
+        if need_x or not target_major:
+            Q = torch.empty((B, T, C, N), device=device)
+            bw.Q = Q.data_ptr()
+        if target_major:
+            Tp = -(-T // 8) * 8
+            QT = torch.empty((C, N, B, Tp), device=device)
+            bw.QT = QT.data_ptr()
         shapes = {"E_syn": (B, Sp, N), "decay": (B, 2, Sp, N), "jump": (B, 2, Sp, N)}
         partial = {}
         for name, field in zip(PHYSIOLOGY, ("g_theta", "g_reset", "g_E_L", "g_C_m", "g_beta",
@@ -165,10 +184,6 @@ class _Simulate(torch.autograd.Function):
             _lib.check(rc, "wt_backward")
             _lib.count_launches(1)
 
-        n_weights = ctx.n_weights
-        need_scale = ctx.needs_input_grad[1]
-        need_x = ctx.needs_input_grad[2] and plan.n_in > 0
-        need_w = any(ctx.needs_input_grad[4 : 4 + n_weights])
         t = plan.tensors
         g_scale = g_w = g_x = None
         if need_scale or need_w or need_x:
@@ -178,7 +193,7 @@ class _Simulate(torch.autograd.Function):
             xs = x.detach().float().contiguous()
             eg.x = xs.data_ptr() if plan.n_in else None
             eg.f_saved = _lib.ptr(save.get("f"))
-            eg.Q = Q.data_ptr()
+            eg.Q = _lib.ptr(Q)
             eg.w_raw, eg.jf = t["w_raw"].data_ptr(), t["jf"].data_ptr()
             sc = scale.detach().float().contiguous()
             eg.scale = sc.data_ptr()
@@ -197,10 +212,33 @@ class _Simulate(torch.autograd.Function):
                 _lib.check(0 if words >= 0 else 1, "wt_edge_grads_scratch_words")
                 fired = torch.empty(words + 1, dtype=torch.int32, device=device)
                 eg.fired, eg.work = fired.data_ptr(), fired[words:].data_ptr()
+            if target_major:
+                ie = _plan.in_edges(plan)
+                eg.QT = QT.data_ptr()
+                for name in ("in_ptr", "in_edge", "in_src", "in_path", "in_fcol"):
+                    setattr(eg, name, _lib.ptr(ie.get(name)))
+                n_src = N + plan.n_in
+                slices = -(-B // slice_trials)
+                # room for every source firing on one step in sixteen (625 Hz at 0.1 ms)
+                ev_cap = min(B * T * n_src // 16 + 4096, 2**31 - 1)
+                ev_start = torch.empty(n_src * (slices + 1), dtype=torch.int32, device=device)
+                ev = torch.empty(ev_cap, dtype=torch.int32, device=device)
+                in_acc = torch.empty(max(int(ie["in_edge"].numel()), 1), device=device)
+                err = torch.zeros(1, dtype=torch.int32, device=device)
+                eg.ev_start, eg.ev, eg.ev_cap = ev_start.data_ptr(), ev.data_ptr(), ev_cap
+                eg.in_acc, eg.err = in_acc.data_ptr(), err.data_ptr()
             with _lib.timed("wt_edge_grads"):
                 rc = _lib.lib().wt_edge_grads(_lib.C.byref(net), _lib.C.byref(eg), stream)
             _lib.check(rc, "wt_edge_grads")
-            _lib.count_launches(int(need_scale or need_w) + int(need_x))
+            # the firing rows (recurrent, input), then the source-by-source kernel or the
+            # event lists (count, scan, list) and the target-by-target kernel
+            fired_kernels = 1 + int(plan.n_in > 0)
+            _lib.count_launches(int(need_scale or need_w) * (fired_kernels + (4 if target_major else 1)) + int(need_x))
+            if target_major:
+                if engine.DEFER_CHECKS:
+                    engine._defer_check(err, "wt_edge_grads")
+                else:
+                    engine.check_device(err, "wt_edge_grads")
 
         ctx.save = ctx.g_init = None  # release the saved run as soon as it is used
         grads_w = [None] * n_weights

@@ -14,6 +14,8 @@
 //   l_r = decay_r l_r + dL/dG ;  l_d = decay_d l_d + dL/dG
 // The decays' gradient sum_t l_t g_t needs no saved conductances per component: with
 // H_{t-1} = l_t + decay H_t it is sum_t jump X_t H_t + g_init H_{-1}.
+#include <algorithm>
+
 #include "common.cuh"
 
 namespace wt {
@@ -100,6 +102,16 @@ __global__ void __launch_bounds__(kBlock, (PHYS || S > 2) ? 1 : 3) backward_kern
         }
     }
     const float R_b = bw.R ? bw.R[(size_t)b * N + n] : 0.0f;
+    // target-major adjoints (a whole scan): eight steps of each channel kept in registers
+    // and written together, one 32-byte sector per thread; slots past T stay zero
+    const int Tp = (T + 7) & ~7;
+    float *const QT_n = bw.QT ? bw.QT + ((size_t)n * net.B + b) * Tp : nullptr;
+    const size_t qt_c = (size_t)N * net.B * Tp;
+    float qb[S][8];
+#pragma unroll
+    for (int c = 0; c < S; c++)
+#pragma unroll
+        for (int u = 0; u < 8; u++) qb[c][u] = 0.0f;
     StepIn<S> q[kAhead];
 #pragma unroll
     for (int d = 0; d < kAhead; d++)
@@ -117,13 +129,25 @@ __global__ void __launch_bounds__(kBlock, (PHYS || S > 2) ? 1 : 3) backward_kern
         const float *G = cur.G;
 
         // The input of step t entered the state step t + 1 saw: its adjoint.
-        float *Qt = bw.Q + ((size_t)b * T + t) * C * N + n;
-        for (int c = 0; c < C; c++) {
+        float *Qt = bw.Q ? bw.Q + ((size_t)b * T + t) * C * N + n : nullptr;
+#pragma unroll
+        for (int c = 0; c < S; c++) {
+            if (c >= C) break;
             float qc = 0.0f;
 #pragma unroll
             for (int j = 0; j < S; j++)
                 if (in_c[j] == c) qc = qc + (net.jump_r[j] * lr[j] + net.jump_d[j] * ld[j]);
-            Qt[(size_t)c * N] = qc;
+            if (Qt) Qt[(size_t)c * N] = qc;
+            if (QT_n) {
+#pragma unroll
+                for (int u = 0; u < 8; u++)
+                    if ((t & 7) == u) qb[c][u] = qc;
+                if ((t & 7) == 0) {  // the group t .. t + 7 is complete
+                    float4 *dst = reinterpret_cast<float4 *>(QT_n + c * qt_c + t);
+                    dst[0] = make_float4(qb[c][0], qb[c][1], qb[c][2], qb[c][3]);
+                    dst[1] = make_float4(qb[c][4], qb[c][5], qb[c][6], qb[c][7]);
+                }
+            }
         }
         if (SYN && (wants & (WT_W_DECAY | WT_W_JUMP))) {
             const float *Xt = bw.X_saved + ((size_t)b * T + t) * C * N + n;
@@ -443,6 +467,162 @@ __global__ void __launch_bounds__(kEdgeWarps * 32) edge_grads_kernel(const WtNet
 }
 
 
+// ---------------------------------------------------------------------------------------
+// The edge gradients target by target (WtEdgeGrads.QT). Each source's events are listed
+// once (b Tp + t, in (trial, step) order, with where each slice of trials starts); then a
+// block per target stages the target's adjoints QT[c, n, b, :] of one slice of trials in
+// shared memory and every thread sums, for its in-edges, a * QT over the source's events
+// of that slice from there. Each adjoint is read from HBM once, by one coalesced copy; the
+// per-edge sums are plain writes (the block owns its target's in-edges).
+// ---------------------------------------------------------------------------------------
+
+constexpr int kTargetThreads = 256;
+constexpr int kSliceBytes = 64 * 1024;  // shared memory a block's slice may take
+
+// Events per source: a warp per source over its fired row.
+__global__ void event_count_kernel(const WtEdgeGrads eg, int n_src, int slices, long long BTw, long long BTw8) {
+    const int lane = threadIdx.x & 31;
+    const long long j = ((long long)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    if (j >= n_src) return;
+    const uint32_t *fw = eg.fired + (size_t)j * BTw8;
+    int cnt = 0;
+    for (long long w = lane; w < BTw; w += 32) cnt += __popc(__ldg(fw + w));
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) cnt += __shfl_xor_sync(kFull, cnt, o);
+    if (lane == 0) eg.ev_start[(size_t)j * (slices + 1)] = cnt;
+}
+
+// Exclusive sums of the counts over the sources (one block): the start of each source's
+// list; WT_ERR_EVENTS when the total exceeds the capacity.
+__global__ void event_scan_kernel(const WtEdgeGrads eg, int n_src, int slices) {
+    __shared__ long long part[1024];
+    const int tid = threadIdx.x, nt = blockDim.x;
+    const long long per = ((long long)n_src + nt - 1) / nt;
+    const long long lo = tid * per, hi = min((long long)n_src, lo + per);
+    long long sum = 0;
+    for (long long j = lo; j < hi; j++) sum += eg.ev_start[(size_t)j * (slices + 1)];
+    part[tid] = sum;
+    __syncthreads();
+    for (int o = 1; o < nt; o <<= 1) {  // inclusive scan of the per-thread sums
+        const long long y = tid >= o ? part[tid - o] : 0;
+        __syncthreads();
+        part[tid] += y;
+        __syncthreads();
+    }
+    long long run = part[tid] - sum;
+    for (long long j = lo; j < hi; j++) {
+        const long long c = eg.ev_start[(size_t)j * (slices + 1)];
+        eg.ev_start[(size_t)j * (slices + 1)] = (int32_t)min(run, eg.ev_cap);
+        run += c;
+    }
+    if (tid == nt - 1 && part[tid] > eg.ev_cap) set_error(eg.err, WT_ERR_EVENTS);
+}
+
+// Each source's list: a warp per source walks its fired row 32 words at a time, writes
+// every event as b Tp + t and records where each slice of trials (bq trials) begins.
+__global__ void event_list_kernel(const WtEdgeGrads eg, int n_src, int slices, int bq, int T, int Tp, long long BT,
+                                  long long BTw, long long BTw8) {
+    const int lane = threadIdx.x & 31;
+    const long long j = ((long long)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    if (j >= n_src) return;
+    if (read_error(eg.err)) return;  // over capacity: no list is written
+    int32_t *starts = eg.ev_start + (size_t)j * (slices + 1);
+    const uint32_t *fw = eg.fired + (size_t)j * BTw8;
+    int base = starts[0];
+    const long long span = (long long)bq * T;  // bits of one slice
+    for (long long w0 = 0; w0 < BTw; w0 += 32) {
+        const long long w = w0 + lane;
+        const uint32_t word = w < BTw ? __ldg(fw + w) : 0u;
+        const int cnt = __popc(word);
+        const int incl = warp_inclusive_sum(cnt, lane);
+        const int total = __shfl_sync(kFull, incl, 31);
+        int off = base + incl - cnt;
+        // slice boundaries that fall inside this lane's word
+        if (w < BTw) {
+            for (long long sl = (w * 32 + span - 1) / span; sl * span < w * 32 + 32 && sl < slices; sl++) {
+                if (sl == 0) continue;
+                const int bits = (int)(sl * span - w * 32);
+                starts[sl] = off + __popc(bits >= 32 ? word : (word & ((1u << bits) - 1u)));
+            }
+        }
+        uint32_t m = word;
+        while (m) {
+            const int bit = __ffs(m) - 1;
+            m &= m - 1;
+            const long long bt = w * 32 + bit;
+            const int b = (int)(bt / T), t = (int)(bt - (long long)b * T);
+            eg.ev[off++] = b * Tp + t;
+        }
+        base += total;
+    }
+    if (lane == 0) starts[slices] = base;
+}
+
+__global__ void __launch_bounds__(kTargetThreads) edge_grads_target_kernel(const WtNet net, const WtEdgeGrads eg,
+                                                                          int slices, int bq, int T, int Tp) {
+    extern __shared__ __align__(16) float qs[];  // [c][b - b0][Tp]
+    const int N = net.N, C = net.C, B = net.B, n_in = net.n_in;
+    const int tid = threadIdx.x;
+    const size_t BTp = (size_t)B * Tp;
+    __shared__ int s_n;
+    if (read_error(eg.err)) return;
+    for (;;) {
+        __syncthreads();
+        if (tid == 0) s_n = (int)atomicAdd(eg.work, 1u);
+        __syncthreads();
+        const int n = s_n;
+        if (n >= N) return;
+        const int i0 = eg.in_ptr[n], i1 = eg.in_ptr[n + 1];
+        if (i0 == i1) continue;
+        for (int sl = 0; sl < slices; sl++) {
+            const int b0 = sl * bq, nb = min(bq, B - b0);
+            // the slice's adjoints of this target, every channel: contiguous runs of nb Tp
+            const int row = nb * Tp;  // floats, a multiple of 8
+            __syncthreads();
+            for (int c = 0; c < C; c++) {
+                const float4 *src = reinterpret_cast<const float4 *>(eg.QT + ((size_t)c * N + n) * BTp + (size_t)b0 * Tp);
+                float4 *dst = reinterpret_cast<float4 *>(qs + (size_t)c * bq * Tp);
+                for (int k = tid; k < row / 4; k += kTargetThreads) dst[k] = __ldcs(src + k);
+            }
+            __syncthreads();
+            const int base = b0 * Tp;
+            for (int i = i0 + tid; i < i1; i += kTargetThreads) {
+                const int j = eg.in_src[i];
+                const int e = eg.in_edge[i];
+                const int c = (int)(net.edge_col[e] >> 27);
+                const int fcol = eg.in_fcol ? eg.in_fcol[i] : -1;
+                const int32_t *st = eg.ev_start + (size_t)j * (slices + 1) + sl;
+                const int q0 = st[0], q1 = st[1];
+                const float *qc = qs + (size_t)c * bq * Tp - base;
+                float acc = 0.0f;
+                if (j < N && fcol < 0) {
+                    for (int q = q0; q < q1; q++) acc += qc[__ldg(eg.ev + q)];
+                } else {  // input values and gating factors scale the events
+                    for (int q = q0; q < q1; q++) {
+                        const int ev = __ldg(eg.ev + q);
+                        const int b = ev / Tp, t = ev - b * Tp;
+                        const size_t bt = (size_t)b * T + t;
+                        float a = j >= N ? eg.x[bt * n_in + (j - N)] : 1.0f;
+                        if (fcol >= 0) a *= eg.f_saved[bt * net.R_f + fcol];
+                        acc += a * qc[ev];
+                    }
+                }
+                eg.in_acc[i] = sl ? eg.in_acc[i] + acc : acc;
+            }
+        }
+        // the target's in-edges done: their gradients (this block alone writes them)
+        for (int i = i0 + tid; i < i1; i += kTargetThreads) {
+            const int e = eg.in_edge[i];
+            const int k = eg.in_path[i];
+            const int c = (int)(net.edge_col[e] >> 27);
+            const double acc = (double)eg.in_acc[i];
+            const double jfv = eg.jf[(size_t)k * C + c];
+            if (eg.g_w) eg.g_w[e] += acc * (double)eg.scale[(size_t)k * N + n] * jfv;
+            if (eg.g_scale) atomicAdd(eg.g_scale + (size_t)k * N + n, acc * (double)eg.w_raw[e] * jfv);
+        }
+    }
+}
+
 // One warp per (trial, step, input column): the input's gradient, fired or not.
 __global__ void input_grads_kernel(const WtNet net, const WtEdgeGrads eg) {
     const int lane = threadIdx.x & 31;
@@ -512,6 +692,12 @@ cudaError_t launch_backward(const WtNet &net, const WtBackward &bw, cudaStream_t
     }
 }
 
+int edge_grads_slice_trials(const WtNet &net, int T) {
+    const long long per_trial = (long long)net.C * ((T + 7) & ~7) * 4;  // bytes of one trial's adjoints
+    if (per_trial > kSliceBytes) return 0;
+    return (int)std::min<long long>(net.B, kSliceBytes / per_trial);
+}
+
 long long edge_grads_fired_words(const WtNet &net, int T) {
     const long long BT = (long long)net.B * T;
     const long long BTw8 = ((BT + 31) / 32 + kFiredGroup - 1) / kFiredGroup * kFiredGroup;
@@ -533,12 +719,34 @@ cudaError_t launch_edge_grads(const WtNet &net, const WtEdgeGrads &eg, cudaStrea
         int sms = 0, dev = 0;
         cudaGetDevice(&dev);
         cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-        int per_sm = 0;
-        e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, edge_grads_kernel, kEdgeWarps * 32, 0);
-        if (e != cudaSuccess) return e;
-        edge_grads_kernel<<<sms * (per_sm > 0 ? per_sm : 1), kEdgeWarps * 32, 0, st>>>(net, eg, BT, BTw8);
-        e = cudaGetLastError();
-        if (e != cudaSuccess) return e;
+        if (eg.QT) {  // target by target
+            const int n_src = net.N + net.n_in;
+            const int T = eg.T, Tp = (T + 7) & ~7;
+            const int bq = edge_grads_slice_trials(net, T);
+            const int slices = (net.B + bq - 1) / bq;
+            const long long BTw = (BT + 31) >> 5;
+            const unsigned wblocks = (unsigned)(((long long)n_src + 7) / 8);
+            event_count_kernel<<<wblocks, 256, 0, st>>>(eg, n_src, slices, BTw, BTw8);
+            event_scan_kernel<<<1, 1024, 0, st>>>(eg, n_src, slices);
+            event_list_kernel<<<wblocks, 256, 0, st>>>(eg, n_src, slices, bq, T, Tp, BT, BTw, BTw8);
+            const size_t smem = (size_t)net.C * bq * Tp * 4;
+            e = cudaFuncSetAttribute(edge_grads_target_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+            if (e != cudaSuccess) return e;
+            int per_sm = 0;
+            e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, edge_grads_target_kernel, kTargetThreads, smem);
+            if (e != cudaSuccess) return e;
+            edge_grads_target_kernel<<<sms * (per_sm > 0 ? per_sm : 1), kTargetThreads, smem, st>>>(net, eg, slices,
+                                                                                                     bq, T, Tp);
+            e = cudaGetLastError();
+            if (e != cudaSuccess) return e;
+        } else {  // source by source
+            int per_sm = 0;
+            e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, edge_grads_kernel, kEdgeWarps * 32, 0);
+            if (e != cudaSuccess) return e;
+            edge_grads_kernel<<<sms * (per_sm > 0 ? per_sm : 1), kEdgeWarps * 32, 0, st>>>(net, eg, BT, BTw8);
+            e = cudaGetLastError();
+            if (e != cudaSuccess) return e;
+        }
     }
     if (eg.g_x && net.n_in > 0) {
         const long long warps = (long long)net.B * eg.T * net.n_in;

@@ -12,6 +12,7 @@ cudaError_t launch_forward_s(const WtNet &net, const WtForward &run, const WtWor
 cudaError_t launch_backward(const WtNet &net, const WtBackward &bw, cudaStream_t st);
 cudaError_t launch_edge_grads(const WtNet &net, const WtEdgeGrads &eg, cudaStream_t st);
 long long edge_grads_fired_words(const WtNet &net, int T);
+int edge_grads_slice_trials(const WtNet &net, int T);
 cudaError_t launch_lowrank_product(const WtLowRankProduct &a, cudaStream_t st);
 cudaError_t launch_lowrank_forward(const WtLowRankNet &net, const WtLowRankRun &run, cudaStream_t st);
 cudaError_t launch_recurrent_carry(const WtNet &net, const WtRecurrentCarry &rc, cudaStream_t st);
@@ -167,8 +168,11 @@ int wt_backward(const WtNet *net, const WtBackward *bw, void *stream) {
     if (rc) return rc;
     if (net->N_src && net->N_src != net->N) return fail(WT_ERR_UNSUPPORTED, "no backward pass for a partitioned net%s");
     if (!bw || bw->T < 0) return fail(WT_ERR_ARGS, "bad backward arguments%s");
-    if (!bw->grad_spikes || !bw->v_saved || !bw->G_saved || !bw->spike_bits || !bw->Q)
+    if (!bw->grad_spikes || !bw->v_saved || !bw->G_saved || !bw->spike_bits || !(bw->Q || bw->QT))
         return fail(WT_ERR_ARGS, "missing saved tensors%s");
+    if (bw->QT && (bw->adj || bw->t_lo != 0 || (bw->t_hi != 0 && bw->t_hi != bw->T) ||
+                   ((uintptr_t)bw->QT & 15)))
+        return fail(WT_ERR_ARGS, "target-major adjoints need a whole scan and a 16-byte aligned buffer%s");
     const int f = bw->flags, w = bw->wants;
     if ((f & WT_F_REFRACTORY) && !bw->held_bits) return fail(WT_ERR_ARGS, "missing refractory bits%s");
     if ((f & WT_F_ADAPT) && (!bw->a_saved || !net->adapt_decay || !net->E_adapt))
@@ -187,7 +191,13 @@ int wt_edge_grads(const WtNet *net, const WtEdgeGrads *eg, void *stream) {
     int rc = check_net(net);
     if (rc) return rc;
     if (net->N_src && net->N_src != net->N) return fail(WT_ERR_UNSUPPORTED, "no backward pass for a partitioned net%s");
-    if (!eg || eg->T < 0 || !eg->Q || !eg->chunk_path || !eg->jf) return fail(WT_ERR_ARGS, "bad edge arguments%s");
+    if (!eg || eg->T < 0 || !eg->chunk_path || !eg->jf) return fail(WT_ERR_ARGS, "bad edge arguments%s");
+    if (!eg->Q && (eg->g_x || !eg->QT)) return fail(WT_ERR_ARGS, "missing adjoints%s");
+    if (eg->QT && (eg->g_scale || eg->g_w) &&
+        (!eg->in_ptr || !eg->in_edge || !eg->in_src || !eg->in_path || (net->slot_gate && !eg->in_fcol) ||
+         !eg->ev_start || !eg->ev || eg->ev_cap < 1 || eg->ev_cap >= (1LL << 31) || !eg->in_acc || !eg->err ||
+         wt::edge_grads_slice_trials(*net, eg->T) < 1 || ((uintptr_t)eg->QT & 15)))
+        return fail(WT_ERR_ARGS, "missing in-edge tables or event scratch%s");
     if ((eg->g_scale || eg->g_w) && (!eg->spike_bits || (net->n_in && !eg->x)))
         return fail(WT_ERR_ARGS, "missing events%s");
     if (eg->g_scale && !eg->w_raw) return fail(WT_ERR_ARGS, "missing raw weights%s");
@@ -203,6 +213,11 @@ int wt_edge_grads(const WtNet *net, const WtEdgeGrads *eg, void *stream) {
 int64_t wt_edge_grads_scratch_words(const WtNet *net, int32_t T) {
     if (check_net(net) || T < 0) return -1;
     return wt::edge_grads_fired_words(*net, T);
+}
+
+int32_t wt_edge_grads_slice_trials(const WtNet *net, int32_t T) {
+    if (check_net(net) || T < 0) return 0;
+    return wt::edge_grads_slice_trials(*net, T);
 }
 
 int wt_filter_forward(const WtFilterArgs *f, void *stream) {

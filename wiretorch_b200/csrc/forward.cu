@@ -654,6 +654,23 @@ __global__ void __launch_bounds__(warps_of<S, FEAT>() * 32, 1) forward_kernel(co
         const float xv = valid ? run.x[((size_t)b * run.T_total + run.t0) * n_in + c] : 0.0f;
         emit_input(0, valid, b, Nsrc + c, xv);
     }
+    // The input columns this lane emits each step (one per warp-iteration of the grid
+    // over B x Ip) are loaded a step ahead, so that the emission does not wait for them.
+    constexpr int kXAhead = 4;
+    float x_ahead[kXAhead];
+    auto load_x = [&](int step_abs) {
+#pragma unroll
+        for (int r = 0; r < kXAhead; r++) {
+            const long long base = warp0 + (long long)r * nthreads;
+            x_ahead[r] = 0.0f;
+            if (base < itemsI && step_abs < run.t0 + T) {
+                const unsigned i = (unsigned)(base + lane);
+                const int b = (int)(i / (unsigned)Ip), c = (int)(i - (unsigned)b * Ip);
+                if (c < n_in) x_ahead[r] = __ldcs(run.x + ((size_t)b * run.T_total + step_abs) * n_in + c);
+            }
+        }
+    };
+    load_x(run.t0 + 1);
     if (PART) __threadfence_system();  // the published words, before the barrier
     if (!bar.sync(ws.err)) return;
     if (PART && !exchange(0)) return;
@@ -675,13 +692,19 @@ __global__ void __launch_bounds__(warps_of<S, FEAT>() * 32, 1) forward_kernel(co
 
         // ---------------- the input columns of the next step ----------------
         if (emit_next) {
-            for (long long base = warp0; base < itemsI; base += nthreads) {
+            int r = 0;
+            for (long long base = warp0; base < itemsI; base += nthreads, r++) {
                 const unsigned i = (unsigned)(base + lane);
                 const int b = (int)(i / (unsigned)Ip), c = (int)(i - (unsigned)b * Ip);
                 const bool valid = c < n_in;
-                const float xv = valid ? run.x[((size_t)b * run.T_total + t_abs + 1) * n_in + c] : 0.0f;
+                float xv = 0.0f;
+#pragma unroll
+                for (int q = 0; q < kXAhead; q++)
+                    if (q == r) xv = x_ahead[q];
+                if (r >= kXAhead && valid) xv = run.x[((size_t)b * run.T_total + t_abs + 1) * n_in + c];
                 emit_input(t + 1, valid, b, Nsrc + c, xv);
             }
+            load_x(t_abs + 2);  // the next step's, landing while this step runs
         }
 
         // ---------------- scatter the events of step t into X_t ----------------

@@ -314,6 +314,7 @@ def build(drive, p, B: int, n_in: int, device, pool: bool = False, n_src: int | 
     order = torch.argsort(src * max(K, 1) + path)
     src, path, row = src[order], path[order], row[order]
     plan.N_src = N_src
+    plan.path_sources = src_l  # per pathway: the source of each of its rows
     n_src = N_src + n_in
     src_slot = torch.zeros(n_src + 1, dtype=torch.int64, device=device)
     src_slot[1:] = torch.cumsum(torch.bincount(src, minlength=n_src), 0)
@@ -428,6 +429,41 @@ def segments(plan: Plan) -> list:
             out.append((k, c, base, n_e, rows, cols))
         t["_segments"] = out
     return t["_segments"]
+
+
+def in_edges(plan: Plan) -> dict:
+    """The in-edges of every target, for the target-by-target edge gradients: ``in_ptr``
+    (N + 1) and per in-edge (ordered by target, then pathway, then edge) its edge
+    ``in_edge``, source ``in_src``, pathway ``in_path`` and — in gated networks — its
+    gating factor's column of the saved factors ``in_fcol`` (-1: ungated); int32 each,
+    built once per plan."""
+    t = plan.tensors
+    if "_in_edges" not in t:
+        dev = plan.device
+        E = max(plan.n_edges, 0)
+        e_l, j_l, k_l, n_l, f_l = [], [], [], [], []
+        for k, c, base, n_e, rows, cols in segments(plan):
+            e_l.append(torch.arange(base, base + n_e, device=dev))
+            j_l.append(plan.path_sources[k][rows])
+            k_l.append(torch.full((n_e,), k, dtype=torch.int64, device=dev))
+            n_l.append(cols)
+            fc = plan.gate_f_cols[k] if plan.gated and k < len(plan.gate_f_cols) else -1
+            f_l.append(rows + fc if fc >= 0 else torch.full((n_e,), -1, dtype=torch.int64, device=dev))
+        if E and e_l:
+            e, j, kk, n, f = (torch.cat(v) for v in (e_l, j_l, k_l, n_l, f_l))
+            # edge order already (segments in order of their base); then stably by target
+            # and pathway
+            order = torch.argsort(n * max(plan.K, 1) + kk, stable=True)
+            e, j, kk, n, f = e[order], j[order], kk[order], n[order], f[order]
+        else:
+            e = j = kk = n = f = torch.zeros(0, dtype=torch.int64, device=dev)
+        in_ptr = torch.zeros(plan.N + 1, dtype=torch.int64, device=dev)
+        in_ptr[1:] = torch.cumsum(torch.bincount(n, minlength=plan.N), 0)
+        out = {"in_ptr": in_ptr, "in_edge": e, "in_src": j, "in_path": kk}
+        if plan.gated:
+            out["in_fcol"] = f
+        t["_in_edges"] = {name: v.to(torch.int32).contiguous() for name, v in out.items()}
+    return t["_in_edges"]
 
 
 def edge_pathway(plan: Plan) -> torch.Tensor:
