@@ -5,8 +5,10 @@
 pass, as in training. ``python tests/profile_cases.py c3-small``: C3 with 128
 trials, 200 steps, then one 10-step call from that state. ``c5-small``: C5 at 250,000
 neurons (4 trials, gated, pooled), 300 steps from rest, then one 20-step call;
-``c5-full`` the same at C5's full size (1,000,000 neurons). In all the second launch of
-the kernel is the one to capture (``-s 1 -c 1``).
+``c5-full`` the same at C5's full size (1,000,000 neurons). In these the second launch
+of the kernel is the one to capture (``-s 1 -c 1``). ``c2-step``: two C2 training steps
+(every kernel of the second step is one to capture); ``c2-carry``: the per-step carry of
+gradients through the recurrent spikes; ``c3-product``: the tensor-core product alone.
 """
 
 from __future__ import annotations
@@ -80,7 +82,65 @@ def c5_full():
     print(f"c5-full: {float(run2.output.sum()) / 20:.0f} spikes per step, {cfg.extra['edges']} edges")
 
 
-CASES = {"c2-active": c2_active, "c3-small": c3_small, "c5-small": c5_small, "c5-full": c5_full}
+def c2_step():
+    """One C2 training step (64 trials, 500 steps, pooled channels): forward with saving,
+    van Rossum rate loss, reverse scan, edge gradients to the per-pair scales, after one
+    untimed step. Every kernel of the step launches once in the second step."""
+    from wiretorch_b200 import configs, engine, filtering
+
+    cfg = configs.c2(B=64, T=500, device="cuda")
+    engine.POOL_SYNAPSES = True
+    x = cfg.inputs(seed=1)
+    v, g, kw = cfg.state()
+    log_sf = torch.zeros(cfg.extra["log_sf_shape"], device="cuda", requires_grad=True)
+    loss_fn = filtering.VanRossumRateLoss(0.1, 20.0, 0.1, cfg.T, device="cuda")
+    target = (cfg.extra["target_rates"] * 1e-4)[:, None, :].expand(cfg.B, cfg.T, cfg.N)
+    for _ in range(2):
+        loss_fn.reset_state()
+        cfg.drive.scale = configs.scale_from_log_sf(cfg, log_sf)
+        run = engine.simulate(v, g, x, cfg.drive, cfg.p, **kw)
+        loss = loss_fn(target, output_spikes=run.output)
+        log_sf.grad = None
+        loss.backward()
+    torch.cuda.synchronize()
+    print(f"c2-step: loss {float(loss.detach()):.5f}, |grad| {float(log_sf.grad.norm()):.3e}")
+
+
+def c2_carry():
+    """C2 with gradients through the recurrent spikes (16 trials, 40 steps): the
+    per-step carry kernel along the recurrent edges, 40 launches in the backward pass."""
+    from wiretorch_b200 import configs, engine
+
+    cfg = configs.c2(B=16, T=40, device="cuda")
+    engine.POOL_SYNAPSES = True
+    cfg.drive.recurrent_gradients = True
+    x = cfg.inputs(seed=1)
+    v, g, kw = cfg.state()
+    log_sf = torch.zeros(cfg.extra["log_sf_shape"], device="cuda", requires_grad=True)
+    cfg.drive.scale = configs.scale_from_log_sf(cfg, log_sf)
+    run = engine.simulate(v, g, x, cfg.drive, cfg.p, **kw)
+    (run.output * torch.randn_like(run.output)).sum().backward()
+    torch.cuda.synchronize()
+    print(f"c2-carry: |grad| {float(log_sf.grad.norm()):.3e}")
+
+
+def c3_product():
+    """The tensor-core product of C3's factors: V (50,000 x 64) times P^T for 256 trials
+    and two pathways (``wt_lowrank_product``), three launches."""
+    from wiretorch_b200 import lowrank
+
+    N, r, B = 50000, 64, 256
+    gen = torch.Generator(device="cuda").manual_seed(0)
+    V = (torch.randn(N, r, generator=gen, device="cuda") / N**0.5).to(torch.bfloat16)
+    P = torch.randn(B, 2, r, generator=gen, device="cuda")  # two pathways (E, I)
+    for _ in range(3):
+        out = lowrank.product(V, P)
+    torch.cuda.synchronize()
+    print(f"c3-product: {tuple(out.shape)}")
+
+
+CASES = {"c2-active": c2_active, "c3-small": c3_small, "c5-small": c5_small, "c5-full": c5_full,
+         "c2-step": c2_step, "c2-carry": c2_carry, "c3-product": c3_product}  # fmt: skip
 
 if __name__ == "__main__":
     CASES[sys.argv[1]]()

@@ -1,16 +1,18 @@
 """ctypes binding of the engine's C ABI (``include/wiretorch_b200.h``).
 
 The structures mirror the header field for field. ``lib()`` loads
-``_lib/libwiretorch_b200.so`` (built by ``wiretorch_b200.build``) and raises if it is
-missing: the engine has no other implementation to fall back on.
+``_lib/libwiretorch_b200.so`` (built by ``wiretorch_b200.build``; the environment
+variable ``WIRETORCH_B200_LIB`` names another build of the same sources) and raises if
+it is missing: the engine has no other implementation to fall back on.
 """
 
 from __future__ import annotations
 
 import ctypes as C
+import os
 from pathlib import Path
 
-LIB = Path(__file__).parent / "_lib" / "libwiretorch_b200.so"
+LIB = Path(os.environ.get("WIRETORCH_B200_LIB") or Path(__file__).parent / "_lib" / "libwiretorch_b200.so")
 MAX_CHANNELS = 8
 CHUNK_EDGES = 128
 EVENT_BYTES = 16  # sizeof(WtEvent)

@@ -75,7 +75,9 @@ __device__ __forceinline__ void cp_async_wait(int pending) {
         case 0: asm volatile("cp.async.wait_group 0;" ::: "memory"); break;
         case 1: asm volatile("cp.async.wait_group 1;" ::: "memory"); break;
         case 2: asm volatile("cp.async.wait_group 2;" ::: "memory"); break;
-        default: asm volatile("cp.async.wait_group 3;" ::: "memory"); break;
+        case 3: asm volatile("cp.async.wait_group 3;" ::: "memory"); break;
+        case 4: asm volatile("cp.async.wait_group 4;" ::: "memory"); break;
+        default: asm volatile("cp.async.wait_group 5;" ::: "memory"); break;
     }
 }
 
@@ -287,7 +289,10 @@ template <int S, int FEAT>
 constexpr int warps_of() {
     return ((FEAT & kGeneric) == 0 && S <= 4) ? ((FEAT & (kMg | kGate | kAdapt | kPart)) ? WT_GATE_WARPS : 24) : 16;
 }
-constexpr int kMaxRing = 4;               // deepest ring of staged items
+#ifndef WT_MAX_RING
+#define WT_MAX_RING 4
+#endif
+constexpr int kMaxRing = WT_MAX_RING;     // deepest ring of staged items
 
 
 // A warp's position in its run of items: neuron group g, trial b, and the trial's row
@@ -658,6 +663,20 @@ __global__ void __launch_bounds__(warps_of<S, FEAT>() * 32, 1) forward_kernel(co
     // over B x Ip) are loaded a step ahead, so that the emission does not wait for them.
     constexpr int kXAhead = 4;
     float x_ahead[kXAhead];
+    // ... and, in gated networks, whether any of those columns has a gated slot (the
+    // columns are the same every step): the others emit without the gate table
+    bool x_gated[kXAhead];
+#pragma unroll
+    for (int r = 0; r < kXAhead; r++) {
+        x_gated[r] = false;
+        const long long base = warp0 + (long long)r * nthreads;
+        if (GSRC && base < itemsI) {
+            const unsigned i = (unsigned)(base + lane);
+            const int b = (int)(i / (unsigned)Ip), c = (int)(i - (unsigned)b * Ip);
+            const bool g = c < n_in && net.src_gate[2 * (Nsrc + c)] != -1;
+            x_gated[r] = __any_sync(kFull, g);
+        }
+    }
     auto load_x = [&](int step_abs) {
 #pragma unroll
         for (int r = 0; r < kXAhead; r++) {
@@ -698,11 +717,25 @@ __global__ void __launch_bounds__(warps_of<S, FEAT>() * 32, 1) forward_kernel(co
                 const int b = (int)(i / (unsigned)Ip), c = (int)(i - (unsigned)b * Ip);
                 const bool valid = c < n_in;
                 float xv = 0.0f;
+                bool xg = true;
 #pragma unroll
                 for (int q = 0; q < kXAhead; q++)
-                    if (q == r) xv = x_ahead[q];
+                    if (q == r) {
+                        xv = x_ahead[q];
+                        xg = x_gated[q];
+                    }
                 if (r >= kXAhead && valid) xv = run.x[((size_t)b * run.T_total + t_abs + 1) * n_in + c];
-                emit_input(t + 1, valid, b, Nsrc + c, xv);
+                if (GSRC && !xg) {  // ungated columns of a gated network
+                    const bool on = valid && xv != 0.0f;
+                    int c0 = 0, cnt = 0;
+                    if (on) {
+                        c0 = net.src_chunk[Nsrc + c];
+                        cnt = net.src_chunk[Nsrc + c + 1] - c0;
+                    }
+                    emit_fast(net, ws, t + 1, on, b, c0, cnt, xv, lane);
+                } else {
+                    emit_input(t + 1, valid, b, Nsrc + c, xv);
+                }
             }
             load_x(t_abs + 2);  // the next step's, landing while this step runs
         }
