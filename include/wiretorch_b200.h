@@ -280,7 +280,8 @@ typedef struct {
      * target's adjoints of a slice of trials in shared memory (wt_edge_grads_slice_trials
      * trials at a time) and sums every in-edge's events from there, so each adjoint is
      * read from HBM once. The in-edges of each target, by pathway then edge (in_ptr
-     * (N + 1), and per in-edge its edge, its source and its pathway, (E_in) each; in_fcol
+     * (N + 1), and per in-edge its edge, its source and its pathway and input channel as
+     * 8 k + c, (E_in) each; in_fcol
      * its gating factor's column of f_saved, -1 ungated, or NULL when nothing is gated);
      * scratch: ev_start ((N + n_in) (slices + 1)) and ev (ev_cap) for each source's events
      * (b Tp + t) and where each slice of trials starts among them, in_acc (E_in) floats,

@@ -16,6 +16,8 @@ its length and of its latest end relative to the step's start:
   late    the odd warps' scatter
   barrier the wait at the grid barrier
   exchange (partitioned runs) the progress wait, barrier and spike emission from the words
+
+and the spread of the warps' ends of work within a step (median, 90th percentile, last).
 """
 
 from __future__ import annotations
@@ -54,6 +56,10 @@ def summary(stamps: np.ndarray) -> dict:
     for k, name in enumerate(NAMES):
         d = (s[:, :, k + 1] - s[:, :, k]) / 1e3
         out[name] = (d.mean(), (s[:, :, k + 1].max(1) - start).mean() / 1e3)
+    # the spread of the warps' ends of work (late scatter done) within a step: median,
+    # 90th percentile and last, from the step's start
+    ends = (s[:, :, 4] - start[:, None]) / 1e3
+    out["ends"] = tuple(np.percentile(ends, q, axis=1).mean() for q in (50, 90, 100))
     return out
 
 
@@ -103,6 +109,8 @@ def main():
     for name in NAMES:
         mean, end = res[name]
         lines.append(f"  {name:9s} {mean:8.2f} us per warp   latest end {end:8.2f} us into the step")
+    p50, p90, last = res["ends"]
+    lines.append(f"  warps' work ends (us into the step): median {p50:.2f}, 90th percentile {p90:.2f}, last {last:.2f}")
     text = "\n".join(lines)
     if part is not None:
         import torch.distributed as dist

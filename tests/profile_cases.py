@@ -7,7 +7,8 @@ trials, 200 steps, then one 10-step call from that state. ``c5-small``: C5 at 25
 neurons (4 trials, gated, pooled), 300 steps from rest, then one 20-step call;
 ``c5-full`` the same at C5's full size (1,000,000 neurons). In these the second launch
 of the kernel is the one to capture (``-s 1 -c 1``). ``c2-step``: two C2 training steps
-(every kernel of the second step is one to capture); ``c2-carry``: the per-step carry of
+(every kernel of the second step is one to capture; ``c2-step-16`` with 16 trials, for
+captures of many passes); ``c2-carry``: the per-step carry of
 gradients through the recurrent spikes; ``c3-product``: the tensor-core product alone.
 """
 
@@ -82,13 +83,13 @@ def c5_full():
     print(f"c5-full: {float(run2.output.sum()) / 20:.0f} spikes per step, {cfg.extra['edges']} edges")
 
 
-def c2_step():
+def c2_step(B=64):
     """One C2 training step (64 trials, 500 steps, pooled channels): forward with saving,
     van Rossum rate loss, reverse scan, edge gradients to the per-pair scales, after one
     untimed step. Every kernel of the step launches once in the second step."""
     from wiretorch_b200 import configs, engine, filtering
 
-    cfg = configs.c2(B=64, T=500, device="cuda")
+    cfg = configs.c2(B=B, T=500, device="cuda")
     engine.POOL_SYNAPSES = True
     x = cfg.inputs(seed=1)
     v, g, kw = cfg.state()
@@ -140,7 +141,8 @@ def c3_product():
 
 
 CASES = {"c2-active": c2_active, "c3-small": c3_small, "c5-small": c5_small, "c5-full": c5_full,
-         "c2-step": c2_step, "c2-carry": c2_carry, "c3-product": c3_product}  # fmt: skip
+         "c2-step": c2_step, "c2-step-16": lambda: c2_step(16), "c2-carry": c2_carry,
+         "c3-product": c3_product}  # fmt: skip
 
 if __name__ == "__main__":
     CASES[sys.argv[1]]()

@@ -558,14 +558,56 @@ __global__ void event_list_kernel(const WtEdgeGrads eg, int n_src, int slices, i
     if (lane == 0) starts[slices] = base;
 }
 
-__global__ void __launch_bounds__(kTargetThreads) edge_grads_target_kernel(const WtNet net, const WtEdgeGrads eg,
+constexpr int kEdgeCache = 4;  // in-edges a thread keeps in registers over the slices
+
+// The sum over source j's events of one slice of a * QT (the slice staged at qc).
+__device__ __forceinline__ float slice_sum(const WtNet &net, const WtEdgeGrads &eg, const float *qc, int j, int fcol,
+                                           int q0, int q1, int T, int Tp) {
+    float acc = 0.0f;
+    if (j < net.N && fcol < 0) {
+        for (int q = q0; q < q1; q++) acc += qc[__ldg(eg.ev + q)];
+    } else {  // input values and gating factors scale the events
+        for (int q = q0; q < q1; q++) {
+            const int ev = __ldg(eg.ev + q);
+            const int b = ev / Tp, t = ev - b * Tp;
+            const size_t bt = (size_t)b * T + t;
+            float a = j >= net.N ? eg.x[bt * net.n_in + (j - net.N)] : 1.0f;
+            if (fcol >= 0) a *= eg.f_saved[bt * net.R_f + fcol];
+            acc += a * qc[ev];
+        }
+    }
+    return acc;
+}
+
+__global__ void __launch_bounds__(kTargetThreads, 3) edge_grads_target_kernel(const WtNet net, const WtEdgeGrads eg,
                                                                           int slices, int bq, int T, int Tp) {
     extern __shared__ __align__(16) float qs[];  // [c][b - b0][Tp]
-    const int N = net.N, C = net.C, B = net.B, n_in = net.n_in;
+    const int N = net.N, C = net.C, B = net.B;
     const int tid = threadIdx.x;
     const size_t BTp = (size_t)B * Tp;
     __shared__ int s_n;
     if (read_error(eg.err)) return;
+    // the slice sl of this target's adjoints, every channel, into shared memory
+    auto stage = [&](int n, int sl) {
+        const int b0 = sl * bq, nb = min(bq, B - b0);
+        const int row = nb * Tp;  // floats, a multiple of 8
+        __syncthreads();
+        for (int c = 0; c < C; c++) {
+            const float4 *src = reinterpret_cast<const float4 *>(eg.QT + ((size_t)c * N + n) * BTp + (size_t)b0 * Tp);
+            float4 *dst = reinterpret_cast<float4 *>(qs + (size_t)c * bq * Tp);
+            for (int k = tid; k < row / 4; k += kTargetThreads) dst[k] = __ldcs(src + k);
+        }
+        __syncthreads();
+    };
+    // in-edge i's gradients from its sum over every event (this block alone writes them)
+    auto finish = [&](int n, int i, float sum) {
+        const int e = eg.in_edge[i];
+        const int k = eg.in_path[i] >> 3, c = eg.in_path[i] & 7;
+        const double acc = (double)sum;
+        const double jfv = eg.jf[(size_t)k * C + c];
+        if (eg.g_w) eg.g_w[e] += acc * (double)eg.scale[(size_t)k * N + n] * jfv;
+        if (eg.g_scale) atomicAdd(eg.g_scale + (size_t)k * N + n, acc * (double)eg.w_raw[e] * jfv);
+    };
     for (;;) {
         __syncthreads();
         if (tid == 0) s_n = (int)atomicAdd(eg.work, 1u);
@@ -574,51 +616,71 @@ __global__ void __launch_bounds__(kTargetThreads) edge_grads_target_kernel(const
         if (n >= N) return;
         const int i0 = eg.in_ptr[n], i1 = eg.in_ptr[n + 1];
         if (i0 == i1) continue;
-        for (int sl = 0; sl < slices; sl++) {
-            const int b0 = sl * bq, nb = min(bq, B - b0);
-            // the slice's adjoints of this target, every channel: contiguous runs of nb Tp
-            const int row = nb * Tp;  // floats, a multiple of 8
-            __syncthreads();
-            for (int c = 0; c < C; c++) {
-                const float4 *src = reinterpret_cast<const float4 *>(eg.QT + ((size_t)c * N + n) * BTp + (size_t)b0 * Tp);
-                float4 *dst = reinterpret_cast<float4 *>(qs + (size_t)c * bq * Tp);
-                for (int k = tid; k < row / 4; k += kTargetThreads) dst[k] = __ldcs(src + k);
+        if (i1 - i0 <= kEdgeCache * kTargetThreads) {
+            // each thread's in-edges (up to kEdgeCache) kept in registers over the slices;
+            // their event sums run side by side
+            int cj[kEdgeCache], cc[kEdgeCache], cf[kEdgeCache];
+            float cacc[kEdgeCache];
+#pragma unroll
+            for (int u = 0; u < kEdgeCache; u++) {
+                const int i = i0 + tid + u * kTargetThreads;
+                cj[u] = -1;
+                cc[u] = 0;
+                cf[u] = -1;
+                cacc[u] = 0.0f;
+                if (i < i1) {
+                    cj[u] = eg.in_src[i];
+                    cc[u] = eg.in_path[i] & 7;
+                    cf[u] = eg.in_fcol ? eg.in_fcol[i] : -1;
+                }
             }
-            __syncthreads();
-            const int base = b0 * Tp;
-            for (int i = i0 + tid; i < i1; i += kTargetThreads) {
-                const int j = eg.in_src[i];
-                const int e = eg.in_edge[i];
-                const int c = (int)(net.edge_col[e] >> 27);
-                const int fcol = eg.in_fcol ? eg.in_fcol[i] : -1;
-                const int32_t *st = eg.ev_start + (size_t)j * (slices + 1) + sl;
-                const int q0 = st[0], q1 = st[1];
-                const float *qc = qs + (size_t)c * bq * Tp - base;
-                float acc = 0.0f;
-                if (j < N && fcol < 0) {
-                    for (int q = q0; q < q1; q++) acc += qc[__ldg(eg.ev + q)];
-                } else {  // input values and gating factors scale the events
-                    for (int q = q0; q < q1; q++) {
-                        const int ev = __ldg(eg.ev + q);
-                        const int b = ev / Tp, t = ev - b * Tp;
-                        const size_t bt = (size_t)b * T + t;
-                        float a = j >= N ? eg.x[bt * n_in + (j - N)] : 1.0f;
-                        if (fcol >= 0) a *= eg.f_saved[bt * net.R_f + fcol];
-                        acc += a * qc[ev];
+            for (int sl = 0; sl < slices; sl++) {
+                stage(n, sl);
+                const int base = sl * bq * Tp;
+                int q[kEdgeCache], qe[kEdgeCache], len = 0;
+                bool plain = true;
+#pragma unroll
+                for (int u = 0; u < kEdgeCache; u++) {
+                    q[u] = qe[u] = 0;
+                    if (cj[u] >= 0) {
+                        const int32_t *st = eg.ev_start + (size_t)cj[u] * (slices + 1) + sl;
+                        q[u] = st[0];
+                        qe[u] = st[1];
+                        len = max(len, qe[u] - q[u]);
+                        plain = plain && cj[u] < N && cf[u] < 0;
                     }
                 }
-                eg.in_acc[i] = sl ? eg.in_acc[i] + acc : acc;
+                if (plain) {  // unscaled spikes: the four sums interleaved
+                    for (int r = 0; r < len; r++) {
+#pragma unroll
+                        for (int u = 0; u < kEdgeCache; u++)
+                            if (q[u] + r < qe[u]) cacc[u] += qs[(size_t)cc[u] * bq * Tp - base + __ldg(eg.ev + q[u] + r)];
+                    }
+                } else {
+#pragma unroll
+                    for (int u = 0; u < kEdgeCache; u++)
+                        if (cj[u] >= 0)
+                            cacc[u] += slice_sum(net, eg, qs + (size_t)cc[u] * bq * Tp - base, cj[u], cf[u], q[u], qe[u],
+                                                 T, Tp);
+                }
             }
-        }
-        // the target's in-edges done: their gradients (this block alone writes them)
-        for (int i = i0 + tid; i < i1; i += kTargetThreads) {
-            const int e = eg.in_edge[i];
-            const int k = eg.in_path[i];
-            const int c = (int)(net.edge_col[e] >> 27);
-            const double acc = (double)eg.in_acc[i];
-            const double jfv = eg.jf[(size_t)k * C + c];
-            if (eg.g_w) eg.g_w[e] += acc * (double)eg.scale[(size_t)k * N + n] * jfv;
-            if (eg.g_scale) atomicAdd(eg.g_scale + (size_t)k * N + n, acc * (double)eg.w_raw[e] * jfv);
+#pragma unroll
+            for (int u = 0; u < kEdgeCache; u++)
+                if (cj[u] >= 0) finish(n, i0 + tid + u * kTargetThreads, cacc[u]);
+        } else {  // more in-edges than the registers hold: the sums kept in in_acc
+            for (int sl = 0; sl < slices; sl++) {
+                stage(n, sl);
+                const int base = sl * bq * Tp;
+                for (int i = i0 + tid; i < i1; i += kTargetThreads) {
+                    const int j = eg.in_src[i];
+                    const int c = eg.in_path[i] & 7;
+                    const int fcol = eg.in_fcol ? eg.in_fcol[i] : -1;
+                    const int32_t *st = eg.ev_start + (size_t)j * (slices + 1) + sl;
+                    const float acc = slice_sum(net, eg, qs + (size_t)c * bq * Tp - base, j, fcol, st[0], st[1], T, Tp);
+                    eg.in_acc[i] = sl ? eg.in_acc[i] + acc : acc;
+                }
+            }
+            for (int i = i0 + tid; i < i1; i += kTargetThreads) finish(n, i, eg.in_acc[i]);
         }
     }
 }

@@ -283,11 +283,15 @@ constexpr int kRef = 1, kSave = 2, kGeneric = 4, kMg = 8, kGate = 16, kAdapt = 3
 // for those with the Mg block, gating, adaptation or a partition, 16 for the others (up
 // to 128 registers).
 #ifndef WT_GATE_WARPS
-#define WT_GATE_WARPS 20
+#define WT_GATE_WARPS 24
+#endif
+#ifndef WT_PLAIN_WARPS
+#define WT_PLAIN_WARPS 24
 #endif
 template <int S, int FEAT>
 constexpr int warps_of() {
-    return ((FEAT & kGeneric) == 0 && S <= 4) ? ((FEAT & (kMg | kGate | kAdapt | kPart)) ? WT_GATE_WARPS : 24) : 16;
+    return ((FEAT & kGeneric) == 0 && S <= 4) ? ((FEAT & (kMg | kGate | kAdapt | kPart)) ? WT_GATE_WARPS : WT_PLAIN_WARPS)
+                                              : 16;
 }
 #ifndef WT_MAX_RING
 #define WT_MAX_RING 4

@@ -433,10 +433,10 @@ def segments(plan: Plan) -> list:
 
 def in_edges(plan: Plan) -> dict:
     """The in-edges of every target, for the target-by-target edge gradients: ``in_ptr``
-    (N + 1) and per in-edge (ordered by target, then pathway, then edge) its edge
-    ``in_edge``, source ``in_src``, pathway ``in_path`` and — in gated networks — its
-    gating factor's column of the saved factors ``in_fcol`` (-1: ungated); int32 each,
-    built once per plan."""
+    (N + 1) and per in-edge (ordered by target, then pathway and channel, then edge) its
+    edge ``in_edge``, source ``in_src``, pathway and input channel ``in_path`` (k 8 + c)
+    and — in gated networks — its gating factor's column of the saved factors
+    ``in_fcol`` (-1: ungated); int32 each, built once per plan."""
     t = plan.tensors
     if "_in_edges" not in t:
         dev = plan.device
@@ -445,7 +445,7 @@ def in_edges(plan: Plan) -> dict:
         for k, c, base, n_e, rows, cols in segments(plan):
             e_l.append(torch.arange(base, base + n_e, device=dev))
             j_l.append(plan.path_sources[k][rows])
-            k_l.append(torch.full((n_e,), k, dtype=torch.int64, device=dev))
+            k_l.append(torch.full((n_e,), k * 8 + c, dtype=torch.int64, device=dev))
             n_l.append(cols)
             fc = plan.gate_f_cols[k] if plan.gated and k < len(plan.gate_f_cols) else -1
             f_l.append(rows + fc if fc >= 0 else torch.full((n_e,), -1, dtype=torch.int64, device=dev))
@@ -453,7 +453,7 @@ def in_edges(plan: Plan) -> dict:
             e, j, kk, n, f = (torch.cat(v) for v in (e_l, j_l, k_l, n_l, f_l))
             # edge order already (segments in order of their base); then stably by target
             # and pathway
-            order = torch.argsort(n * max(plan.K, 1) + kk, stable=True)
+            order = torch.argsort(n * (8 * max(plan.K, 1)) + kk, stable=True)
             e, j, kk, n, f = e[order], j[order], kk[order], n[order], f[order]
         else:
             e = j = kk = n = f = torch.zeros(0, dtype=torch.int64, device=dev)
