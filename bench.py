@@ -363,7 +363,7 @@ def cpu_baseline(cfg, seconds_target=15.0, threads=None):
 
     threads = threads or os.cpu_count() or 1
     oracle.set_threads(threads)
-    B = min(cfg.B, threads)
+    B = cfg.B if cfg.B <= threads else threads * (cfg.B // threads)  # whole rounds of trials
     if _CPU_NET.get("cfg") is not cfg:  # the network on the host, built once per run
         cpu = _to_cpu(cfg)
         _CPU_NET.update(cfg=cfg, cpu=cpu, net=oracle.Network(cpu.drive, cpu.p, B, cfg.n_in))
@@ -383,8 +383,9 @@ def cpu_baseline(cfg, seconds_target=15.0, threads=None):
     net.simulate(x, v, g, **kw, track=False)
     el = time.perf_counter() - t0
     rate = B * T2 * cfg.N / el
-    used = min(threads, B)  # the oracle runs its trials in parallel, one thread each
-    return rate, used, f"{B} trials x {T2} steps of the {cfg.name} network, forward only ({el:.1f} s)"
+    # the oracle runs a thread per trial, or with fewer trials than threads splits each
+    # step's neurons over all of them
+    return rate, threads, f"{B} trials x {T2} steps of the {cfg.name} network, forward only ({el:.1f} s)"
 
 
 _CPU_NET: dict = {}
