@@ -54,6 +54,7 @@ enum {
     WT_F_PROB = 1 << 7,       /* escape-noise probabilities output */
     WT_F_SAVE_INPUT = 1 << 8, /* save each step's synaptic input X (learnt decay/jump) */
     WT_F_PARTITION = 1 << 9,  /* one rank of a neuron-partitioned run (WtForward.words...) */
+    WT_F_STREAM = 1 << 10,    /* keep the state in HBM even where it fits on chip (tests) */
 };
 
 /* The network as the kernels see it (built once per network and per call from the

@@ -75,3 +75,40 @@ def test_c5_model_lockstep_against_oracle(pool):
     assert float(run.output.sum()) > 20  # the network is active
     n_e = cfg.drive.gates[0].n
     assert float(run.gating[:, n_e : 2 * n_e].min()) < 0.99  # and its excitatory synapses depress
+
+
+def _streamed(drive, p, x, v, g, kw, stream):
+    engine.FORCE_STREAM = stream
+    try:
+        with torch.no_grad():
+            return engine.simulate(v, g, x, drive, p, **kw)
+    finally:
+        engine.FORCE_STREAM = False
+
+
+@pytest.mark.parametrize("feature", ["refractory", "everything"])
+@pytest.mark.parametrize("N", [3000, 1001])
+def test_streamed_state_gives_the_same_run(N, feature):
+    """The state streamed through shared memory every step (the path of networks too
+    large to keep it on chip: 16-byte pieces when N is a multiple of 4, else 4-byte
+    copies) gives the very run of the state kept on chip, bit for bit, and matches the
+    oracle in lockstep."""
+    drive, p, x, v, g, kw = random_network(N=N, n_in=200, B=3, T=80, seed=N, device="cuda", **FEATURES[feature])
+    on_chip = _streamed(drive, p, x, v, g, kw, False)
+    streamed = _streamed(drive, p, x, v, g, kw, True)
+    assert float(on_chip.output.sum()) > 0
+    assert torch.equal(on_chip.output, streamed.output)
+    assert torch.equal(on_chip.v, streamed.v)
+    assert torch.equal(on_chip.syn, streamed.syn)
+    net = oracle.Network(drive, p, x.shape[0], x.shape[2])
+
+    def sim(v_, g_, x_, kw_):
+        engine.FORCE_STREAM = True
+        try:
+            with torch.no_grad():
+                return engine.simulate(v_, g_, x_, drive, p, track=True, **kw_)
+        finally:
+            engine.FORCE_STREAM = False
+
+    excused, windows, dv, dg = lockstep.compare(sim, net, drive, p, x, v, g, kw)
+    assert excused <= 0.01 * windows

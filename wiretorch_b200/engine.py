@@ -37,6 +37,10 @@ _PLANS: dict = {}
 #: traverses (recurrent, input): the synaptic events of the run, counted on the device.
 EDGE_COUNTER = None
 
+#: Keep the forward kernel's state in HBM, streamed through shared memory every step,
+#: even where it would fit on chip (the path of networks too large for it; for tests).
+FORCE_STREAM = False
+
 #: If set to a list, every forward launch appends to it a (T, warps, WT_PHASES) int64
 #: tensor: per step and warp of the grid the global timer (ns) at the end of each phase
 #: of the step (instrumented runs; see ``WT_PHASES`` in the C header).
@@ -186,6 +190,8 @@ def run_forward(plan, p, x, v, g, counter, g_a, gating, *, probabilities=False, 
         flags |= _lib.F_SAMPLE
     if plan.gated:
         flags |= _lib.F_GATED
+    if FORCE_STREAM:
+        flags |= _lib.F_STREAM
     out = {"spikes": torch.empty((B, T, N), device=device)}
     run.v, run.g = v.data_ptr(), g.data_ptr()
     run.counter = _lib.ptr(counter) if flags & _lib.F_REFRACTORY else None
