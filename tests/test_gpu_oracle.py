@@ -90,9 +90,8 @@ def _streamed(drive, p, x, v, g, kw, stream):
 @pytest.mark.parametrize("N", [3000, 1001])
 def test_streamed_state_gives_the_same_run(N, feature):
     """The state streamed through shared memory every step (the path of networks too
-    large to keep it on chip: 16-byte pieces when N is a multiple of 4, else 4-byte
-    copies) gives the very run of the state kept on chip, bit for bit, and matches the
-    oracle in lockstep."""
+    large to keep it on chip) gives the very run of the state kept on chip, bit for bit,
+    and matches the oracle in lockstep."""
     drive, p, x, v, g, kw = random_network(N=N, n_in=200, B=3, T=80, seed=N, device="cuda", **FEATURES[feature])
     on_chip = _streamed(drive, p, x, v, g, kw, False)
     streamed = _streamed(drive, p, x, v, g, kw, True)

@@ -558,8 +558,6 @@ __global__ void event_list_kernel(const WtEdgeGrads eg, int n_src, int slices, i
     if (lane == 0) starts[slices] = base;
 }
 
-constexpr int kEdgeCache = 4;  // in-edges a thread keeps in registers over the slices
-
 // The sum over source j's events of one slice of a * QT (the slice staged at qc).
 __device__ __forceinline__ float slice_sum(const WtNet &net, const WtEdgeGrads &eg, const float *qc, int j, int fcol,
                                            int q0, int q1, int T, int Tp) {
@@ -616,72 +614,22 @@ __global__ void __launch_bounds__(kTargetThreads, 3) edge_grads_target_kernel(co
         if (n >= N) return;
         const int i0 = eg.in_ptr[n], i1 = eg.in_ptr[n + 1];
         if (i0 == i1) continue;
-        if (i1 - i0 <= kEdgeCache * kTargetThreads) {
-            // each thread's in-edges (up to kEdgeCache) kept in registers over the slices;
-            // their event sums run side by side
-            int cj[kEdgeCache], cc[kEdgeCache], cf[kEdgeCache];
-            float cacc[kEdgeCache];
-#pragma unroll
-            for (int u = 0; u < kEdgeCache; u++) {
-                const int i = i0 + tid + u * kTargetThreads;
-                cj[u] = -1;
-                cc[u] = 0;
-                cf[u] = -1;
-                cacc[u] = 0.0f;
-                if (i < i1) {
-                    cj[u] = eg.in_src[i];
-                    cc[u] = eg.in_path[i] & 7;
-                    cf[u] = eg.in_fcol ? eg.in_fcol[i] : -1;
-                }
+        // each thread's in-edges, slice by slice, the sums kept in in_acc (keeping up to
+        // four in-edges in registers across the slices and summing them side by side
+        // measured twice as slow on C2)
+        for (int sl = 0; sl < slices; sl++) {
+            stage(n, sl);
+            const int base = sl * bq * Tp;
+            for (int i = i0 + tid; i < i1; i += kTargetThreads) {
+                const int j = eg.in_src[i];
+                const int c = eg.in_path[i] & 7;
+                const int fcol = eg.in_fcol ? eg.in_fcol[i] : -1;
+                const int32_t *st = eg.ev_start + (size_t)j * (slices + 1) + sl;
+                const float acc = slice_sum(net, eg, qs + (size_t)c * bq * Tp - base, j, fcol, st[0], st[1], T, Tp);
+                eg.in_acc[i] = sl ? eg.in_acc[i] + acc : acc;
             }
-            for (int sl = 0; sl < slices; sl++) {
-                stage(n, sl);
-                const int base = sl * bq * Tp;
-                int q[kEdgeCache], qe[kEdgeCache], len = 0;
-                bool plain = true;
-#pragma unroll
-                for (int u = 0; u < kEdgeCache; u++) {
-                    q[u] = qe[u] = 0;
-                    if (cj[u] >= 0) {
-                        const int32_t *st = eg.ev_start + (size_t)cj[u] * (slices + 1) + sl;
-                        q[u] = st[0];
-                        qe[u] = st[1];
-                        len = max(len, qe[u] - q[u]);
-                        plain = plain && cj[u] < N && cf[u] < 0;
-                    }
-                }
-                if (plain) {  // unscaled spikes: the four sums interleaved
-                    for (int r = 0; r < len; r++) {
-#pragma unroll
-                        for (int u = 0; u < kEdgeCache; u++)
-                            if (q[u] + r < qe[u]) cacc[u] += qs[(size_t)cc[u] * bq * Tp - base + __ldg(eg.ev + q[u] + r)];
-                    }
-                } else {
-#pragma unroll
-                    for (int u = 0; u < kEdgeCache; u++)
-                        if (cj[u] >= 0)
-                            cacc[u] += slice_sum(net, eg, qs + (size_t)cc[u] * bq * Tp - base, cj[u], cf[u], q[u], qe[u],
-                                                 T, Tp);
-                }
-            }
-#pragma unroll
-            for (int u = 0; u < kEdgeCache; u++)
-                if (cj[u] >= 0) finish(n, i0 + tid + u * kTargetThreads, cacc[u]);
-        } else {  // more in-edges than the registers hold: the sums kept in in_acc
-            for (int sl = 0; sl < slices; sl++) {
-                stage(n, sl);
-                const int base = sl * bq * Tp;
-                for (int i = i0 + tid; i < i1; i += kTargetThreads) {
-                    const int j = eg.in_src[i];
-                    const int c = eg.in_path[i] & 7;
-                    const int fcol = eg.in_fcol ? eg.in_fcol[i] : -1;
-                    const int32_t *st = eg.ev_start + (size_t)j * (slices + 1) + sl;
-                    const float acc = slice_sum(net, eg, qs + (size_t)c * bq * Tp - base, j, fcol, st[0], st[1], T, Tp);
-                    eg.in_acc[i] = sl ? eg.in_acc[i] + acc : acc;
-                }
-            }
-            for (int i = i0 + tid; i < i1; i += kTargetThreads) finish(n, i, eg.in_acc[i]);
         }
+        for (int i = i0 + tid; i < i1; i += kTargetThreads) finish(n, i, eg.in_acc[i]);
     }
 }
 

@@ -53,7 +53,6 @@ struct Geometry {
     int max_items;                // most items of one warp
     int D;                        // ring slots per warp (copies issued D items ahead)
     int slot_rows, warp_rows;     // 128-byte rows of a ring slot, of a warp's shared memory
-    int st16;                     // streamed state copied in 16-byte pieces (rows 16-byte aligned)
 };
 
 namespace {
@@ -361,33 +360,6 @@ __global__ void __launch_bounds__(warps_of<S, FEAT>() * 32, 1) forward_kernel(co
     const int D = geo.D, ks = geo.ks, w_cnt = geo.w_cnt, w_ga = geo.w_ga, w_gd = geo.w_gd;
     const int slot_words = geo.slot_rows * 32;
     GridBarrier bar(ws.barrier, gridDim.x);
-    // Streamed state in 16-byte pieces: each state word's row for trial b, neurons n is
-    // s_wrow[w] + b N s_wmul[w] + n (v, counter and adaptation: (B, N); the conductances'
-    // rise and decay rows: (B, 2, S, N)). Filled before the first grid barrier.
-    __shared__ const float *s_wrow[4 + 2 * WT_MAX_CHANNELS];
-    __shared__ unsigned s_wmul[4 + 2 * WT_MAX_CHANNELS];
-    if (threadIdx.x == 0 && geo.st16) {
-        s_wrow[0] = run.v;
-        s_wmul[0] = 1;
-        if (REF) {
-            s_wrow[geo.w_cnt] = reinterpret_cast<const float *>(run.counter);
-            s_wmul[geo.w_cnt] = 1;
-        }
-        if (ADAPT) {
-            s_wrow[geo.w_ga] = run.g_a;
-            s_wmul[geo.w_ga] = 1;
-        }
-        int r = 0;
-        for (int c = 0; c < S; c++) {
-            s_wrow[geo.w_gd + c] = run.g + (size_t)(S + c) * N;
-            s_wmul[geo.w_gd + c] = 2 * S;
-            if (net.decay_r[c] != 0.0f) {
-                s_wrow[geo.w_gr + r] = run.g + (size_t)c * N;
-                s_wmul[geo.w_gr + r] = 2 * S;
-                r++;
-            }
-        }
-    }
     // instrumented runs: lane 0 of each warp stamps the end of each phase of a step
     unsigned long long *const phases =
         (run.phases && gwarp < run.phase_warps) ? run.phases + (size_t)gwarp * WT_PHASES : nullptr;
@@ -463,13 +435,7 @@ __global__ void __launch_bounds__(warps_of<S, FEAT>() * 32, 1) forward_kernel(co
                 for (int k = lane; k < C * 16; k += 32, src += 2 * BNp, dst += 128) cp_async16(dst, src);
             }
             const int n = q.g * 32 + lane;
-            if (!RES && geo.st16) {  // each state word's 128-byte row in eight 16-byte pieces
-                float *st = slot + 2 * C * 32;
-                for (int k = lane; k < ks * 8; k += 32) {
-                    const int w = k >> 3, n0 = q.g * 32 + 4 * (k & 7);
-                    if (n0 < N) cp_async16(st + w * 32 + 4 * (k & 7), s_wrow[w] + q.bN * s_wmul[w] + n0);
-                }
-            } else if (!RES && n < N) {
+            if (!RES && n < N) {
                 const size_t o = q.bN + n;
                 const float *g_b = run.g + q.bN * 2 * S + n;
                 float *st = slot + 2 * C * 32 + lane;
@@ -1237,10 +1203,6 @@ static cudaError_t launch_sf(const WtNet &net, const WtForward &run, const WtWor
     WtNet n = net;
     WtForward r = run;
     WtWorkspace w = ws;
-    // streamed state in 16-byte pieces when every state row starts on a 16-byte boundary
-    auto a16 = [](const void *ptr) { return ((uintptr_t)ptr & 15) == 0; };
-    geo.st16 = !geo.resident && net.N % 4 == 0 && a16(run.v) && a16(run.g) &&
-               (!(run.flags & WT_F_REFRACTORY) || a16(run.counter)) && (!(run.flags & WT_F_ADAPT) || a16(run.g_a));
     void *args[] = {&n, &r, &w, &geo};
     return cudaLaunchCooperativeKernel((const void *)forward_kernel<S, FEAT>, dim3(grid), dim3(warps_of<S, FEAT>() * 32), args, dyn,
                                        st);
