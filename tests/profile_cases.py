@@ -9,7 +9,8 @@ neurons (4 trials, gated, pooled), 300 steps from rest, then one 20-step call;
 of the kernel is the one to capture (``-s 1 -c 1``). ``c2-step``: two C2 training steps
 (every kernel of the second step is one to capture; ``c2-step-16`` with 16 trials, for
 captures of many passes); ``c2-carry``: the per-step carry of
-gradients through the recurrent spikes; ``c3-product``: the tensor-core product alone.
+gradients through the recurrent spikes; ``c3-product``: the tensor-core product alone; ``misc``: one launch each of the
+filter, fold, input-gradient, carry and product kernels.
 """
 
 from __future__ import annotations
@@ -140,7 +141,32 @@ def c3_product():
     print(f"c3-product: {tuple(out.shape)}")
 
 
-CASES = {"c2-active": c2_active, "c3-small": c3_small, "c5-small": c5_small, "c5-full": c5_full,
+def misc():
+    """One launch each of the kernels outside the training step's main three: the
+    double-exponential filter forward and backward on C2's output shape (64 x 500 x
+    20,000), the weight fold of C2, the input gradient (C2 at 16 trials, 100 steps, the
+    input requiring grad), the recurrent carry (``c2_carry``) and the factorised product
+    (``c3_product``)."""
+    from wiretorch_b200 import configs, engine, filtering
+
+    gen = torch.Generator(device="cuda").manual_seed(0)
+    x = (torch.rand((64, 500, 20000), generator=gen, device="cuda") < 0.0015).float().requires_grad_(True)
+    t = torch.arange(500, dtype=torch.float32, device="cuda") * 0.1
+    rise, smooth = filtering.double_exponential(x, torch.exp(-t / 0.1), torch.exp(-t / 20.0), None, None)
+    smooth.sum().backward()
+    cfg = configs.c2(B=16, T=100, device="cuda")
+    engine.POOL_SYNAPSES = True
+    xi = cfg.inputs(seed=1).requires_grad_(True)
+    v, g, kw = cfg.state()
+    run = engine.simulate(v, g, xi, cfg.drive, cfg.p, **kw)  # folds the weights, saves for backward
+    (run.output * torch.randn_like(run.output)).sum().backward()
+    torch.cuda.synchronize()
+    c2_carry()
+    c3_product()
+    print(f"misc: |dL/dx| {float(xi.grad.norm()):.3e}")
+
+
+CASES = {"c2-active": c2_active, "misc": misc, "c3-small": c3_small, "c5-small": c5_small, "c5-full": c5_full,
          "c2-step": c2_step, "c2-step-16": lambda: c2_step(16), "c2-carry": c2_carry,
          "c3-product": c3_product}  # fmt: skip
 

@@ -58,10 +58,10 @@ class _LonelyPartition:
 
 
 def test_partition_progress_wait_gives_up():
-    """A bounded device wait that runs out: the exchange of a neuron-partitioned step
+    """A bounded device wait that runs out: the barrier of a neuron-partitioned step
     waits for every rank's progress slot; with the partner's slot never written, the
     spin gives up after its poll limit (well under a second), the kernel records
-    ``WT_ERR_BARRIER`` and every block leaves at the next grid barrier; the host raises.
+    ``WT_ERR_BARRIER`` and every block leaves at that barrier; the host raises.
     The context stays usable: a normal run follows and succeeds."""
     from wiretorch_b200 import plan as P
 

@@ -68,6 +68,57 @@ struct GridBarrier {
         __syncthreads();
         return ok;
     }
+
+    // The barrier of a neuron-partitioned run's step, fused with its exchange of progress:
+    // the last block to arrive writes `mine` into every rank's progress slot of this rank
+    // (`peer_progress[r] + rank`), waits (bounded) until every rank's slot here (`slots[r]`) holds at
+    // least `mine`, and only then releases the blocks. One grid barrier instead of a barrier,
+    // a progress exchange by one block and a second barrier.
+    __device__ bool sync_progress(int32_t *err, unsigned long long *const *peer_progress, int rank,
+                                  const unsigned long long *slots, int n_ranks, unsigned long long mine) {
+        __shared__ int ok;
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            const unsigned g = local;
+            __threadfence_system();  // this block's spike words, before the ranks learn of them
+            const unsigned arrived = atomicAdd(count, 1u);
+            if (arrived == nblocks - 1) {
+                atomicExch(count, 0u);
+                __threadfence_system();
+                for (int r = 0; r < n_ranks; r++)
+                    asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(peer_progress[r] + rank), "l"(mine)
+                                 : "memory");
+                for (int r = 0; r < n_ranks; r++) {
+                    unsigned long long spins = 0, seen = 0;
+                    for (;;) {
+                        asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(seen) : "l"(slots + r) : "memory");
+                        if (seen >= mine) break;
+                        if (++spins > kSpinLimit) {
+                            set_error(err, WT_ERR_BARRIER);
+                            break;
+                        }
+                        __nanosleep(64);
+                    }
+                }
+                __threadfence();
+                atomicExch(gen, g + 1);
+            } else {
+                unsigned long long spins = 0;
+                while (ld_acquire(gen) == g) {
+                    if (++spins > 4 * kSpinLimit) {  // the last block may wait its own limit for the ranks
+                        set_error(err, WT_ERR_BARRIER);
+                        break;
+                    }
+                    __nanosleep(64);
+                }
+            }
+            __threadfence();
+            local = g + 1;
+            ok = read_error(err) == 0;
+        }
+        __syncthreads();
+        return ok;
+    }
 };
 
 __device__ __forceinline__ float sigmoid(float x) { return 1.0f / (1.0f + expf(-x)); }

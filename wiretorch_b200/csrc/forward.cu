@@ -535,30 +535,15 @@ __global__ void __launch_bounds__(warps_of<S, FEAT>() * 32, 1) forward_kernel(co
             for (int r = 0; r < run.n_ranks; r++) run.peer_words[r][wi] = word;
         }
     };
-    // ... and once every rank has published `step` (each rank's progress slot, written
-    // by block 0 of its kernel after a grid barrier, waited for with a bounded spin),
-    // the events of that step of every source from the words. Leaves after a grid
-    // barrier; false when an error ended the run.
+    // ... and once every rank has published `step`, the events of that step of every
+    // source from the words. The step's grid barrier is fused with the exchange of
+    // progress (GridBarrier::sync_progress: the last block to arrive writes this rank's
+    // progress slot, (epoch << 32) | step + 1, into every rank and waits, bounded, for
+    // every rank's, before it releases the grid). Leaves after a second grid barrier;
+    // false when an error ended the run.
     auto exchange = [&](int step) -> bool {
-        if (blockIdx.x == 0 && threadIdx.x == 0) {
-            const unsigned long long mine = ((unsigned long long)run.epoch << 32) | (unsigned)(step + 1);
-            for (int r = 0; r < run.n_ranks; r++)
-                asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(run.peer_progress[r] + run.rank), "l"(mine)
-                             : "memory");
-            for (int r = 0; r < run.n_ranks; r++) {
-                unsigned long long spins = 0, seen = 0;
-                for (;;) {
-                    asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(seen) : "l"(run.progress + r) : "memory");
-                    if (seen >= mine) break;
-                    if (++spins > kSpinLimit) {
-                        set_error(ws.err, WT_ERR_BARRIER);
-                        break;
-                    }
-                    __nanosleep(64);
-                }
-            }
-        }
-        if (!bar.sync(ws.err)) return false;
+        const unsigned long long mine = ((unsigned long long)run.epoch << 32) | (unsigned)(step + 1);
+        if (!bar.sync_progress(ws.err, run.peer_progress, run.rank, run.progress, run.n_ranks, mine)) return false;
         const uint32_t *wsrc = run.words + (size_t)(step & 1) * B * words_src;
         const long long n_words = (long long)B * words_src;
         // a warp takes 32 words at once (one per lane) and walks the ones with a spike;
@@ -694,9 +679,11 @@ __global__ void __launch_bounds__(warps_of<S, FEAT>() * 32, 1) forward_kernel(co
         }
     };
     load_x(run.t0 + 1);
-    if (PART) __threadfence_system();  // the published words, before the barrier
-    if (!bar.sync(ws.err)) return;
-    if (PART && !exchange(0)) return;
+    if (PART) {
+        if (!exchange(0)) return;  // its barrier fences the published words first
+    } else if (!bar.sync(ws.err)) {
+        return;
+    }
 
     for (int t = 0; t < T; t++) {
         const int t_abs = run.t0 + t;
@@ -1036,10 +1023,13 @@ __global__ void __launch_bounds__(warps_of<S, FEAT>() * 32, 1) forward_kernel(co
         stamp(t, 3);
         if (scatter_late) scatter();
         stamp(t, 4);
-        if (PART) __threadfence_system();
-        if (!bar.sync(ws.err)) return;
-        stamp(t, 5);
-        if (PART && emit_next && !exchange(t + 1)) return;
+        if (PART && emit_next) {  // the step's barrier is the exchange's
+            stamp(t, 5);
+            if (!exchange(t + 1)) return;
+        } else {
+            if (!bar.sync(ws.err)) return;
+            stamp(t, 5);
+        }
         stamp(t, 6);
     }
 
