@@ -40,6 +40,8 @@ enum {
     WT_ERR_EVENTS = 4,      /* device: an event list overflowed its capacity */
     WT_ERR_FIXED_POINT = 5, /* device: a synaptic input exceeded the fixed-point range */
     WT_ERR_UNSUPPORTED = 6, /* a combination the kernels do not implement */
+    WT_ERR_RANGE = 7,       /* device: an index outside its table (partitioned runs check; the
+                             * bits above 8 name the check), the access skipped */
 };
 
 /* Feature flags of a forward run (WtForward.flags). */
@@ -103,6 +105,13 @@ typedef struct {
     const int32_t *src_gate;
 } WtNet;
 
+/* One scatter work item: a chunk of a source's edges, for one trial. */
+typedef struct {
+    int64_t edge;               /* first edge */
+    uint32_t trial_len;         /* trial << 8 | edge count */
+    float amp;                  /* the spike's (or input's) value times its gating factor */
+} WtEvent;
+
 /* Buffers of one forward run of T steps (outputs indexed by step t0 + t of a chunk of
  * T_total steps, so a chunk may be run in several launches). */
 typedef struct {
@@ -145,6 +154,28 @@ typedef struct {
      * source's gates from the spike words. */
     float *amps;
     float *peer_amps[8];
+    /* optional, a partitioned run whose ranks push their events (networks without gating,
+     * or whose gates their owners step): instead of publishing spike words for every rank
+     * to walk, a rank writes the events of its own neurons' spikes onto each rank r's
+     * targets straight into r's inbound event area over the interconnect, so that a step
+     * takes one grid barrier (fused with the progress exchange). Per rank r: r's chunk
+     * range of every neuron (push_src_chunk[r], N_src + 1 entries) and r's chunk
+     * descriptors (push_chunk_desc[r]), local copies; this rank's region of r's area
+     * (push_ev[r], push_cap[r] events, the two step parities push_half[r] events apart)
+     * and r's inbound counts (push_count[r]: [2][8], this rank's at [parity][rank]).
+     * push_reserve ([2][8], zeroed): this rank's reservations per parity and rank. This
+     * rank's own area: pull_ev (regions pull_off[q] of source rank q, parities pull_half
+     * apart) and pull_count ([2][8], written by the ranks). NULL push_reserve: words. */
+    const int32_t *push_src_chunk[8];
+    const long long *push_chunk_desc[8];
+    WtEvent *push_ev[8];
+    long long push_cap[8], push_half[8];
+    uint32_t *push_count[8];
+    uint32_t *push_reserve;
+    const WtEvent *pull_ev;
+    long long pull_off[8];
+    long long pull_half;
+    const uint32_t *pull_count;
     /* optional, instrumented runs: per step and warp of the grid, the global timer (ns)
      * at the ends of the step's phases, (T, phase_warps, WT_PHASES); warps of the grid
      * beyond phase_warps record nothing. NULL: no record. */
@@ -158,13 +189,6 @@ typedef struct {
  * spike emission); the late scatter done (the odd warps); the grid barrier passed; the
  * spike exchange of a partitioned run done (its progress wait, barrier and emission). */
 #define WT_PHASES 7
-
-/* One scatter work item: a chunk of a source's edges, for one trial. */
-typedef struct {
-    int64_t edge;               /* first edge */
-    uint32_t trial_len;         /* trial << 8 | edge count */
-    float amp;                  /* the spike's (or input's) value times its gating factor */
-} WtEvent;
 
 /* Scratch memory of a forward run; all of it device memory the caller allocated. */
 typedef struct {

@@ -17,7 +17,7 @@ MAX_CHANNELS = 8
 CHUNK_EDGES = 128
 EVENT_BYTES = 16  # sizeof(WtEvent)
 
-OK, ERR_ARGS, ERR_LAUNCH, ERR_BARRIER, ERR_EVENTS, ERR_FIXED_POINT, ERR_UNSUPPORTED = range(7)
+OK, ERR_ARGS, ERR_LAUNCH, ERR_BARRIER, ERR_EVENTS, ERR_FIXED_POINT, ERR_UNSUPPORTED, ERR_RANGE = range(8)
 PHASES = 7  # WT_PHASES: the phases of a forward step that WtForward.phases records
 ERRORS = {
     ERR_ARGS: "inconsistent arguments",
@@ -26,6 +26,7 @@ ERRORS = {
     ERR_EVENTS: "an event list overflowed",
     ERR_FIXED_POINT: "a synaptic input exceeded the fixed-point range",
     ERR_UNSUPPORTED: "unsupported configuration",
+    ERR_RANGE: "a device index outside its table (range check)",
 }
 
 F_REFRACTORY, F_MG_BLOCK, F_ADAPT, F_SAMPLE, F_GATED = 1, 2, 4, 8, 16
@@ -68,6 +69,10 @@ class WtForward(C.Structure):
         ("words", P), ("peer_words", P * 8), ("progress", P), ("peer_progress", P * 8),
         ("n_ranks", C.c_int32), ("rank", C.c_int32), ("word0", C.c_int32), ("epoch", C.c_uint32),
         ("amps", P), ("peer_amps", P * 8),
+        ("push_src_chunk", P * 8), ("push_chunk_desc", P * 8), ("push_ev", P * 8),
+        ("push_cap", C.c_longlong * 8), ("push_half", C.c_longlong * 8), ("push_count", P * 8),
+        ("push_reserve", P), ("pull_ev", P), ("pull_off", C.c_longlong * 8), ("pull_half", C.c_longlong),
+        ("pull_count", P),
         ("phases", P), ("phase_warps", C.c_int32),
     ]  # fmt: skip
 

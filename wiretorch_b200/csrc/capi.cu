@@ -136,6 +136,13 @@ int check_forward(const WtNet *net, const WtForward *run, const WtWorkspace *ws)
             return fail(WT_ERR_ARGS, "bad partition%s");
         for (int r = 0; r < run->n_ranks; r++)
             if (!run->peer_words[r] || !run->peer_progress[r]) return fail(WT_ERR_ARGS, "missing peer buffers%s");
+        if (run->push_reserve) {  // pushed events
+            if ((f & WT_F_GATED) && !run->amps) return fail(WT_ERR_ARGS, "a gated run pushes its events only with owner-stepped gates%s");
+            if (!run->pull_ev || !run->pull_count) return fail(WT_ERR_ARGS, "missing inbound event area%s");
+            for (int r = 0; r < run->n_ranks; r++)
+                if (!run->push_src_chunk[r] || !run->push_chunk_desc[r] || !run->push_ev[r] || !run->push_count[r])
+                    return fail(WT_ERR_ARGS, "missing push tables%s");
+        }
         if (run->amps) {  // owner-stepped gates
             if (!(f & WT_F_GATED) || !net->src_gate) return fail(WT_ERR_ARGS, "amplitudes need a gated net with src_gate%s");
             for (int r = 0; r < run->n_ranks; r++)

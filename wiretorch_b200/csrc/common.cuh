@@ -73,9 +73,13 @@ struct GridBarrier {
     // the last block to arrive writes `mine` into every rank's progress slot of this rank
     // (`peer_progress[r] + rank`), waits (bounded) until every rank's slot here (`slots[r]`) holds at
     // least `mine`, and only then releases the blocks. One grid barrier instead of a barrier,
-    // a progress exchange by one block and a second barrier.
+    // a progress exchange by one block and a second barrier. With `reserve` (a run that
+    // pushes its events: this rank's event counts per step parity and destination rank,
+    // [2][8]), the last block first writes parity `par`'s counts into every rank's inbound
+    // counts (`push_count[r][par * 8 + rank]`) and clears them for the step after next.
     __device__ bool sync_progress(int32_t *err, unsigned long long *const *peer_progress, int rank,
-                                  const unsigned long long *slots, int n_ranks, unsigned long long mine) {
+                                  const unsigned long long *slots, int n_ranks, unsigned long long mine,
+                                  uint32_t *reserve = nullptr, uint32_t *const *push_count = nullptr, int par = 0) {
         __shared__ int ok;
         __syncthreads();
         if (threadIdx.x == 0) {
@@ -84,6 +88,13 @@ struct GridBarrier {
             const unsigned arrived = atomicAdd(count, 1u);
             if (arrived == nblocks - 1) {
                 atomicExch(count, 0u);
+                __threadfence();
+                if (reserve) {
+                    for (int r = 0; r < n_ranks; r++) {
+                        const unsigned v = atomicExch(reserve + par * 8 + r, 0u);
+                        push_count[r][par * 8 + rank] = v;
+                    }
+                }
                 __threadfence_system();
                 for (int r = 0; r < n_ranks; r++)
                     asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(peer_progress[r] + rank), "l"(mine)

@@ -535,6 +535,59 @@ __global__ void __launch_bounds__(warps_of<S, FEAT>() * 32, 1) forward_kernel(co
             for (int r = 0; r < run.n_ranks; r++) run.peer_words[r][wi] = word;
         }
     };
+    // A rank that pushes its events (PUSH): the warp's sources jg (this rank's neurons,
+    // global indices) that fire at `step` with `amp` get their events onto every rank r's
+    // targets written straight into r's inbound area: one reservation per warp and rank
+    // (this rank's local counter), all 32 lanes writing each firing source's chunks.
+    const bool PUSH = PART && run.push_reserve != nullptr;
+    // the edges of the network (partitioned runs check every event's edges against them)
+    long long n_edges_all = 0;
+    if (PART && net.n_chunks > 0) {
+        const unsigned long long d = (unsigned long long)net.chunk_desc[net.n_chunks - 1];
+        n_edges_all = (long long)(d & ((1ull << 56) - 1)) + (long long)(d >> 56);
+    }
+    auto push = [&](int step, int b, int jg, bool on, float amp) {
+        if (!__any_sync(kFull, on)) return;
+        for (int r = 0; r < run.n_ranks; r++) {
+            int c0 = 0, cnt = 0;
+            if (on && (jg < 0 || jg >= Nsrc)) {  // range checks of the pushed events: a record, no access
+                set_error(ws.err, WT_ERR_RANGE | (1 << 8));
+            } else if (on) {
+                const int32_t *sc = run.push_src_chunk[r];
+                c0 = sc[jg];
+                cnt = sc[jg + 1] - c0;
+                if (cnt < 0 || c0 < 0 || c0 + cnt > sc[Nsrc]) {
+                    set_error(ws.err, WT_ERR_RANGE | (2 << 8));
+                    cnt = 0;
+                }
+            }
+            const int incl = warp_inclusive_sum(cnt, lane);
+            const int total = __shfl_sync(kFull, incl, 31);
+            if (total == 0) continue;
+            unsigned base = 0;
+            if (lane == 31) base = atomicAdd(run.push_reserve + (step & 1) * 8 + r, (unsigned)total);
+            base = __shfl_sync(kFull, base, 31);
+            int4 *evs = reinterpret_cast<int4 *>(run.push_ev[r] + (size_t)(step & 1) * run.push_half[r]);
+            const long long *desc = run.push_chunk_desc[r];
+            unsigned m = __ballot_sync(kFull, cnt > 0);
+            while (m) {
+                const int l = __ffs(m) - 1;
+                m &= m - 1;
+                const int lc0 = __shfl_sync(kFull, c0, l), lcnt = __shfl_sync(kFull, cnt, l);
+                const long long off = (long long)base + __shfl_sync(kFull, incl, l) - lcnt;
+                const int a = __float_as_int(__shfl_sync(kFull, amp, l));
+                for (int q = lane; q < lcnt; q += 32) {
+                    if (off + q >= run.push_cap[r]) {
+                        set_error(ws.err, WT_ERR_EVENTS);
+                        break;
+                    }
+                    const unsigned long long d = (unsigned long long)desc[lc0 + q];
+                    evs[off + q] = make_int4((int)(unsigned)d, (int)(unsigned)((d >> 32) & 0xffffffu),
+                                             (int)(((unsigned)b << 8) | (unsigned)(d >> 56)), a);
+                }
+            }
+        }
+    };
     // ... and once every rank has published `step`, the events of that step of every
     // source from the words. The step's grid barrier is fused with the exchange of
     // progress (GridBarrier::sync_progress: the last block to arrive writes this rank's
@@ -543,6 +596,9 @@ __global__ void __launch_bounds__(warps_of<S, FEAT>() * 32, 1) forward_kernel(co
     // false when an error ended the run.
     auto exchange = [&](int step) -> bool {
         const unsigned long long mine = ((unsigned long long)run.epoch << 32) | (unsigned)(step + 1);
+        if (PUSH)  // the events are in place: the barrier publishes their counts with the progress
+            return bar.sync_progress(ws.err, run.peer_progress, run.rank, run.progress, run.n_ranks, mine,
+                                     run.push_reserve, run.push_count, step & 1);
         if (!bar.sync_progress(ws.err, run.peer_progress, run.rank, run.progress, run.n_ranks, mine)) return false;
         const uint32_t *wsrc = run.words + (size_t)(step & 1) * B * words_src;
         const long long n_words = (long long)B * words_src;
@@ -627,15 +683,18 @@ __global__ void __launch_bounds__(warps_of<S, FEAT>() * 32, 1) forward_kernel(co
                 s = spike_of(v, k.theta, cnt, u01, sflags, ksur, held);
             }
             if (PART) {
+                float amp = s;
+                const int jg = run.word0 * 32 + n;
                 if (OG) {
-                    const int jg = run.word0 * 32 + n;
                     const SrcGate G = valid ? src_gate_of(net, jg) : no_gate();
                     if (G.gate == -2) set_error(ws.err, WT_ERR_UNSUPPORTED);
-                    float amp = s;
                     if (valid && G.gate >= 0) amp = s * step_gate(G, 0, q.b, s);
-                    publish_amp(0, q.b, jg, valid && s != 0.0f, amp);
+                    if (!PUSH) publish_amp(0, q.b, jg, valid && s != 0.0f, amp);
                 }
-                publish(0, q.b, q.g, s);
+                if (PUSH)
+                    push(0, q.b, jg, valid && s != 0.0f, amp);
+                else
+                    publish(0, q.b, q.g, s);
             } else {
                 emit_neuron(0, valid, q.b, n, k, s);
             }
@@ -680,7 +739,8 @@ __global__ void __launch_bounds__(warps_of<S, FEAT>() * 32, 1) forward_kernel(co
     };
     load_x(run.t0 + 1);
     if (PART) {
-        if (!exchange(0)) return;  // its barrier fences the published words first
+        __threadfence_system();  // this thread's stores to the ranks (words, events), first
+        if (!exchange(0)) return;
     } else if (!bar.sync(ws.err)) {
         return;
     }
@@ -740,21 +800,49 @@ __global__ void __launch_bounds__(warps_of<S, FEAT>() * 32, 1) forward_kernel(co
         // X_{t-1} and the events of t + 1), so half the warps of a block scatter before
         // their items and half after: the reductions drain while the other half computes.
         auto scatter = [&]() {
-            const long long count = min((long long)*reinterpret_cast<volatile unsigned *>(&ws.ev_count[t]),
-                                        (long long)ws.ev_cap);  // never above: one event per (trial, chunk)
+            const long long n_local = min((long long)*reinterpret_cast<volatile unsigned *>(&ws.ev_count[t]),
+                                          (long long)ws.ev_cap);  // never above: one event per (trial, chunk)
             const WtEvent *evs = ws.ev + (size_t)(t & 1) * ws.ev_cap;
+            // a pushing rank's events of step t: its own list (the input columns), then the
+            // region of each rank in its inbound area, counts published with the progress
+            // (a count is never above its region's room; clamped all the same, so that no
+            // read leaves the area)
+            auto pulled = [&](int r) -> long long {
+                const long long room = (r + 1 < run.n_ranks ? run.pull_off[r + 1] : run.pull_half) - run.pull_off[r];
+                return min((long long)__ldcg(run.pull_count + (t & 1) * 8 + r), room);
+            };
+            long long count = n_local;
+            if (PUSH)
+                for (int r = 0; r < run.n_ranks; r++) count += pulled(r);
+            const WtEvent *pull = PUSH ? run.pull_ev + (size_t)(t & 1) * run.pull_half : nullptr;
             unsigned long long *X = ws.X + (size_t)(t & 1) * C * BNp;
             for (long long base = gwarp; base < count; base += nwarps * 32) {
                 // lane k holds event base + k nwarps: the events go round the warps
                 int4 raw = make_int4(0, 0, 0, 0);
                 const long long mine = base + lane * nwarps;
-                if (mine < count) raw = __ldcg(reinterpret_cast<const int4 *>(evs + mine));
+                if (mine < n_local) {
+                    raw = __ldcg(reinterpret_cast<const int4 *>(evs + mine));
+                } else if (mine < count) {
+                    long long m = mine - n_local;
+                    for (int r = 0; r < run.n_ranks; r++) {
+                        const long long cr = pulled(r);
+                        if (m < cr) {
+                            raw = __ldcg(reinterpret_cast<const int4 *>(pull + run.pull_off[r] + m));
+                            break;
+                        }
+                        m -= cr;
+                    }
+                }
                 const int ne = (int)min(32LL, (count - base + nwarps - 1) / nwarps);
                 unsigned long long cw[4], cw_n[4];
                 auto load = [&](int e, unsigned long long *dst) {
                     const unsigned x = __shfl_sync(kFull, raw.x, e), y = __shfl_sync(kFull, raw.y, e);
-                    const int len = __shfl_sync(kFull, raw.z, e) & 255;
+                    int len = __shfl_sync(kFull, raw.z, e) & 255;
                     const long long e0 = ((long long)y << 32) | x;
+                    if (PART && (e0 < 0 || e0 + len > n_edges_all || len > WT_CHUNK_EDGES)) {
+                        if (lane == 0) set_error(ws.err, WT_ERR_RANGE | (3 << 8));
+                        len = 0;
+                    }
 #pragma unroll
                     for (int u = 0; u < 4; u++) {
                         const int q = lane + 32 * u;
@@ -765,10 +853,14 @@ __global__ void __launch_bounds__(warps_of<S, FEAT>() * 32, 1) forward_kernel(co
                 for (int e = 0; e < ne; e++) {
                     const unsigned bl = (unsigned)__shfl_sync(kFull, raw.z, e);
                     const float amp = __int_as_float(__shfl_sync(kFull, raw.w, e));
-                    const int len = (int)(bl & 255u);
+                    int len = (int)(bl & 255u);
 #pragma unroll
                     for (int u = 0; u < 4; u++) cw[u] = cw_n[u];
                     if (e + 1 < ne) load(e + 1, cw_n);
+                    if (PART && ((int)(bl >> 8) >= B || len > WT_CHUNK_EDGES)) {
+                        if (lane == 0) set_error(ws.err, WT_ERR_RANGE | (4 << 8));
+                        len = 0;
+                    }
                     unsigned long long *Xb = X + (size_t)(bl >> 8) * Np;
                     if (ws.edges) {  // counting edges (instrumented runs)
                         const unsigned x = __shfl_sync(kFull, raw.x, e), y = __shfl_sync(kFull, raw.y, e);
@@ -783,6 +875,10 @@ __global__ void __launch_bounds__(warps_of<S, FEAT>() * 32, 1) forward_kernel(co
                         const float prod = __uint_as_float((uint32_t)(cw[u] >> 32)) * amp;
                         if (fabsf(prod) >= 0x1p62f) {
                             set_error(ws.err, WT_ERR_FIXED_POINT);
+                            continue;
+                        }
+                        if (PART && ((int)(col & 0x7ffffffu) >= N || (int)(col >> 27) >= C)) {
+                            set_error(ws.err, WT_ERR_RANGE | (5 << 8));
                             continue;
                         }
                         atomicAdd(Xb + (size_t)(col >> 27) * BNp + (col & 0x7ffffffu),
@@ -985,8 +1081,8 @@ __global__ void __launch_bounds__(warps_of<S, FEAT>() * 32, 1) forward_kernel(co
             }
             if (emit_next) {
                 if (PART) {
+                    float amp = s_next;
                     if (OG) {
-                        float amp = s_next;
                         if (gstep) {
                             const float f = gate_math(net.gate_params + 5 * kg.gate, kg.u_off >= 0, kg.a_off >= 0, gu, gx, gsa, s_next);
                             if (kg.u_off >= 0) {
@@ -996,9 +1092,12 @@ __global__ void __launch_bounds__(warps_of<S, FEAT>() * 32, 1) forward_kernel(co
                             if (kg.a_off >= 0) gb[kg.a_off] = gsa;
                             amp = s_next * f;
                         }
-                        publish_amp(t + 1, b, run.word0 * 32 + n, valid && s_next != 0.0f, amp);
+                        if (!PUSH) publish_amp(t + 1, b, run.word0 * 32 + n, valid && s_next != 0.0f, amp);
                     }
-                    publish(t + 1, b, q.g, s_next);
+                    if (PUSH)
+                        push(t + 1, b, run.word0 * 32 + n, valid && s_next != 0.0f, amp);
+                    else
+                        publish(t + 1, b, q.g, s_next);
                 } else if (GN && !gmulti) {
                     float amp = s_next;
                     if (gstep) {
@@ -1024,6 +1123,7 @@ __global__ void __launch_bounds__(warps_of<S, FEAT>() * 32, 1) forward_kernel(co
         if (scatter_late) scatter();
         stamp(t, 4);
         if (PART && emit_next) {  // the step's barrier is the exchange's
+            __threadfence_system();  // this thread's stores to the ranks (words, events), first
             stamp(t, 5);
             if (!exchange(t + 1)) return;
         } else {

@@ -132,7 +132,7 @@ def check_device(err: torch.Tensor, what: str) -> None:
     """Raise if a kernel recorded an error (synchronises)."""
     code = int(err.item())
     if code:
-        raise RuntimeError(f"{what}: {_lib.ERRORS.get(code, code)}")
+        raise RuntimeError(f"{what}: {_lib.ERRORS.get(code & 255, code)} (code {code})")
 
 
 #: When True, a forward launch's device error word is not read at once (a host
@@ -164,7 +164,7 @@ def check_errors(block: bool = True) -> None:
         code = int(host[0])
         if code:
             _PENDING.clear()
-            raise RuntimeError(f"{what}: {_lib.ERRORS.get(code, code)}")
+            raise RuntimeError(f"{what}: {_lib.ERRORS.get(code & 255, code)} (code {code})")
 
 
 def run_forward(plan, p, x, v, g, counter, g_a, gating, *, probabilities=False, track=False,

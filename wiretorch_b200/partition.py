@@ -103,30 +103,89 @@ class Partition:
         words_bytes = -(-(2 * B * self.words_src * 4) // 256) * 256
         amps_off = words_bytes + 256  # after the progress slots (8 x 8 bytes)
         total = amps_off + 2 * B * self.words_src * 32 * 4
+        self._allocs, self._opened = [], []
+        bases = self._shared(total)
+        self._base = self._allocs[0]
+        self.peer_words = bases
+        self.peer_progress = [b + words_bytes for b in bases]
+        self.peer_amps = [b + amps_off for b in bases]
+        self.words, self.progress = bases[self.rank], bases[self.rank] + words_bytes
+        self.epoch = 0
+        self._push = {}  # per local plan: the tables and areas of pushed events
+        dist.barrier(group=group)
+
+    def _shared(self, nbytes: int) -> list:
+        """A zeroed ``cudaMalloc`` of ``nbytes`` on every rank (collective), mapped into the
+        others with CUDA IPC: the base address of every rank's, as this rank sees it."""
+        import torch.distributed as dist
+        from cuda.bindings import runtime as rt
+
         torch.cuda.synchronize()
-        self._base = _cuda(rt.cudaMalloc(total))
-        _cuda(rt.cudaMemset(self._base, 0, total))
+        base = _cuda(rt.cudaMalloc(max(int(nbytes), 256)))
+        _cuda(rt.cudaMemset(base, 0, max(int(nbytes), 256)))
         _cuda(rt.cudaDeviceSynchronize())
-        handle = _cuda(rt.cudaIpcGetMemHandle(self._base))
+        self._allocs.append(base)
+        handle = _cuda(rt.cudaIpcGetMemHandle(base))
         handles = [None] * self.P
-        dist.all_gather_object(handles, bytes(handle.reserved), group=group)
-        self._opened = []
+        dist.all_gather_object(handles, bytes(handle.reserved), group=self.group)
         bases = []
         for r, hb in enumerate(handles):
             if r == self.rank:
-                bases.append(int(self._base))
+                bases.append(int(base))
                 continue
             h = rt.cudaIpcMemHandle_t()
             h.reserved = hb
             peer = _cuda(rt.cudaIpcOpenMemHandle(h, rt.cudaIpcMemLazyEnablePeerAccess))
             self._opened.append(peer)
             bases.append(int(peer))
-        self.peer_words = bases
-        self.peer_progress = [b + words_bytes for b in bases]
-        self.peer_amps = [b + amps_off for b in bases]
-        self.words, self.progress = bases[self.rank], bases[self.rank] + words_bytes
-        self.epoch = 0
-        dist.barrier(group=group)
+        return bases
+
+    def push_tables(self, plan) -> dict:
+        """What a rank that pushes its events needs (collective, once per local plan):
+        every rank's chunk range of every neuron and chunk descriptors (local copies), and
+        an inbound event area on every rank with a region per source rank (sized for each
+        source rank's neurons' chunks there, every trial) and inbound counts."""
+        import torch.distributed as dist
+
+        key = id(plan)
+        if key in self._push:
+            return self._push[key]
+        t = plan.tensors
+        dev = plan.device
+        N_src = plan.N_src
+        sc = t["src_chunk"][: N_src + 1].contiguous()
+        n_chunks = int(sc[-1])
+        cd = t["chunk_desc"][:n_chunks].contiguous()
+        P = self.P
+        sizes = [None] * P
+        dist.all_gather_object(sizes, n_chunks, group=self.group)
+        # every rank's tables, through the host (any backend)
+        scs = [None] * P
+        dist.all_gather_object(scs, sc.cpu(), group=self.group)
+        cds = [None] * P
+        dist.all_gather_object(cds, cd.cpu(), group=self.group)
+        src_chunk = [x.to(dev) for x in scs]
+        chunk_desc = [(x if x.numel() else torch.zeros(1, dtype=torch.int64)).to(dev) for x in cds]
+        # this rank's inbound area: a region per source rank q (its neurons' chunks here)
+        caps = [self.B * int(sc[n1] - sc[n0]) for n0, n1 in blocks(self.N, P)]
+        offs = [0]
+        for c in caps[:-1]:
+            offs.append(offs[-1] + c)
+        half = sum(caps)
+        counts_off = -(-(2 * half * 16) // 256) * 256
+        bases = self._shared(counts_off + 2 * 8 * 4)
+        layout = [None] * P  # every rank's regions and where its inbound counts sit
+        dist.all_gather_object(layout, (caps, offs, half, counts_off), group=self.group)
+        reserve = torch.zeros(2 * 8, dtype=torch.int32, device=dev)
+        tables = {"src_chunk": src_chunk, "chunk_desc": chunk_desc, "reserve": reserve,
+                  "push_ev": [bases[r] + layout[r][1][self.rank] * 16 for r in range(P)],
+                  "push_cap": [layout[r][0][self.rank] for r in range(P)],
+                  "push_half": [layout[r][2] for r in range(P)],
+                  "push_count": [bases[r] + layout[r][3] for r in range(P)],
+                  "pull_ev": bases[self.rank], "pull_off": offs, "pull_half": half,
+                  "pull_count": bases[self.rank] + counts_off}  # fmt: skip
+        self._push[key] = tables
+        return tables
 
     def fill(self, run, plan=None) -> None:
         """The partition's fields of a ``WtForward`` for the next call (a new epoch); the
@@ -141,6 +200,17 @@ class Partition:
             run.amps = self.peer_amps[self.rank]
             for r in range(self.P):
                 run.peer_amps[r] = self.peer_amps[r]
+        if plan is not None and PUSH and (not plan.gated or owner_gates(plan)):
+            tb = self.push_tables(plan)
+            for r in range(self.P):
+                run.push_src_chunk[r] = tb["src_chunk"][r].data_ptr()
+                run.push_chunk_desc[r] = tb["chunk_desc"][r].data_ptr()
+                run.push_ev[r], run.push_cap[r] = tb["push_ev"][r], tb["push_cap"][r]
+                run.push_half[r], run.push_count[r] = tb["push_half"][r], tb["push_count"][r]
+                run.pull_off[r] = tb["pull_off"][r]
+            tb["reserve"].zero_()  # every call starts with no reservation (even after a failed one)
+            run.push_reserve = tb["reserve"].data_ptr()
+            run.pull_ev, run.pull_half, run.pull_count = tb["pull_ev"], tb["pull_half"], tb["pull_count"]
 
     def close(self) -> None:
         from cuda.bindings import runtime as rt
@@ -148,9 +218,15 @@ class Partition:
         for peer in self._opened:
             _cuda(rt.cudaIpcCloseMemHandle(peer))
         self._opened = []
-        if self._base is not None:
-            _cuda(rt.cudaFree(self._base))
-            self._base = None
+        for base in self._allocs:
+            _cuda(rt.cudaFree(base))
+        self._allocs, self._base, self._push = [], None, {}
+
+
+#: Ranks push their events straight into every rank's inbound area (one grid barrier a
+#: step) where the network has no gating or its owners step the gates; False: the spike
+#: words are published and every rank walks them (two more grid barriers a step).
+PUSH = True
 
 
 def owner_gates(plan) -> bool:
