@@ -124,3 +124,26 @@ def test_owner_stepped_gating_gathered_from_the_owners():
     result = manager.dict()
     mp.start_processes(_gating_rank_main, args=(world, _free_port(), result), nprocs=world, start_method="spawn")
     assert dict(result) == {0: True, 1: True}
+
+
+def test_pushed_events_land_in_each_peers_own_layout():
+    """A rank writes its pushed events and their counts into every peer's inbound area at
+    that peer's offsets: with areas of different sizes (ranks with different chunk
+    counts), each region and each counts slot lies inside the peer's own area."""
+    from wiretorch_b200.partition import inbound_layout, push_pointers
+
+    B, P = 4, 3
+    chunks = [[10, 3, 7], [1, 50, 2], [4, 4, 100]]  # chunks[r][q]: source rank q's chunks on rank r
+    layouts = [inbound_layout(chunks[r], B) for r in range(P)]
+    sizes = [lay[3] + 2 * 8 * 4 for lay in layouts]
+    bases = [10**9 * (r + 1) for r in range(P)]  # disjoint address ranges
+    for q in range(P):
+        ptr = push_pointers(q, bases, layouts)
+        for r in range(P):
+            lo, hi = bases[r], bases[r] + sizes[r]
+            region_end = ptr["push_ev"][r] + (ptr["push_half"][r] + ptr["push_cap"][r]) * 16
+            assert lo <= ptr["push_ev"][r] and region_end <= bases[r] + layouts[r][3]  # both parities
+            assert ptr["push_cap"][r] == B * chunks[r][q]
+            assert lo <= ptr["push_count"][r] and ptr["push_count"][r] + 16 * 4 <= hi
+            assert ptr["push_count"][r] == bases[r] + layouts[r][3]
+        assert ptr["pull_count"] == bases[q] + layouts[q][3]

@@ -167,23 +167,13 @@ class Partition:
         src_chunk = [x.to(dev) for x in scs]
         chunk_desc = [(x if x.numel() else torch.zeros(1, dtype=torch.int64)).to(dev) for x in cds]
         # this rank's inbound area: a region per source rank q (its neurons' chunks here)
-        caps = [self.B * int(sc[n1] - sc[n0]) for n0, n1 in blocks(self.N, P)]
-        offs = [0]
-        for c in caps[:-1]:
-            offs.append(offs[-1] + c)
-        half = sum(caps)
-        counts_off = -(-(2 * half * 16) // 256) * 256
-        bases = self._shared(counts_off + 2 * 8 * 4)
+        mine = inbound_layout([int(sc[n1] - sc[n0]) for n0, n1 in blocks(self.N, P)], self.B)
+        bases = self._shared(mine[3] + 2 * 8 * 4)
         layout = [None] * P  # every rank's regions and where its inbound counts sit
-        dist.all_gather_object(layout, (caps, offs, half, counts_off), group=self.group)
+        dist.all_gather_object(layout, mine, group=self.group)
         reserve = torch.zeros(2 * 8, dtype=torch.int32, device=dev)
         tables = {"src_chunk": src_chunk, "chunk_desc": chunk_desc, "reserve": reserve,
-                  "push_ev": [bases[r] + layout[r][1][self.rank] * 16 for r in range(P)],
-                  "push_cap": [layout[r][0][self.rank] for r in range(P)],
-                  "push_half": [layout[r][2] for r in range(P)],
-                  "push_count": [bases[r] + layout[r][3] for r in range(P)],
-                  "pull_ev": bases[self.rank], "pull_off": offs, "pull_half": half,
-                  "pull_count": bases[self.rank] + counts_off}  # fmt: skip
+                  **push_pointers(self.rank, bases, layout)}  # fmt: skip
         self._push[key] = tables
         return tables
 
@@ -221,6 +211,35 @@ class Partition:
         for base in self._allocs:
             _cuda(rt.cudaFree(base))
         self._allocs, self._base, self._push = [], None, {}
+
+
+def inbound_layout(chunks_of_ranks: list, B: int) -> tuple:
+    """A rank's inbound event area: per source rank q the room for its neurons' chunks
+    here (``chunks_of_ranks[q]``) in every trial, the regions' starts, one step parity's
+    events, and the byte offset of the inbound counts ([2][8] uint32) after both
+    parities' events."""
+    caps = [B * int(c) for c in chunks_of_ranks]
+    offs = [0]
+    for c in caps[:-1]:
+        offs.append(offs[-1] + c)
+    half = sum(caps)
+    counts_off = -(-(2 * half * 16) // 256) * 256
+    return caps, offs, half, counts_off
+
+
+def push_pointers(rank: int, bases: list, layouts: list) -> dict:
+    """Where rank ``rank`` writes and reads pushed events, from every rank's area base (as
+    this rank sees it) and every rank's ``inbound_layout``: its region of each rank r's
+    area (events), that region's room, r's parity stride, and r's inbound counts — each
+    at r's own offsets — and its own area."""
+    caps, offs, half, counts_off = layouts[rank]
+    P = len(bases)
+    return {"push_ev": [bases[r] + layouts[r][1][rank] * 16 for r in range(P)],
+            "push_cap": [layouts[r][0][rank] for r in range(P)],
+            "push_half": [layouts[r][2] for r in range(P)],
+            "push_count": [bases[r] + layouts[r][3] for r in range(P)],
+            "pull_ev": bases[rank], "pull_off": offs, "pull_half": half,
+            "pull_count": bases[rank] + counts_off}  # fmt: skip
 
 
 #: Ranks push their events straight into every rank's inbound area (one grid barrier a
