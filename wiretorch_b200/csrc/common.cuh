@@ -77,6 +77,13 @@ struct GridBarrier {
     // pushes its events: this rank's event counts per step parity and destination rank,
     // [2][8]), the last block first writes parity `par`'s counts into every rank's inbound
     // counts (`push_count[r][par * 8 + rank]`) and clears them for the step after next.
+    //
+    // Ordering: the blocks' stores to the ranks (spike words, events) are ordered before
+    // their arrival by the block barrier and a fence at GPU scope; the last block's one
+    // fence at system scope then orders all of them (causality order is transitive across
+    // the GPU-scope synchronisation with the other blocks) and its own counts before the
+    // relaxed system-scope progress stores: one system fence per step on the path (each
+    // costs microseconds), not one per thread, per block or per rank.
     __device__ bool sync_progress(int32_t *err, unsigned long long *const *peer_progress, int rank,
                                   const unsigned long long *slots, int n_ranks, unsigned long long mine,
                                   uint32_t *reserve = nullptr, uint32_t *const *push_count = nullptr, int par = 0) {
@@ -84,7 +91,7 @@ struct GridBarrier {
         __syncthreads();
         if (threadIdx.x == 0) {
             const unsigned g = local;
-            __threadfence_system();  // this block's spike words, before the ranks learn of them
+            __threadfence();  // this block's stores (here and to the ranks), before its arrival
             const unsigned arrived = atomicAdd(count, 1u);
             if (arrived == nblocks - 1) {
                 atomicExch(count, 0u);
@@ -95,9 +102,9 @@ struct GridBarrier {
                         push_count[r][par * 8 + rank] = v;
                     }
                 }
-                __threadfence_system();
+                __threadfence_system();  // every block's stores to the ranks and the counts, first
                 for (int r = 0; r < n_ranks; r++)
-                    asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(peer_progress[r] + rank), "l"(mine)
+                    asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(peer_progress[r] + rank), "l"(mine)
                                  : "memory");
                 for (int r = 0; r < n_ranks; r++) {
                     unsigned long long spins = 0, seen = 0;

@@ -738,8 +738,7 @@ __global__ void __launch_bounds__(warps_of<S, FEAT>() * 32, 1) forward_kernel(co
         }
     };
     load_x(run.t0 + 1);
-    if (PART) {
-        __threadfence_system();  // this thread's stores to the ranks (words, events), first
+    if (PART) {  // the barrier orders every thread's stores to the ranks before the progress
         if (!exchange(0)) return;
     } else if (!bar.sync(ws.err)) {
         return;
@@ -1123,7 +1122,6 @@ __global__ void __launch_bounds__(warps_of<S, FEAT>() * 32, 1) forward_kernel(co
         if (scatter_late) scatter();
         stamp(t, 4);
         if (PART && emit_next) {  // the step's barrier is the exchange's
-            __threadfence_system();  // this thread's stores to the ranks (words, events), first
             stamp(t, 5);
             if (!exchange(t + 1)) return;
         } else {
