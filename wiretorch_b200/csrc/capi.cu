@@ -104,6 +104,7 @@ int check_forward(const WtNet *net, const WtForward *run, const WtWorkspace *ws)
     if (!run || !ws) return fail(WT_ERR_ARGS, "run or workspace is null%s");
     if (run->T < 0 || run->t0 < 0 || run->t0 + run->T > run->T_total)
         return fail(WT_ERR_ARGS, "steps out of range%s");
+    if (run->T > (1 << 24)) return fail(WT_ERR_UNSUPPORTED, "at most 2^24 steps a call%s");  // the barrier's count
     if (!run->v || !run->g || !run->spikes || (net->n_in && !run->x))
         return fail(WT_ERR_ARGS, "missing state or output%s");
     const int f = run->flags;
@@ -271,6 +272,7 @@ int wt_lowrank_forward(const WtLowRankNet *net, const WtLowRankRun *run, void *s
         return fail(WT_ERR_ARGS, "missing network tables%s");
     if (((uintptr_t)net->U & 15) || ((uintptr_t)net->V & 15)) return fail(WT_ERR_ARGS, "U and V must be 16-byte aligned%s");
     if (run->T < 0 || run->t0 < 0 || run->t0 + run->T > run->T_total) return fail(WT_ERR_ARGS, "steps out of range%s");
+    if (run->T > (1 << 24)) return fail(WT_ERR_UNSUPPORTED, "at most 2^24 steps a call%s");  // the barrier's count
     if (!run->v || !run->g || !run->spikes || !run->P || !run->barrier || !run->err || (run->T && !run->x) ||
         (net->n_ref && !run->counter))
         return fail(WT_ERR_ARGS, "missing run buffers%s");

@@ -547,44 +547,54 @@ __global__ void __launch_bounds__(warps_of<S, FEAT>() * 32, 1) forward_kernel(co
         n_edges_all = (long long)(d & ((1ull << 56) - 1)) + (long long)(d >> 56);
     }
     auto push = [&](int step, int b, int jg, bool on, float amp) {
-        if (!__any_sync(kFull, on)) return;
-        for (int r = 0; r < run.n_ranks; r++) {
+        unsigned firing = __ballot_sync(kFull, on);
+        const int P = run.n_ranks, par = step & 1;
+        // one firing source at a time, its ranks across the lanes: lane r < P finds the
+        // source's chunks on rank r and reserves room for them there, then the lanes write
+        // all of the source's events on all ranks at once (three dependent round trips a
+        // source, whatever the number of ranks)
+        while (firing) {
+            const int l = __ffs(firing) - 1;
+            firing &= firing - 1;
+            const int j = __shfl_sync(kFull, jg, l);
+            const int bl = __shfl_sync(kFull, b, l);
+            const int a = __float_as_int(__shfl_sync(kFull, amp, l));
+            if (j < 0 || j >= Nsrc) {  // range checks of the pushed events: a record, no access
+                if (lane == 0) set_error(ws.err, WT_ERR_RANGE | (1 << 8));
+                continue;
+            }
             int c0 = 0, cnt = 0;
-            if (on && (jg < 0 || jg >= Nsrc)) {  // range checks of the pushed events: a record, no access
-                set_error(ws.err, WT_ERR_RANGE | (1 << 8));
-            } else if (on) {
-                const int32_t *sc = run.push_src_chunk[r];
-                c0 = sc[jg];
-                cnt = sc[jg + 1] - c0;
+            if (lane < P) {
+                const int32_t *sc = run.push_src_chunk[lane];
+                c0 = sc[j];
+                cnt = sc[j + 1] - c0;
                 if (cnt < 0 || c0 < 0 || c0 + cnt > sc[Nsrc]) {
                     set_error(ws.err, WT_ERR_RANGE | (2 << 8));
                     cnt = 0;
                 }
             }
+            unsigned base = 0;
+            if (cnt > 0) base = atomicAdd(run.push_reserve + par * 8 + lane, (unsigned)cnt);
             const int incl = warp_inclusive_sum(cnt, lane);
             const int total = __shfl_sync(kFull, incl, 31);
-            if (total == 0) continue;
-            unsigned base = 0;
-            if (lane == 31) base = atomicAdd(run.push_reserve + (step & 1) * 8 + r, (unsigned)total);
-            base = __shfl_sync(kFull, base, 31);
-            int4 *evs = reinterpret_cast<int4 *>(run.push_ev[r] + (size_t)(step & 1) * run.push_half[r]);
-            const long long *desc = run.push_chunk_desc[r];
-            unsigned m = __ballot_sync(kFull, cnt > 0);
-            while (m) {
-                const int l = __ffs(m) - 1;
-                m &= m - 1;
-                const int lc0 = __shfl_sync(kFull, c0, l), lcnt = __shfl_sync(kFull, cnt, l);
-                const long long off = (long long)base + __shfl_sync(kFull, incl, l) - lcnt;
-                const int a = __float_as_int(__shfl_sync(kFull, amp, l));
-                for (int q = lane; q < lcnt; q += 32) {
-                    if (off + q >= run.push_cap[r]) {
-                        set_error(ws.err, WT_ERR_EVENTS);
-                        break;
-                    }
-                    const unsigned long long d = (unsigned long long)desc[lc0 + q];
-                    evs[off + q] = make_int4((int)(unsigned)d, (int)(unsigned)((d >> 32) & 0xffffffu),
-                                             (int)(((unsigned)b << 8) | (unsigned)(d >> 56)), a);
+            for (int i0 = 0; i0 < total; i0 += 32) {
+                const int i = i0 + lane;  // event i of the source: rank r, its chunk k there
+                int r = 0;
+#pragma unroll
+                for (int q = 0; q < 8; q++) r += q < P && __shfl_sync(kFull, incl, q) <= i;
+                const int rr = min(r, 7);
+                const int k = i - (__shfl_sync(kFull, incl, rr) - __shfl_sync(kFull, cnt, rr));
+                const int cr = __shfl_sync(kFull, c0, rr);
+                const long long off = (long long)__shfl_sync(kFull, base, rr) + k;
+                if (i >= total) continue;
+                if (off >= run.push_cap[rr]) {
+                    set_error(ws.err, WT_ERR_EVENTS);
+                    continue;
                 }
+                const unsigned long long d = (unsigned long long)run.push_chunk_desc[rr][cr + k];
+                int4 *evs = reinterpret_cast<int4 *>(run.push_ev[rr] + (size_t)par * run.push_half[rr]);
+                evs[off] = make_int4((int)(unsigned)d, (int)(unsigned)((d >> 32) & 0xffffffu),
+                                     (int)(((unsigned)bl << 8) | (unsigned)(d >> 56)), a);
             }
         }
     };
