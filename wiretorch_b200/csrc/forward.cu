@@ -816,13 +816,20 @@ __global__ void __launch_bounds__(warps_of<S, FEAT>() * 32, 1) forward_kernel(co
             // region of each rank in its inbound area, counts published with the progress
             // (a count is never above its region's room; clamped all the same, so that no
             // read leaves the area)
-            auto pulled = [&](int r) -> long long {
-                const long long room = (r + 1 < run.n_ranks ? run.pull_off[r + 1] : run.pull_half) - run.pull_off[r];
-                return min((long long)__ldcg(run.pull_count + (t & 1) * 8 + r), room);
-            };
+            // (each rank's count read once, into registers: the lanes then find their
+            // event's region without a load per rank)
+            int pr[8];
             long long count = n_local;
-            if (PUSH)
-                for (int r = 0; r < run.n_ranks; r++) count += pulled(r);
+#pragma unroll
+            for (int r = 0; r < 8; r++) {
+                pr[r] = 0;
+                if (PUSH && r < run.n_ranks) {
+                    const long long room =
+                        (r + 1 < run.n_ranks ? run.pull_off[r + 1] : run.pull_half) - run.pull_off[r];
+                    pr[r] = (int)min((long long)__ldcg(run.pull_count + (t & 1) * 8 + r), room);
+                    count += pr[r];
+                }
+            }
             const WtEvent *pull = PUSH ? run.pull_ev + (size_t)(t & 1) * run.pull_half : nullptr;
             unsigned long long *X = ws.X + (size_t)(t & 1) * C * BNp;
             for (long long base = gwarp; base < count; base += nwarps * 32) {
@@ -832,15 +839,13 @@ __global__ void __launch_bounds__(warps_of<S, FEAT>() * 32, 1) forward_kernel(co
                 if (mine < n_local) {
                     raw = __ldcg(reinterpret_cast<const int4 *>(evs + mine));
                 } else if (mine < count) {
-                    long long m = mine - n_local;
-                    for (int r = 0; r < run.n_ranks; r++) {
-                        const long long cr = pulled(r);
-                        if (m < cr) {
-                            raw = __ldcg(reinterpret_cast<const int4 *>(pull + run.pull_off[r] + m));
-                            break;
-                        }
-                        m -= cr;
+                    long long m = mine - n_local, off = -1;
+#pragma unroll
+                    for (int r = 0; r < 8; r++) {
+                        if (off < 0 && m < pr[r]) off = run.pull_off[r] + m;
+                        if (off < 0) m -= pr[r];
                     }
+                    if (off >= 0) raw = __ldcg(reinterpret_cast<const int4 *>(pull + off));
                 }
                 const int ne = (int)min(32LL, (count - base + nwarps - 1) / nwarps);
                 unsigned long long cw[4], cw_n[4];
