@@ -309,6 +309,20 @@ class Prefetcher:
             self.pending = self._fetch()
 
 
+PACKED_NOTE = "spike input held on the host as bits (wiretorch_b200.chunks.PackedSpikes), unpacked on the device"
+
+
+def packed_input(x):
+    """One engine call's spike input as pinned host bits (the dataset format of
+    ``wiretorch_b200.chunks``; packed once, outside the timed region) and the conversion
+    the prefetcher applies on the device: ``wt_unpack_spikes`` into float32."""
+    from wiretorch_b200.chunks import PackedSpikes, pack_spikes
+
+    n = x.shape[-1]
+    bits = pack_spikes(x.detach().cpu(), check=False).bits.pin_memory()
+    return [bits], lambda b: PackedSpikes(b, n, torch.float32).unpack()
+
+
 def x_device(cfg):
     return cfg.drive.scale.device
 
@@ -610,9 +624,9 @@ def main_partition(args, rank, world, local):
     # ---- end to end: each call's input from pinned host memory, the block's state read back ----
     e2e = None
     if not args.no_e2e:
-        x_host = [(x.cpu() != 0).to(torch.uint8).pin_memory()]
+        x_host, unpack = packed_input(x)
         out_host = torch.empty((cfg.B, n_b), pin_memory=True)
-        fetch = Prefetcher(x_host, device, lambda t: t.float())
+        fetch = Prefetcher(x_host, device, unpack)
         fetch.start()
         out_host.copy_(step(fetch).v, non_blocking=True)
         torch.cuda.synchronize()
@@ -627,7 +641,7 @@ def main_partition(args, rank, world, local):
         e2e = {"value": neuron_steps / e2e_el, "unit": "neuron-steps/s",
                "h2d_bytes_per_step": calls * x_host[0].numel(), "d2h_bytes_per_step": out_host.numel() * 4,
                "ms_per_step": e2e_el / K * 1000.0,
-               "note": "every rank copies the replicated input; bytes are per rank"}  # fmt: skip
+               "note": "every rank copies the replicated input; bytes are per rank", "input": PACKED_NOTE}  # fmt: skip
     engine.check_errors()
     if rank == 0:
         print(json.dumps({
@@ -760,12 +774,12 @@ def main_single(args, rank, world, local):
     # ---- end to end from host buffers ----
     e2e = None
     if not args.no_e2e:
-        x_host = [(x.cpu() != 0).to(torch.uint8).pin_memory()]
+        x_host, unpack = packed_input(x)
         calls = cfg.T // x.shape[1] if cfg.name in ("c3", "c4", "c5") else 1
         if train:
-            e2e = e2e_training(cfg, step, log_sf, x_host[0], device, world, K, neuron_steps)
+            e2e = e2e_training(cfg, step, log_sf, x_host[0], unpack, device, world, K, neuron_steps)
         else:
-            fetch = Prefetcher(x_host, device, lambda t: t.float())
+            fetch = Prefetcher(x_host, device, unpack)
             out_host = torch.empty((cfg.B, cfg.N), pin_memory=True)
             fetch.start()
             out_host.copy_(step(x, fetch=fetch), non_blocking=True)
@@ -780,7 +794,7 @@ def main_single(args, rank, world, local):
             e2e_el = max_over_ranks(s2.elapsed_time(e2) / 1000.0, world)
             e2e = {"value": neuron_steps / e2e_el, "unit": "neuron-steps/s",
                    "h2d_bytes_per_step": calls * x_host[0].numel(), "d2h_bytes_per_step": out_host.numel() * 4,
-                   "ms_per_step": e2e_el / K * 1000.0}  # fmt: skip
+                   "ms_per_step": e2e_el / K * 1000.0, "input": PACKED_NOTE}  # fmt: skip
 
     engine.check_errors()  # every deferred device error check of the runs above
     cpu = None
@@ -804,15 +818,15 @@ def main_single(args, rank, world, local):
         print(json.dumps(line))
 
 
-def e2e_training(cfg, step, log_sf, x_host, device, world, K, neuron_steps):
-    """The c2 training step fed from pinned host memory (spike input as bytes, target
-    rates), the loss and the learnt scales read back every step; each step's input
-    copied on a second stream while the previous step computes."""
+def e2e_training(cfg, step, log_sf, x_host, unpack, device, world, K, neuron_steps):
+    """The c2 training step fed from pinned host memory (spike input as bits, unpacked on
+    the device; target rates), the loss and the learnt scales read back every step; each
+    step's input copied on a second stream while the previous step computes."""
     tgt_host = cfg.extra["target_rates"].cpu().pin_memory()
     out_host = torch.empty(1 + log_sf.numel(), pin_memory=True)
     h2d = x_host.numel() + tgt_host.numel() * 4
     d2h = out_host.numel() * 4
-    fetch_x = Prefetcher([x_host], device, lambda t: t.float())
+    fetch_x = Prefetcher([x_host], device, unpack)
     fetch_t = Prefetcher([tgt_host], device, lambda t: t * (DT / 1000.0))
 
     def e2e_step():
@@ -835,7 +849,7 @@ def e2e_training(cfg, step, log_sf, x_host, device, world, K, neuron_steps):
     torch.cuda.synchronize()
     e2e_el = max_over_ranks(s2.elapsed_time(e2) / 1000.0, world)
     return {"value": neuron_steps / e2e_el, "unit": "neuron-steps/s", "h2d_bytes_per_step": h2d,
-            "d2h_bytes_per_step": d2h, "ms_per_step": e2e_el / K * 1000.0}
+            "d2h_bytes_per_step": d2h, "ms_per_step": e2e_el / K * 1000.0, "input": PACKED_NOTE}
 
 
 if __name__ == "__main__":

@@ -479,6 +479,32 @@ typedef struct {
  * conductance/engine.py:306-355 in the reference: a dense W assembled, then gathered). */
 int wt_lowrank_forward(const WtLowRankNet *net, const WtLowRankRun *run, void *stream);
 
+/* Spikes as bits, the form in which the runners move spikes between host and device: a
+ * spike tensor of `rows` rows (the product of all but its last dimension) of n spikes,
+ * each row packed into ceil(n / 8) bytes, spike i of a row in bit i % 8 (least
+ * significant first) of byte i / 8 (numpy's packbits(x, axis=-1, bitorder="little")).
+ * An eighth of the bytes of the bool spike tensors that the reference's data path copies
+ * whole (snn_runners/chunks.py:19-25 `to_device`, used by `Prefetcher` at
+ * chunks.py:28-70; snn_runners/inference_runner.py:111-150 `_Stager`), a thirty-second of
+ * a float tensor's. */
+#define WT_SPIKES_F32 0 /* float, 0 or 1 */
+#define WT_SPIKES_U8 1  /* bool or uint8, 0 or 1 */
+typedef struct {
+    int64_t rows;
+    int32_t n;
+    int32_t kind;           /* WT_SPIKES_F32 or WT_SPIKES_U8 */
+    uint8_t *bits;          /* (rows, ceil(n / 8)) */
+    void *spikes;           /* (rows, n) of `kind` */
+    int32_t *err;           /* wt_pack_spikes: device error word, or null */
+} WtSpikeBits;
+
+/* bits -> spikes (0 or 1 of `kind`), on the device. */
+int wt_unpack_spikes(const WtSpikeBits *a, void *stream);
+
+/* spikes -> bits, on the device: a spike is any value other than 0; a value other than
+ * 0 or 1 (a count the bits cannot hold) records WT_ERR_ARGS in `err`. */
+int wt_pack_spikes(const WtSpikeBits *a, void *stream);
+
 /* Reading back: a static description of the last host-side error on this thread. */
 const char *wt_last_error(void);
 

@@ -37,7 +37,7 @@ def test_abi_version(lib):
 def test_structures_match_the_header_sizes():
     """The ctypes mirrors have the members the header declares, in order."""
     text = HEADER.read_text()
-    from wiretorch_b200 import autograd, filtering, lowrank
+    from wiretorch_b200 import autograd, chunks, filtering, lowrank
 
     for struct, cls in (("WtNet", _lib.WtNet), ("WtForward", _lib.WtForward),
                         ("WtWorkspace", _lib.WtWorkspace),
@@ -48,7 +48,8 @@ def test_structures_match_the_header_sizes():
                         ("WtVanRossumGradArgs", filtering._VanRossumGradArgs),
                         ("WtLowRankProduct", lowrank._ProductArgs),
                         ("WtLowRankNet", lowrank._LrNet), ("WtLowRankRun", lowrank._LrRun),
-                        ("WtRecurrentCarry", autograd._CarryArgs)):  # fmt: skip
+                        ("WtRecurrentCarry", autograd._CarryArgs),
+                        ("WtSpikeBits", chunks._SpikeBits)):  # fmt: skip
         body = re.search(r"typedef struct \{((?:(?!typedef struct).)*?)\}\s*" + struct + ";", text,
                          re.S).group(1)
         body = re.sub(r"/\*.*?\*/", "", body, flags=re.S)

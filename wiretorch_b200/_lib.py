@@ -103,7 +103,8 @@ def lib() -> C.CDLL:
         for name in ("wt_forward", "wt_fold_weights", "wt_workspace_bytes", "wt_abi_version",
                      "wt_backward", "wt_edge_grads", "wt_filter_forward", "wt_filter_backward",
                      "wt_forward_noalloc", "wt_noalloc_error", "wt_van_rossum_forward",
-                     "wt_van_rossum_backward", "wt_lowrank_product", "wt_lowrank_forward", "wt_recurrent_carry"):
+                     "wt_van_rossum_backward", "wt_lowrank_product", "wt_lowrank_forward", "wt_recurrent_carry",
+                     "wt_unpack_spikes", "wt_pack_spikes"):
             getattr(_lib, name).restype = C.c_int
     return _lib
 

@@ -20,6 +20,8 @@ cudaError_t launch_filter(const WtFilterArgs &f, cudaStream_t st);
 cudaError_t launch_filter_grad(const WtFilterGradArgs &f, cudaStream_t st);
 cudaError_t launch_van_rossum(const WtVanRossumArgs &a, cudaStream_t st);
 cudaError_t launch_van_rossum_grad(const WtVanRossumGradArgs &a, cudaStream_t st);
+cudaError_t launch_unpack_spikes(const WtSpikeBits &a, cudaStream_t st);
+cudaError_t launch_pack_spikes(const WtSpikeBits &a, cudaStream_t st);
 cudaError_t launch_fold(const WtNet &net, const float *w_raw, const int32_t *chunk_path, const float *scale,
                         const float *jf, const float *fx_scale, uint64_t *out, cudaStream_t st);
 }
@@ -226,6 +228,25 @@ int64_t wt_edge_grads_scratch_words(const WtNet *net, int32_t T) {
 int32_t wt_edge_grads_slice_trials(const WtNet *net, int32_t T) {
     if (check_net(net) || T < 0) return 0;
     return wt::edge_grads_slice_trials(*net, T);
+}
+
+static int check_spike_bits(const WtSpikeBits *a) {
+    if (!a || a->rows < 0 || a->n < 0 || (a->kind != WT_SPIKES_F32 && a->kind != WT_SPIKES_U8))
+        return fail(WT_ERR_ARGS, "bad spike-bit arguments%s");
+    if (a->rows && a->n && (!a->bits || !a->spikes)) return fail(WT_ERR_ARGS, "missing spike or bit buffer%s");
+    return WT_OK;
+}
+
+int wt_unpack_spikes(const WtSpikeBits *a, void *stream) {
+    const int rc = check_spike_bits(a);
+    if (rc) return rc;
+    return launch_status(wt::launch_unpack_spikes(*a, (cudaStream_t)stream), "unpack spikes");
+}
+
+int wt_pack_spikes(const WtSpikeBits *a, void *stream) {
+    const int rc = check_spike_bits(a);
+    if (rc) return rc;
+    return launch_status(wt::launch_pack_spikes(*a, (cudaStream_t)stream), "pack spikes");
 }
 
 int wt_filter_forward(const WtFilterArgs *f, void *stream) {
