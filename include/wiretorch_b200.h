@@ -57,6 +57,8 @@ enum {
     WT_F_SAVE_INPUT = 1 << 8, /* save each step's synaptic input X (learnt decay/jump) */
     WT_F_PARTITION = 1 << 9,  /* one rank of a neuron-partitioned run (WtForward.words...) */
     WT_F_STREAM = 1 << 10,    /* keep the state in HBM even where it fits on chip (tests) */
+    WT_F_CURRENT = 1 << 11,   /* current-based neurons (see WtNet): the step's own input enters
+                               * the currents before the membrane update */
 };
 
 /* The network as the kernels see it (built once per network and per call from the
@@ -66,6 +68,10 @@ typedef struct {
     int32_t S, C;        /* synapse channels carried per neuron, input channels */
     /* per neuron (N) */
     const float *theta, *U_reset, *E_L, *C_m, *beta;
+    /* (WT_F_CURRENT, network_simulators/current/dynamics.py:116-205: E_L holds U_rest,
+     * C_m the resistance R, E_syn the synapse types' signs, adapt and adapt_decay the
+     * adaptation current's rise and decay; each channel a single exponential, decay_d
+     * and jump_d 1) */
     const int32_t *n_ref;                       /* WT_F_REFRACTORY */
     const float *adapt, *adapt_decay, *E_adapt; /* WT_F_ADAPT */
     /* per channel (S): decays and jumps of the rise (r) and decay (d) components */
@@ -446,7 +452,11 @@ int wt_lowrank_product(const WtLowRankProduct *a, void *stream);
  * synapse type). */
 typedef struct {
     int32_t B, N, S, KP;
-    const float *theta, *U_reset, *E_L, *C_m, *beta; /* (N) */
+    const float *theta, *U_reset, *E_L, *C_m, *beta;
+    /* (WT_F_CURRENT, network_simulators/current/dynamics.py:116-205: E_L holds U_rest,
+     * C_m the resistance R, E_syn the synapse types' signs, adapt and adapt_decay the
+     * adaptation current's rise and decay; each channel a single exponential, decay_d
+     * and jump_d 1) */ /* (N) */
     const int32_t *n_ref;                            /* (N) or NULL */
     float decay_r[WT_MAX_CHANNELS], decay_d[WT_MAX_CHANNELS];
     float jump_r[WT_MAX_CHANNELS], jump_d[WT_MAX_CHANNELS];

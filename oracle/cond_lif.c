@@ -55,6 +55,11 @@ typedef struct {
     float dt, surr_scale;
     int sample; /* escape noise: spike where noise < sigmoid(k (v - theta)) */
     int R;      /* columns of the gating state */
+    /* 1: current-based neurons (network_simulators/current/dynamics.py:116-205): E_L
+     * holds U_rest, C_m the resistance R, E_syn the types' signs; decay and jump (2, S)
+     * with no rise component. The step's input enters the currents before the membrane
+     * update, which uses them. */
+    int current;
 } WtoNet;
 
 typedef struct {
@@ -168,6 +173,26 @@ static void membrane_of(const WtoNet *net, const float *v, const float *g, int32
     if (g_a) g_a[n] = g_a[n] * net->adapt_decay[n] + net->adapt[n] * s[n];
 }
 
+/* The current-based membrane of neuron n (current/dynamics.py:116-125, 180-183), with
+ * the currents after this step's input: the adaptation current rises by the spike, then
+ * v' = (beta v + (1 - beta)(U_rest + R (sum_j sign_j I_j - I_a)))(1 - r) + U_reset r. */
+static void membrane_current(const WtoNet *net, const float *v, const float *g, int32_t *counter, float *g_a,
+                             const float *s, const float *held, float *v_next, int n) {
+    const int S = net->S;
+    const float *gn = g + (size_t)n * 2 * S;
+    if (g_a) g_a[n] = g_a[n] * net->adapt_decay[n] + net->adapt[n] * s[n];
+    float Isyn = 0.0f;
+    for (int j = 0; j < S; j++) Isyn = Isyn + gn[S + j] * net->E_syn[j];
+    if (g_a) Isyn = Isyn - g_a[n];
+    const float b = net->beta[n];
+    const float r = s[n] > held[n] ? s[n] : held[n];
+    v_next[n] = (b * v[n] + (1.0f - b) * (net->E_L[n] + net->C_m[n] * Isyn)) * (1.0f - r) + net->U_reset[n] * r;
+    if (net->n_ref) {
+        int32_t c = counter[n] - 1;
+        counter[n] = s[n] > 0.0f ? net->n_ref[n] : (c > 0 ? c : 0);
+    }
+}
+
 /* Pathway k's activation a_k = (pre_k * f_k) @ W_k of one trial, event-driven over the
  * rows that carry input, each target's sum in double. */
 static void activation_of(const WtoNet *net, int k, const float *s, const float *xt, float *gating, float *pre,
@@ -232,10 +257,12 @@ int wto_simulate(const WtoNet *net, WtoState *st, const float *x, int T, WtoOut 
                 for (int t = 0; t < T; t++) {
                     const float *xt = x + ((size_t)b * T + t) * n_in;
                     for (int n = 0; n < N; n++) spike_of(net, v, counter, noise, b, T, t, n, sb, hb, out->prob);
-                    for (int n = 0; n < N; n++) membrane_of(net, v, g, counter, g_a, sb, hb, vn, n);
+                    if (!net->current)
+                        for (int n = 0; n < N; n++) membrane_of(net, v, g, counter, g_a, sb, hb, vn, n);
                     for (int k = 0; k < K; k++) activation_of(net, k, sb, xt, gating, pr, fc, ab + (size_t)k * N);
                     for (int n = 0; n < N; n++) {
                         conductances_of(net, g, ab, n);
+                        if (net->current) membrane_current(net, v, g, counter, g_a, sb, hb, vn, n);
                         v[n] = vn[n];
                         size_t o = ((size_t)b * T + t) * N + n;
                         out->spikes[o] = sb[n] > 0.0f;
@@ -270,6 +297,7 @@ int wto_simulate(const WtoNet *net, WtoState *st, const float *x, int T, WtoOut 
 #pragma omp parallel for schedule(static)
         for (long long i = 0; i < (long long)BN; i++) {
             const int b = (int)(i / N), n = (int)(i % N);
+            if (net->current) continue;  /* after the currents take the step's input */
             membrane_of(net, st->v + (size_t)b * N, st->g + (size_t)b * N * 2 * S,
                         st->counter ? st->counter + (size_t)b * N : NULL, st->g_a ? st->g_a + (size_t)b * N : NULL,
                         s + (size_t)b * N, held + (size_t)b * N, v_next + (size_t)b * N, n);
@@ -286,6 +314,11 @@ int wto_simulate(const WtoNet *net, WtoState *st, const float *x, int T, WtoOut 
         for (long long i = 0; i < (long long)BN; i++) {
             const int b = (int)(i / N), n = (int)(i % N);
             conductances_of(net, st->g + (size_t)b * N * 2 * S, acc + (size_t)b * K * N, n);
+            if (net->current)
+                membrane_current(net, st->v + (size_t)b * N, st->g + (size_t)b * N * 2 * S,
+                                 st->counter ? st->counter + (size_t)b * N : NULL,
+                                 st->g_a ? st->g_a + (size_t)b * N : NULL, s + (size_t)b * N, held + (size_t)b * N,
+                                 v_next + (size_t)b * N, n);
             st->v[i] = v_next[i];
             size_t o = ((size_t)b * T + t) * N + n;
             out->spikes[o] = s[i] > 0.0f;
@@ -296,4 +329,4 @@ int wto_simulate(const WtoNet *net, WtoState *st, const float *x, int T, WtoOut 
     return 0;
 }
 
-int wto_version(void) { return 1; }
+int wto_version(void) { return 2; }

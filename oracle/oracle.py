@@ -3,7 +3,8 @@
 Only ``tests/``, ``__graft_entry__.smoke()`` and ``bench.py``'s CPU-baseline arm import
 this module, and only as the checker (or the timed CPU baseline). It drives
 ``cond_lif.c``, the C restatement of wiretorch's
-``conductance/dynamics.py:146-237`` time loop, from a ``Drive`` and ``Physiology`` as
+``conductance/dynamics.py:146-237`` time loop (and of the current-based
+``current/dynamics.py:116-205`` one), from a ``Drive`` and ``Physiology`` as
 the reference's networks hand them to their engine (``network.py:889-909``): dense
 ``(n_rows, N)`` weights (or ``SparseRows``) are turned into CSR here with numpy,
 independently of the engine's own conversion.
@@ -45,7 +46,7 @@ class _Net(C.Structure):
         ("n_ref", _i32), ("adapt", _f), ("adapt_decay", _f), ("E_adapt", _f),
         ("E_syn", _f), ("g_clip", _f), ("decay", _f), ("jump", _f),
         ("mg_c", _f), ("mg_a", _f), ("dt", C.c_float), ("surr_scale", C.c_float),
-        ("sample", C.c_int), ("R", C.c_int),
+        ("sample", C.c_int), ("R", C.c_int), ("current", C.c_int),
     ]  # fmt: skip
 
 
@@ -100,10 +101,33 @@ def csr_of(W) -> tuple[np.ndarray, np.ndarray, np.ndarray]:
     return np.cumsum(row_ptr), cols.astype(np.int32), W[rows, cols].astype(np.float32)
 
 
+class _CurrentAsFields:
+    """A current-based physiology (``current/dynamics.py:56-85``) in the fields the C
+    structure holds: U_rest as E_L, R as C_m, the types' signs as E_syn, each type's
+    current a decay component with a unit jump and no rise."""
+
+    def __init__(self, p):
+        sign = _np(p.sign, np.float32)
+        S = sign.shape[0]
+        self.theta, self.U_reset, self.beta = p.theta, p.U_reset, p.beta
+        self.E_L, self.C_m, self.E_syn = p.U_rest, p.R, sign
+        self.g_clip = np.full(S, np.inf, np.float32)
+        self.decay = np.stack([np.zeros(S, np.float32), _np(p.decay, np.float32)])
+        self.jump = np.stack([np.zeros(S, np.float32), np.ones(S, np.float32)])
+        self.adapt, self.adapt_decay, self.E_adapt = p.adapt, p.adapt_decay, None
+        self.mg_c = self.mg_a = None
+        self.n_ref, self.dt, self.surr_scale, self.spike_mode = p.n_ref, np.float32(1.0), p.surr_scale, p.spike_mode
+
+
 class Network:
-    """A ``Drive`` + ``Physiology`` held as the oracle's C structures."""
+    """A ``Drive`` + ``Physiology`` held as the oracle's C structures. A current-based
+    physiology (one with ``sign`` and ``U_rest``) runs the current-based step; its state
+    is then the currents ``(B, N, S)`` in place of the conductances."""
 
     def __init__(self, drive, p, B: int, n_in: int, csr_cache: dict | None = None):
+        self.current = hasattr(p, "sign") and hasattr(p, "U_rest")
+        if self.current:
+            p = _CurrentAsFields(p)
         self.keep = []  # arrays the C structures point into
         made = _np(drive.made, np.uint8)
         scale = _np(drive.scale, np.float32)
@@ -155,6 +179,7 @@ class Network:
         net.surr_scale = float(np.asarray(_np(p.surr_scale)).reshape(-1)[0])
         net.sample = int(p.spike_mode == "sample")
         net.R = R
+        net.current = int(self.current)
         self.net = net
         self.has_ref = p.n_ref is not None
         self.has_adapt = p.adapt is not None
@@ -165,9 +190,12 @@ class Network:
         x = _np(x, np.float32)
         B, T = x.shape[:2]
         assert B == self.B and x.shape[2] == self.n_in
+        g = _np(g, np.float32)
+        if self.current:  # the currents (B, N, S) as the decay component of (B, N, 2, S)
+            g = np.stack([np.zeros_like(g), g], axis=2)
         st = {
             "v": _np(v, np.float32).copy(),
-            "g": _np(g, np.float32).copy(),
+            "g": g.copy(),
             "refractory": None if not self.has_ref else (
                 np.zeros((B, self.N), np.int32) if refractory is None
                 else _np(refractory, np.int32).copy()),
@@ -189,6 +217,8 @@ class Network:
                                 C.byref(out), _ptr(nz, _f))  # fmt: skip
         if rc:
             raise MemoryError("oracle: allocation failed")
+        if self.current:
+            st["g"] = np.ascontiguousarray(st["g"][:, :, 1])
         return dict(spikes=spikes.astype(bool), v_track=v_track, prob=prob, **st)
 
 

@@ -31,6 +31,11 @@ Three more kinds of case:
   ``STATS_NETWORKS``, 2,000 and 1,000 neurons, 3,000 and 2,000 steps of 1 ms), their
   inputs, the firing rates (and feedforward spikes) recorded from the reference's GPU
   simulator in ``tests/fixtures/statistics.npz``, and a run of its CPU dynamics.
+* ``current_*``: the reference's current-based test networks (``tests/networks.py``
+  ``current_recurrent``, ``current_feedforward``, ``current_feedforward_probabilities``,
+  and the recurrent one with a refractory period, short-term plasticity and adaptation)
+  run through ``network_simulators/current/dynamics.py`` ``simulate`` (forward only),
+  with the reference suite's recordings (``tests/fixtures/current_*.npz``) where there are.
 * ``loss_filter`` / ``loss_van_rossum``: the reference's ``double_exponential``
   (``training_utils/filtering.py:28-73``, its CPU Toeplitz path) and
   ``VanRossumRateLoss`` over three chunks with the filter state carried, with the
@@ -507,6 +512,42 @@ def make_loss_cases():
     print("loss_filter, loss_van_rossum written")
 
 
+def current_scenarios(networks):
+    """The current-based family's cases: ``name -> (build(batch) -> Built, probabilities,
+    recorded fixture)``, from the reference's ``tests/networks.py``."""
+    SEED = networks.SEED
+    return {
+        "current_recurrent": (lambda b: networks.current_recurrent(b, SEED), False, "current_recurrent"),
+        "current_feedforward": (lambda b: networks.current_feedforward(b, SEED), False, "current_feedforward"),
+        "current_feedforward_probabilities": (
+            lambda b: networks.current_feedforward_probabilities(b, SEED), True,
+            "current_feedforward_probabilities",
+        ),
+        "current_recurrent_features": (
+            lambda b: networks.current_recurrent(b, SEED, tau_ref=2.0, stp=True, adapt=0.3), False, None,
+        ),
+    }  # fmt: skip
+
+
+def make_current_case(name, spec, reference, batch=2):
+    """A current-based network's free run through the reference's
+    ``current/dynamics.py`` ``simulate`` (forward only), with the reference suite's
+    recording where it has one."""
+    from wiretorch.network_simulators.current import dynamics as current_dynamics
+
+    build, probabilities, fixture = spec
+    built = build(batch)
+    x = torch.from_numpy(built.input_spikes).float()[:, :T_FREE]
+    drive, p, inputs, outputs = free_run(current_dynamics, built.model, x, probabilities)
+    recorded = recorded_fixture(reference, fixture, "I_syn") if fixture else {}
+    meta = dict(case=name, batch=batch, steps=T_FREE, window=WINDOW, probabilities=probabilities,
+                family="current", origin="reference tests/networks.py current-based network")  # fmt: skip
+    golden_io.save(HERE / f"{name}.npz", drive=drive, p=p, inputs=inputs, outputs=outputs, grads={},
+                   recorded=recorded, meta=meta)  # fmt: skip
+    s = outputs["spikes"]
+    print(f"{name}: {int(s.sum())} spikes in {tuple(s.shape)}")
+
+
 def main():
     parser = argparse.ArgumentParser()
     parser.add_argument("--reference", default=os.environ.get("WIRETORCH_REFERENCE"))
@@ -520,9 +561,12 @@ def main():
     cases = scenario_cases(networks)
     configs_ = config_builders()
     stats = ["statistics_recurrent", "statistics_feedforward"]
-    todo = args.names or [*cases, "recurrent_gradients", *configs_, *stats, "loss"]
+    current = current_scenarios(networks)
+    todo = args.names or [*cases, "recurrent_gradients", *configs_, *stats, "loss", *current]
     for name in todo:
-        if name in configs_:
+        if name in current:
+            make_current_case(name, current[name], reference)
+        elif name in configs_:
             make_config_case(name, *configs_[name], dynamics)
         elif name in stats:
             make_statistics_case(name, reference, networks, dynamics)

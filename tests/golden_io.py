@@ -25,7 +25,7 @@ from pathlib import Path
 import numpy as np
 import torch
 
-from wiretorch_b200.types import Drive, Gate, Physiology, SparseRows
+from wiretorch_b200.types import CurrentPhysiology, Drive, Gate, Physiology, SparseRows
 
 GOLDEN = Path(__file__).parent / "golden"
 
@@ -33,6 +33,11 @@ PHYSIOLOGY_FIELDS = (
     "theta", "U_reset", "E_L", "C_m", "beta", "E_syn", "g_clip", "decay", "jump",
     "dt", "surr_scale", "n_ref", "mg_c", "mg_a", "adapt", "adapt_decay", "E_adapt",
 )  # fmt: skip
+
+
+#: The current-based family's physiology (``meta["family"] == "current"``).
+CURRENT_FIELDS = ("theta", "U_reset", "beta", "U_rest", "R", "sign", "decay", "surr_scale", "n_ref",
+                  "adapt", "adapt_decay")  # fmt: skip
 
 
 def pack(spikes) -> np.ndarray:
@@ -86,7 +91,7 @@ def save(path: Path, *, drive, p, inputs: dict, outputs: dict, grads: dict,
     meta["spike_mode"] = p.spike_mode
     arrays["net.made"] = _np(drive.made).astype(bool)
     arrays["net.scale"] = _np(drive.scale).astype(np.float32)
-    for name in PHYSIOLOGY_FIELDS:
+    for name in CURRENT_FIELDS if meta.get("family") == "current" else PHYSIOLOGY_FIELDS:
         value = getattr(p, name)
         if value is not None:
             arrays[f"phys.{name}"] = _np(value)
@@ -146,10 +151,11 @@ def load(name: str, device="cpu"):
         gates=gates,
     )
     phys = {}
-    for name in PHYSIOLOGY_FIELDS:
+    current = meta.get("family") == "current"
+    for name in CURRENT_FIELDS if current else PHYSIOLOGY_FIELDS:
         key = f"phys.{name}"
         phys[name] = t(arrays[key]) if key in arrays else None
-    p = Physiology(**phys, spike_mode=meta["spike_mode"])
+    p = (CurrentPhysiology if current else Physiology)(**phys, spike_mode=meta["spike_mode"])
     data = {}
     for key, value in arrays.items():
         if key.startswith(("net.", "phys.")) or key.endswith((".shape", ".xshape")):
@@ -164,12 +170,17 @@ def load(name: str, device="cpu"):
     return drive, p, data, meta
 
 
-KINDS = ("config_", "statistics_", "loss_")
+KINDS = ("config_", "statistics_", "loss_", "current_")
 
 
 def cases() -> list[str]:
     """The scenario cases (one engine call of a reference test network each)."""
     return sorted(p.stem for p in GOLDEN.glob("*.npz") if not p.stem.startswith(KINDS))
+
+
+def current_cases() -> list[str]:
+    """The current-based family's scenario cases (``current_*``)."""
+    return sorted(p.stem for p in GOLDEN.glob("current_*.npz"))
 
 
 def config_cases() -> list[str]:

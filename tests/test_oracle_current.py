@@ -1,0 +1,35 @@
+"""The oracle's current-based step (``cond_lif.c`` with ``current`` set, restating
+``network_simulators/current/dynamics.py:116-205``) against the reference's own runs of
+its current-based test networks (golden cases ``current_*``; three also match the
+reference suite's recordings): the spike raster exactly, voltages within 1e-5 (natural
+units, threshold 1) and the final currents within 1e-5 relative. Both of the oracle's
+schedules (whole trials per thread, and each step's neurons over all threads) are run."""
+
+import numpy as np
+import pytest
+
+import golden_io
+from oracle import oracle
+
+CASES = golden_io.current_cases()
+
+
+@pytest.mark.parametrize("threads", [1, 4])
+@pytest.mark.parametrize("name", CASES)
+def test_oracle_free_run_matches_reference(name, threads):
+    drive, p, d, meta = golden_io.load(name)
+    oracle.set_threads(threads)
+    try:
+        net = oracle.Network(drive, p, d["in.x"].shape[0], d["in.x"].shape[2])
+        kw = {k: d[f"in.{k}"] for k in ("refractory", "gating", "adaptation") if f"in.{k}" in d}
+        out = net.simulate(d["in.x"], d["in.v"], d["in.g"], probabilities=meta["probabilities"], **kw)
+    finally:
+        oracle.set_threads(1)
+    differs = (out["spikes"] != d["out.spikes"]).any(axis=(0, 2))
+    assert not differs.any(), f"first divergence at step {int(np.argmax(differs))}"
+    np.testing.assert_allclose(out["v_track"], d["out.v_track"], rtol=0, atol=1e-5)
+    np.testing.assert_allclose(out["g"], d["out.g"], rtol=1e-5, atol=1e-6)
+    if meta["probabilities"]:
+        np.testing.assert_allclose(out["prob"], d["out.prob"], rtol=0, atol=1e-5)
+    if "rec.spikes" in d:
+        assert (out["spikes"] == d["rec.spikes"]).all()

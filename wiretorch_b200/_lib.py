@@ -32,6 +32,7 @@ ERRORS = {
 F_REFRACTORY, F_MG_BLOCK, F_ADAPT, F_SAMPLE, F_GATED = 1, 2, 4, 8, 16
 F_PARTITION = 1 << 9
 F_STREAM = 1 << 10
+F_CURRENT = 1 << 11
 F_SAVE, F_TRACK, F_PROB, F_SAVE_INPUT = 32, 64, 128, 256
 
 P = C.c_void_p

@@ -111,8 +111,10 @@ int check_forward(const WtNet *net, const WtForward *run, const WtWorkspace *ws)
         return fail(WT_ERR_ARGS, "missing state or output%s");
     const int f = run->flags;
     if ((f & WT_F_REFRACTORY) && (!run->counter || !net->n_ref)) return fail(WT_ERR_ARGS, "refractory buffers%s");
-    if ((f & WT_F_ADAPT) && (!run->g_a || !net->adapt || !net->adapt_decay || !net->E_adapt))
+    if ((f & WT_F_ADAPT) && (!run->g_a || !net->adapt || !net->adapt_decay || (!net->E_adapt && !(f & WT_F_CURRENT))))
         return fail(WT_ERR_ARGS, "adaptation buffers%s");
+    if ((f & WT_F_CURRENT) && (f & (WT_F_PARTITION | WT_F_MG_BLOCK)))
+        return fail(WT_ERR_UNSUPPORTED, "current-based neurons: no neuron partition or Mg block%s");
     if ((f & WT_F_SAMPLE) && !run->noise) return fail(WT_ERR_ARGS, "noise buffer%s");
     if ((f & WT_F_GATED) && (!run->gating || !net->slot_gate || !net->slot_row || !net->gate_params ||
                              !net->gate_cols))

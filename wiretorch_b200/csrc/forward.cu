@@ -341,6 +341,10 @@ __global__ void __launch_bounds__(warps_of<S, FEAT>() * 32, 1) forward_kernel(co
     const bool TRACK = GEN && (flags & WT_F_TRACK);
     const bool SAVE_IN = GEN && (flags & WT_F_SAVE_INPUT);
     const bool PART = GEN ? (flags & WT_F_PARTITION) != 0 : (FEAT & kPart) != 0;
+    // current-based neurons: a step's input enters the currents the same step's membrane
+    // update uses, so every warp scatters first and a grid barrier completes X_t before
+    // the items read it (the conductance step uses the input a step later)
+    const bool CUR = GEN && (flags & WT_F_CURRENT);
 
     const int B = net.B, N = net.N, n_in = net.n_in, C = net.C, T = run.T, Np = geo.Np;
     const int Nsrc = net.N_src > 0 ? net.N_src : N;  // neuron sources (all ranks' when partitioned)
@@ -412,14 +416,14 @@ __global__ void __launch_bounds__(warps_of<S, FEAT>() * 32, 1) forward_kernel(co
             k.E_L = net.E_L[n];
             k.Cm = net.C_m[n];
             k.rate = -log1pf(net.beta[n] - 1.0f) / dt;
-            k.g_L = k.Cm * k.rate;
+            k.g_L = CUR ? net.beta[n] : k.Cm * k.rate;  // current-based: the leak's decay beta
             k.n_ref = REF ? net.n_ref[n] : 0;
             k.c0 = net.src_chunk[n];
             k.cnt = net.src_chunk[n + 1] - k.c0;
             if (ADAPT) {
                 k.adapt = net.adapt[n];
                 k.a_decay = net.adapt_decay[n];
-                k.E_a = net.E_adapt[n];
+                k.E_a = CUR ? 0.0f : net.E_adapt[n];
             }
         }
         return k;
@@ -757,17 +761,22 @@ __global__ void __launch_bounds__(warps_of<S, FEAT>() * 32, 1) forward_kernel(co
     for (int t = 0; t < T; t++) {
         const int t_abs = run.t0 + t;
         const bool emit_next = t + 1 < T;
-        const bool has_x = t > 0;
-        unsigned long long *Xprev = ws.X + (size_t)((t + 1) & 1) * C * BNp;  // X_{t-1}
+        const bool has_x = CUR || t > 0;
+        // the input the items complete their state with: X_{t-1}, or X_t (current-based)
+        unsigned long long *Xprev = ws.X + (size_t)((t + (CUR ? 0 : 1)) & 1) * C * BNp;
         stamp(t, 0);
-        // The first D items' copies go out now and land while the warp scatters.
+        // The first D items' copies go out now and land while the warp scatters (after
+        // the scatter's barrier when the items read this step's input).
         Cursor qi = start;
         int wr = 0;
-        for (int d = 0; d < D; d++) {
-            issue(d, qi, wr, Xprev, has_x);
-            qi.next(B, N, Np, TN);
-            if (++wr == D) wr = 0;
-        }
+        auto issue_first = [&]() {
+            for (int d = 0; d < D; d++) {
+                issue(d, qi, wr, Xprev, has_x);
+                qi.next(B, N, Np, TN);
+                if (++wr == D) wr = 0;
+            }
+        };
+        if (!CUR) issue_first();
 
         // ---------------- the input columns of the next step ----------------
         if (emit_next) {
@@ -902,8 +911,12 @@ __global__ void __launch_bounds__(warps_of<S, FEAT>() * 32, 1) forward_kernel(co
             }
         };
         stamp(t, 1);
-        const bool scatter_late = (threadIdx.x >> 5) & 1;
+        const bool scatter_late = !CUR && ((threadIdx.x >> 5) & 1);
         if (!scatter_late) scatter();
+        if (CUR) {
+            if (!bar.sync(ws.err)) return;
+            issue_first();
+        }
         stamp(t, 2);
 
         // ---------------- the neurons: step t, and the spikes of step t + 1 ----------------
@@ -991,12 +1004,13 @@ __global__ void __launch_bounds__(warps_of<S, FEAT>() * 32, 1) forward_kernel(co
                     }
                     unsigned long long *xz = Xprev + q.bNp + n;
                     for (int c = 0; c < C; c++, xz += BNp) *xz = 0ull;
+                    const int t_in = CUR ? t_abs : t_abs - 1;  // the step whose input this is
                     if (SAVE_IN)
                         for (int c = 0; c < C; c++)
-                            run.X_saved[(((size_t)b * run.T_total + t_abs - 1) * C + c) * N + n] = xall[c];
+                            run.X_saved[(((size_t)b * run.T_total + t_in) * C + c) * N + n] = xall[c];
                     if (TRACK && (run.track_b < 0 || run.track_b == b)) {
                         const int bt = run.track_b < 0 ? b : 0;
-                        float *tg = run.track_g + (((size_t)bt * run.T_total + t_abs - 1) * N + n) * 2 * S;
+                        float *tg = run.track_g + (((size_t)bt * run.T_total + t_in) * N + n) * 2 * S;
 #pragma unroll
                         for (int c = 0; c < S; c++) {
                             tg[c] = gr[c];
@@ -1006,31 +1020,45 @@ __global__ void __launch_bounds__(warps_of<S, FEAT>() * 32, 1) forward_kernel(co
                 }
                 const float u01 = SAMPLE ? run.noise[out] : 0.0f;
                 s = spike_of(v, k.theta, cnt, u01, sflags, ksur, held);
-                // membrane (conductance/dynamics.py:116-143), float32, in its order
-                float Gt[S];
-                float G = 0.0f, Isum = 0.0f;
-#pragma unroll
-                for (int c = 0; c < S; c++) {
-                    float gs = gr[c] + gd[c];
-                    gs = fminf(fmaxf(gs, 0.0f), net.g_clip[c]);
-                    // a channel without the block (mg_lc -inf) multiplies by sigmoid(+inf) = 1
-                    if (MG && net.mg_lc[c] != -INFINITY) gs = gs * sigmoid(net.mg_a[c] * v - net.mg_lc[c]);
-                    Gt[c] = gs;
-                }
-#pragma unroll
-                for (int c = 0; c < S; c++) G = G + Gt[c];
-#pragma unroll
-                for (int c = 0; c < S; c++) Isum = Isum + Gt[c] * (v - net.E_syn[c]);
-                const float I_leak = k.g_L * (v - k.E_L);
-                float J = Isum + I_leak;
-                if (ADAPT) {
-                    G = G + ga;
-                    J = J + ga * (v - k.E_a);
-                }
-                const float xx = dt * k.rate + dt * G / k.Cm;
-                const float step = -expm1f(-xx) / (k.g_L + G);
                 const float rr = fmaxf(s, held);
-                const float v_next = (v - step * J) * (1.0f - rr) + k.U_reset * rr;
+                float Gt[S];
+                float I_leak = 0.0f, v_next;
+                if (CUR) {
+                    // current-based membrane (current/dynamics.py:116-125, 180-183), float32,
+                    // in its order: the adaptation current rises by the spike first, then
+                    // v' = (beta v + (1 - beta)(U_rest + R (sum_j sign_j I_j - I_a)))(1 - r) + U r
+                    if (ADAPT) ga = ga * k.a_decay + k.adapt * s;
+                    float Isyn = 0.0f;
+#pragma unroll
+                    for (int c = 0; c < S; c++) Isyn = Isyn + gd[c] * net.E_syn[c];
+                    if (ADAPT) Isyn = Isyn - ga;
+                    const float beta = k.g_L;
+                    v_next = (beta * v + (1.0f - beta) * (k.E_L + k.Cm * Isyn)) * (1.0f - rr) + k.U_reset * rr;
+                } else {
+                    // membrane (conductance/dynamics.py:116-143), float32, in its order
+                    float G = 0.0f, Isum = 0.0f;
+#pragma unroll
+                    for (int c = 0; c < S; c++) {
+                        float gs = gr[c] + gd[c];
+                        gs = fminf(fmaxf(gs, 0.0f), net.g_clip[c]);
+                        // a channel without the block (mg_lc -inf) multiplies by sigmoid(+inf) = 1
+                        if (MG && net.mg_lc[c] != -INFINITY) gs = gs * sigmoid(net.mg_a[c] * v - net.mg_lc[c]);
+                        Gt[c] = gs;
+                    }
+#pragma unroll
+                    for (int c = 0; c < S; c++) G = G + Gt[c];
+#pragma unroll
+                    for (int c = 0; c < S; c++) Isum = Isum + Gt[c] * (v - net.E_syn[c]);
+                    I_leak = k.g_L * (v - k.E_L);
+                    float J = Isum + I_leak;
+                    if (ADAPT) {
+                        G = G + ga;
+                        J = J + ga * (v - k.E_a);
+                    }
+                    const float xx = dt * k.rate + dt * G / k.Cm;
+                    const float step = -expm1f(-xx) / (k.g_L + G);
+                    v_next = (v - step * J) * (1.0f - rr) + k.U_reset * rr;
+                }
                 if (SAVE) {
                     run.v_saved[out] = v;
                     float *Gs = run.G_saved + (q.bTN + tN) * S + n;
@@ -1042,7 +1070,7 @@ __global__ void __launch_bounds__(warps_of<S, FEAT>() * 32, 1) forward_kernel(co
                     const int c1 = cnt - 1;
                     cnt = s > 0.0f ? k.n_ref : (c1 > 0 ? c1 : 0);
                 }
-                if (ADAPT) ga = ga * k.a_decay + k.adapt * s;
+                if (ADAPT && !CUR) ga = ga * k.a_decay + k.adapt * s;
                 run.spikes[out] = s;
                 if (PROB) {
                     const float p = sigmoid(ksur * (v - k.theta));
@@ -1052,10 +1080,12 @@ __global__ void __launch_bounds__(warps_of<S, FEAT>() * 32, 1) forward_kernel(co
                     const int bt = run.track_b < 0 ? b : 0;
                     const size_t to = ((size_t)bt * run.T_total + t_abs) * N + n;
                     run.track_v[to] = v_next;
-                    float *tI = run.track_I + to * (S + 1);
+                    if (!CUR) {  // (current-based: the currents are the tracked channels)
+                        float *tI = run.track_I + to * (S + 1);
 #pragma unroll
-                    for (int c = 0; c < S; c++) tI[c] = Gt[c] * (v - net.E_syn[c]);
-                    tI[S] = I_leak;
+                        for (int c = 0; c < S; c++) tI[c] = Gt[c] * (v - net.E_syn[c]);
+                        tI[S] = I_leak;
+                    }
                     if (ADAPT) run.track_a[to] = ga;
                 }
                 // the state entering step t + 1 (g: before this step's input)
@@ -1163,6 +1193,13 @@ __global__ void __launch_bounds__(warps_of<S, FEAT>() * 32, 1) forward_kernel(co
             float gr[S], gd[S];
 #pragma unroll
             for (int c = 0; c < S; c++) {
+                if (CUR) {  // the currents already hold the last step's input
+                    gd[c] = RES ? rp[(w_gd + c) * 32] : g_b[(size_t)(S + c) * N];
+                    gr[c] = (RES && rw[c] >= 0) ? rp[rw[c] * 32] : g_b[(size_t)c * N];
+                    g_b[(size_t)c * N] = gr[c];
+                    g_b[(size_t)(S + c) * N] = gd[c];
+                    continue;
+                }
                 gd[c] = (RES ? rp[(w_gd + c) * 32] : g_b[(size_t)(S + c) * N]) * net.decay_d[c];
                 if (rw[c] >= 0)
                     gr[c] = (RES ? rp[rw[c] * 32] : g_b[(size_t)c * N]) * net.decay_r[c];
@@ -1176,11 +1213,11 @@ __global__ void __launch_bounds__(warps_of<S, FEAT>() * 32, 1) forward_kernel(co
                 g_b[(size_t)c * N] = gr[c];
                 g_b[(size_t)(S + c) * N] = gd[c];
             }
-            if (SAVE_IN)
+            if (SAVE_IN && !CUR)
                 for (int c = 0; c < C; c++)
                     run.X_saved[(((size_t)b * run.T_total + t_last) * C + c) * N + n] =
                         __ll2float_rn((long long)__ldcg(Xl + (size_t)c * BNp + xo)) * net.fx_inv[c];
-            if (TRACK && (run.track_b < 0 || run.track_b == b)) {
+            if (TRACK && !CUR && (run.track_b < 0 || run.track_b == b)) {
                 const int bt = run.track_b < 0 ? b : 0;
                 float *tg = run.track_g + (((size_t)bt * run.T_total + t_last) * N + n) * 2 * S;
 #pragma unroll
@@ -1315,7 +1352,7 @@ static cudaError_t launch_sf(const WtNet &net, const WtForward &run, const WtWor
 // and saving as given; no other feature); everything else runs the generic kernel.
 template <int S>
 static cudaError_t launch_s(const WtNet &net, const WtForward &run, const WtWorkspace &ws, cudaStream_t st) {
-    const int generic = WT_F_SAMPLE | WT_F_PROB | WT_F_TRACK | WT_F_SAVE_INPUT;
+    const int generic = WT_F_SAMPLE | WT_F_PROB | WT_F_TRACK | WT_F_SAVE_INPUT | WT_F_CURRENT;
     const int feat = ((run.flags & WT_F_REFRACTORY) ? kRef : 0) | ((run.flags & WT_F_SAVE) ? kSave : 0) |
                      ((run.flags & WT_F_MG_BLOCK) ? kMg : 0) | ((run.flags & WT_F_GATED) ? kGate : 0) |
                      ((run.flags & WT_F_ADAPT) ? kAdapt : 0) | ((run.flags & WT_F_PARTITION) ? kPart : 0);

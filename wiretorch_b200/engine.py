@@ -192,6 +192,8 @@ def run_forward(plan, p, x, v, g, counter, g_a, gating, *, probabilities=False, 
         flags |= _lib.F_GATED
     if FORCE_STREAM:
         flags |= _lib.F_STREAM
+    if getattr(p, "current", False):  # current-based neurons (wiretorch_b200.current)
+        flags |= _lib.F_CURRENT
     out = {"spikes": torch.empty((B, T, N), device=device)}
     run.v, run.g = v.data_ptr(), g.data_ptr()
     run.counter = _lib.ptr(counter) if flags & _lib.F_REFRACTORY else None

@@ -133,6 +133,33 @@ class Physiology:
 
 
 @dataclass
+class CurrentPhysiology:
+    """Every parameter of the current-based dynamics (``current/dynamics.py:56-85``).
+
+    Per neuron ``(N,)``: ``theta``, ``U_reset``, ``beta`` (the leak's per-step decay),
+    ``U_rest`` (the voltage the leak relaxes to), ``R`` (the membrane resistance); per
+    synapse type ``(S,)``: ``sign`` (+1 or -1) and ``decay`` (the current's per-step
+    decay). ``n_ref`` ``(N,)`` int32 refractory periods in steps (None: none); ``adapt``,
+    ``adapt_decay`` ``(N,)`` the adaptation current's rise per spike and decay (None:
+    none adapts).
+    """
+
+    theta: torch.Tensor
+    U_reset: torch.Tensor
+    beta: torch.Tensor
+    U_rest: torch.Tensor
+    R: torch.Tensor
+    sign: torch.Tensor
+    decay: torch.Tensor
+    surr_scale: torch.Tensor
+    spike_mode: str = "deterministic"
+    storage_dtype: torch.dtype = torch.float32
+    n_ref: torch.Tensor | None = None
+    adapt: torch.Tensor | None = None
+    adapt_decay: torch.Tensor | None = None
+
+
+@dataclass
 class Run:
     """What a simulation produced (``network_simulators/network.py:321-351``).
 
