@@ -34,8 +34,9 @@ Three more kinds of case:
 * ``current_*``: the reference's current-based test networks (``tests/networks.py``
   ``current_recurrent``, ``current_feedforward``, ``current_feedforward_probabilities``,
   and the recurrent one with a refractory period, short-term plasticity and adaptation)
-  run through ``network_simulators/current/dynamics.py`` ``simulate`` (forward only),
-  with the reference suite's recordings (``tests/fixtures/current_*.npz``) where there are.
+  run through ``network_simulators/current/dynamics.py`` ``simulate``, with the
+  reference suite's recordings (``tests/fixtures/current_*.npz``) where there are, and the
+  gradients of a fixed readout with respect to the scale, the weights and the input.
 * ``loss_filter`` / ``loss_van_rossum``: the reference's ``double_exponential``
   (``training_utils/filtering.py:28-73``, its CPU Toeplitz path) and
   ``VanRossumRateLoss`` over three chunks with the filter state carried, with the
@@ -529,23 +530,68 @@ def current_scenarios(networks):
     }  # fmt: skip
 
 
+def current_gradients(dynamics, model, x, probabilities):
+    """Gradients of ``sum(spikes R) (+ sum(prob R2))`` over ``GRAD_STEPS`` steps of a
+    current-based network with respect to its scale, weights and input (its physiology
+    fixed), through the recurrent spikes when the network's drive says so (the
+    current-based networks' default)."""
+    drive, p = model._drive(), model._physiology()
+    v, I, kw = engine_inputs(model)
+    x = x[:, :GRAD_STEPS].clone().requires_grad_(True)
+    leaves = {"x": x}
+    drive.scale = drive.scale.detach().clone().requires_grad_(True)
+    leaves["scale"] = drive.scale
+    made = {}
+
+    def leaf(W):
+        if id(W) not in made:
+            made[id(W)] = W.detach().clone().requires_grad_(True)
+        return made[id(W)]
+
+    drive.recurrent = [(r, leaf(W)) for r, W in drive.recurrent]
+    drive.feedforward = [(r, leaf(W)) for r, W in drive.feedforward]
+    for name in ("theta", "U_reset", "beta", "U_rest", "R", "sign", "decay", "surr_scale", "adapt", "adapt_decay"):
+        value = getattr(p, name)
+        if isinstance(value, torch.Tensor):
+            setattr(p, name, value.detach())
+    run = dynamics.simulate(v, I, x, drive, p, probabilities=probabilities, **kw)
+    loss = (run.output * readout(READOUT_SEED, run.output.shape)).sum()
+    if probabilities:
+        loss = loss + (run.probabilities * readout(READOUT_SEED + 2, run.output.shape)).sum()
+    loss.backward()
+    grads = {"loss": loss.detach()}
+    for key, value in leaves.items():
+        grads[key] = value.grad if value.grad is not None else torch.zeros_like(value)
+    seen = {}
+    for W in [W for _, W in drive.recurrent] + [W for _, W in drive.feedforward]:
+        if id(W) not in seen:
+            seen[id(W)] = len(seen)
+            grads[f"W.{seen[id(W)]}"] = W.grad if W.grad is not None else torch.zeros_like(W)
+    grads["spikes_sum"] = run.output.sum().detach()
+    return grads
+
+
 def make_current_case(name, spec, reference, batch=2):
     """A current-based network's free run through the reference's
-    ``current/dynamics.py`` ``simulate`` (forward only), with the reference suite's
-    recording where it has one."""
+    ``current/dynamics.py`` ``simulate``, with the reference suite's recording where it
+    has one, and the gradients of a fixed readout of its first ``GRAD_STEPS`` steps."""
     from wiretorch.network_simulators.current import dynamics as current_dynamics
 
     build, probabilities, fixture = spec
     built = build(batch)
     x = torch.from_numpy(built.input_spikes).float()[:, :T_FREE]
     drive, p, inputs, outputs = free_run(current_dynamics, built.model, x, probabilities)
+    built.model.reset_state()
+    grads = current_gradients(current_dynamics, built.model, x, probabilities)
     recorded = recorded_fixture(reference, fixture, "I_syn") if fixture else {}
     meta = dict(case=name, batch=batch, steps=T_FREE, window=WINDOW, probabilities=probabilities,
                 family="current", origin="reference tests/networks.py current-based network")  # fmt: skip
-    golden_io.save(HERE / f"{name}.npz", drive=drive, p=p, inputs=inputs, outputs=outputs, grads={},
+    meta.update(grad_steps=GRAD_STEPS, readout_seed=READOUT_SEED)
+    golden_io.save(HERE / f"{name}.npz", drive=drive, p=p, inputs=inputs, outputs=outputs, grads=grads,
                    recorded=recorded, meta=meta)  # fmt: skip
     s = outputs["spikes"]
-    print(f"{name}: {int(s.sum())} spikes in {tuple(s.shape)}")
+    print(f"{name}: {int(s.sum())} spikes in {tuple(s.shape)}, loss {float(grads['loss']):.4f}, "
+          f"recurrent gradients {bool(drive.recurrent_gradients)}")  # fmt: skip
 
 
 def main():

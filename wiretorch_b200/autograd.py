@@ -136,6 +136,8 @@ class _Simulate(torch.autograd.Function):
             flags |= _lib.F_ADAPT
         if p.spike_mode == "sample":
             flags |= _lib.F_SAMPLE
+        if getattr(p, "current", False):  # current-based neurons (wiretorch_b200.current)
+            flags |= _lib.F_CURRENT
         if cx.probabilities and grad_prob is not None and grad_prob.numel():
             flags |= _lib.F_PROB
             grad_prob = grad_prob.contiguous().float()

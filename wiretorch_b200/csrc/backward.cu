@@ -42,6 +42,7 @@ __global__ void __launch_bounds__(kBlock, (PHYS || S > 2) ? 1 : 3) backward_kern
     const int flags = bw.flags, wants = PHYS ? bw.wants : 0;
     const bool REF = flags & WT_F_REFRACTORY, MG = flags & WT_F_MG_BLOCK, ADAPT = flags & WT_F_ADAPT;
     const bool SAMPLE = flags & WT_F_SAMPLE, PROB = flags & WT_F_PROB;
+    const bool CUR = flags & WT_F_CURRENT;
     const int words = (N + 31) >> 5;
     const float dt = net.dt, k = net.surr_scale;
 
@@ -49,7 +50,7 @@ __global__ void __launch_bounds__(kBlock, (PHYS || S > 2) ? 1 : 3) backward_kern
     const float rate = -log1pf(beta - 1.0f) / dt;
     const float g_L = Cm * rate, inv_C = 1.0f / Cm;
     const float a_decay = ADAPT ? net.adapt_decay[n] : 0.0f;
-    const float E_a = ADAPT ? net.E_adapt[n] : 0.0f;
+    const float E_a = (ADAPT && !CUR) ? net.E_adapt[n] : 0.0f;
     int in_c[S];
 #pragma unroll
     for (int c = 0; c < S; c++) in_c[c] = net.input_of[c];
@@ -165,6 +166,52 @@ __global__ void __launch_bounds__(kBlock, (PHYS || S > 2) ? 1 : 3) backward_kern
                     H_d[c] = ld[c] + net.decay_d[c] * H_d[c];
                 }
             }
+        }
+        if (CUR) {
+            // Current-based step (current/dynamics.py:116-125, 166-183): the adjoint state
+            // entering step t is dL/dv_{t+1} and the adjoints of I_{t+1} and I_a{t+1}
+            // with the membrane of step t already added (so that Q_t above is complete,
+            // and the recurrent carry, which reads Q_t from the same state, sees it too).
+            const float gx = dv * (1.0f - r);
+            if (ADAPT) la = la * a_decay;  // I_a{t+1} = a_decay I_a{t} + adapt s_t (s detached)
+            const float xv = v - theta;
+            const float gs = cur.gs + R_b;
+            float g_x;
+            if (SAMPLE) {
+                const float p = sigmoid(k * xv);
+                g_x = gs * k * p * (1.0f - p);
+            } else {
+                const float d = k * fabsf(xv) + 1.0f;
+                g_x = __fdividef(gs, d * d);
+            }
+            if (PROB && bw.grad_prob) {
+                const float p = sigmoid(k * xv);
+                g_x += cur.gp * k * p * (1.0f - p);
+            }
+            if (REF) g_x *= 1.0f - held;
+            dv = gx * beta + g_x;
+#pragma unroll
+            for (int c = 0; c < S; c++) {
+                ld[c] = ld[c] * net.decay_d[c];
+                lr[c] = 0.0f;
+            }
+            // the membrane of step t - 1 read I_t and I_a{t}: its term, ahead
+            if (t >= 1) {
+                unsigned sb1, hb1;
+                if (t - 1 >= t_lo) {
+                    sb1 = q[0].sb;
+                    hb1 = q[0].hb;
+                } else {
+                    sb1 = __ldg(sb_b + (size_t)(t - 1) * words);
+                    hb1 = REF ? __ldg(hb_b + (size_t)(t - 1) * words) : 0u;
+                }
+                const float r1 = ((sb1 >> (n & 31)) & 1u) || (REF && ((hb1 >> (n & 31)) & 1u)) ? 1.0f : 0.0f;
+                const float c1 = dv * (1.0f - r1) * (1.0f - beta) * Cm;
+#pragma unroll
+                for (int c = 0; c < S; c++) ld[c] = ld[c] + c1 * net.E_syn[c];
+                if (ADAPT) la = la - c1;
+            }
+            continue;
         }
         float g_a = 0.0f;
         if (ADAPT) {

@@ -187,8 +187,10 @@ int wt_backward(const WtNet *net, const WtBackward *bw, void *stream) {
         return fail(WT_ERR_ARGS, "target-major adjoints need a whole scan and a 16-byte aligned buffer%s");
     const int f = bw->flags, w = bw->wants;
     if ((f & WT_F_REFRACTORY) && !bw->held_bits) return fail(WT_ERR_ARGS, "missing refractory bits%s");
-    if ((f & WT_F_ADAPT) && (!bw->a_saved || !net->adapt_decay || !net->E_adapt))
+    if ((f & WT_F_ADAPT) && (!bw->a_saved || !net->adapt_decay || (!net->E_adapt && !(f & WT_F_CURRENT))))
         return fail(WT_ERR_ARGS, "missing adaptation%s");
+    if ((f & WT_F_CURRENT) && (bw->wants || (f & WT_F_MG_BLOCK)))
+        return fail(WT_ERR_UNSUPPORTED, "current-based neurons: no physiology gradients%s");
     if ((w & (WT_W_DECAY | WT_W_JUMP)) && !bw->X_saved) return fail(WT_ERR_ARGS, "missing saved input%s");
     if ((w & WT_W_DECAY) && !bw->g_init) return fail(WT_ERR_ARGS, "missing initial conductances%s");
     float *const outs[11] = {bw->g_theta, bw->g_reset, bw->g_E_L, bw->g_C_m, bw->g_beta, bw->g_E_syn,

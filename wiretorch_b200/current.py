@@ -21,7 +21,10 @@ float32.
 
 The kernel reads the current-based parameters in the conductance fields of ``WtNet``
 (``U_rest`` as ``E_L``, ``R`` as ``C_m``, the types' signs as ``E_syn``; each type a single
-exponential). Forward only: a call that needs gradients raises.
+exponential). Gradients flow to the scales, the weights and the input (and, with
+``Drive.recurrent_gradients``, the current-based networks' default, through the recurrent
+spikes): the backward kernel's current-based adjoint, then the engine's edge gradients. A
+learnt physiology has no gradient here (such a call raises).
 """
 
 from __future__ import annotations
@@ -101,23 +104,33 @@ def simulate(
     if not x.is_cuda:
         raise RuntimeError("wiretorch_b200 runs on CUDA tensors only (no CPU path)")
     weights = [W for _, W in drive.recurrent] + [W for _, W in drive.feedforward]
-    if torch.is_grad_enabled() and (
-        drive.scale.requires_grad or x.requires_grad
-        or any(getattr(W, "requires_grad", False) for W in weights)
-        or any(isinstance(getattr(p, n, None), torch.Tensor) and getattr(p, n).requires_grad for n in PHYSIOLOGY)
-    ):  # fmt: skip
-        raise NotImplementedError("current-based networks: forward only on this engine (no gradients)")
+    if torch.is_grad_enabled() and any(
+        isinstance(getattr(p, n, None), torch.Tensor) and getattr(p, n).requires_grad for n in PHYSIOLOGY
+    ):
+        raise NotImplementedError("current-based networks: learnt physiology has no gradient on this engine")
+    grad = torch.is_grad_enabled() and (
+        drive.scale.requires_grad or x.requires_grad or any(getattr(W, "requires_grad", False) for W in weights)
+    )
     B, T, n_in = x.shape
     device = x.device
     f = _fields(p)
     plan = engine.get_plan(drive, f, B, n_in, device, pool=False)
-    _plan.fold(plan, drive.scale)
-    # the kernel's state: (B, 2, S, N), the rise component zero
+    # the kernel's state (B, 2, S, N) seen as the conductance layout (B, N, 2, S): the
+    # currents are the decay component, the rise component zero
     S = plan.ch.Sp
-    g = torch.zeros((B, 2, S, v.shape[1]), device=device)
-    g[:, 1] = I.detach().to(device, torch.float32).permute(0, 2, 1)
-    v_k, g_k, counter, g_a, gating_k = engine._prepare_state(plan, v, g.permute(0, 3, 1, 2), refractory, gating,
-                                                            adaptation, f)  # fmt: skip
+    g = torch.zeros((B, v.shape[1], 2, S), device=device)
+    g[:, :, 1] = I.detach().to(device, torch.float32)
+    if grad:
+        from wiretorch_b200 import autograd
+
+        run = autograd.simulate_with_grad(plan, v, g, x, drive, f, refractory, gating, adaptation, probabilities,
+                                          track, track_batch_idx)  # fmt: skip
+        run.syn = run.syn[:, :, 1]
+        if run.tracked is not None:
+            run.tracked["I"] = run.tracked.pop("g")[..., 1, :]
+        return run
+    _plan.fold(plan, drive.scale)
+    v_k, g_k, counter, g_a, gating_k = engine._prepare_state(plan, v, g, refractory, gating, adaptation, f)
     track_b = -1 if track_batch_idx is None else int(track_batch_idx)
     with torch.no_grad():
         out = engine.run_forward(plan, f, x.detach().float(), v_k, g_k, counter, g_a, gating_k,
