@@ -62,7 +62,8 @@ def parse():
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
-    ap.add_argument("--config", default="c5", choices=["c5", "c2", "c1", "c3", "c4"])
+    ap.add_argument("--config", default="c5", choices=["c5", "c2", "c1", "c3", "c4", "c2c"],
+                    help="c2c: the current-based family on C2's network (forward)")
     ap.add_argument("--chunk", type=int, default=None,
                     help="c3 / c4 / c5: steps per engine call, the state carried over (default 250 / 1000 / 1000)")
     ap.add_argument("--partition", action="store_true",
@@ -208,10 +209,28 @@ def build(args, rank, device):
         args.chunk = args.chunk or (250 if args.config == "c3" else 1000)
         cfg.extra["chunk"] = args.chunk
         return cfg, cfg.inputs(T=args.chunk, seed=1 + rank)  # one chunk of input, reused
+    elif args.config == "c2c":
+        cfg = configs.c2_current(B=args.batch or 64, T=500, seed=0, device=device)
     else:
         cfg = configs.c1(B=args.batch or 8, T=1000, seed=0, device=device)
     x = cfg.inputs(seed=1 + rank)
     return cfg, x
+
+
+def simulate_of(cfg):
+    """The engine entry point of a configuration's family: ``wiretorch_b200.current`` for
+    the current-based one (``c2c``), ``wiretorch_b200.engine`` otherwise."""
+    from wiretorch_b200 import current, engine
+
+    return current.simulate if cfg.name == "c2c" else engine.simulate
+
+
+def plan_of(cfg, device):
+    from wiretorch_b200 import current, engine
+
+    if cfg.name == "c2c":
+        return engine.get_plan(cfg.drive, current._fields(cfg.p), cfg.B, cfg.n_in, device, pool=False)
+    return engine.get_plan(cfg.drive, cfg.p, cfg.B, cfg.n_in, device)
 
 
 def make_step(cfg, world, train: bool):
@@ -237,12 +256,14 @@ def make_step(cfg, world, train: bool):
 
         return forward_chunks, None
     if not train:
+        sim = simulate_of(cfg)
+
         def forward(x, target=None, fetch=None):
             xi = x if fetch is None else fetch.get()
             if fetch is not None:
                 fetch.prefetch()
             with torch.no_grad():
-                run = engine.simulate(v0, g0, xi, cfg.drive, cfg.p, **kw0)
+                run = sim(v0, g0, xi, cfg.drive, cfg.p, **kw0)
             return run.v
 
         return forward, None
@@ -341,7 +362,8 @@ def forward_bytes(cfg, plan, T, spikes_bits_saved: bool, fired_sources_edges: fl
     weight) per edge of every source that fired in at least one trial of a step; and the
     gating state (release probabilities, resources) read and written, 8 per column-step."""
     S = plan.ch.Sp
-    per = 8 + 16 * S + 2 + 1 / 8
+    # (the current-based family's channels have no rise component: 8 bytes each)
+    per = 8 + (8 if cfg.name == "c2c" else 16) * S + 2 + 1 / 8
     if cfg.p.adapt is not None:
         per += 8
     if spikes_bits_saved:
@@ -482,7 +504,11 @@ def reference_dynamics_baseline(args, cfg):
     sys.path.insert(0, str(ref_dir))
     try:
         from wiretorch.network_simulators import network as ref_net
-        from wiretorch.network_simulators.conductance import dynamics as ref_dyn
+
+        if cfg.name == "c2c":  # the current-based family: current/dynamics.py
+            from wiretorch.network_simulators.current import dynamics as ref_dyn
+        else:
+            from wiretorch.network_simulators.conductance import dynamics as ref_dyn
     except Exception as e:  # noqa: BLE001
         return {"unavailable": f"importing the reference failed: {type(e).__name__}: {e}"}
     cpu = _to_cpu(cfg)
@@ -503,6 +529,9 @@ def reference_dynamics_baseline(args, cfg):
                           feedforward=[(r, dense_of(W)) for r, W in cpu.drive.feedforward])  # fmt: skip
     fields = ("theta", "U_reset", "E_L", "C_m", "beta", "E_syn", "g_clip", "decay", "jump", "dt",
               "surr_scale", "n_ref", "mg_c", "mg_a", "adapt", "adapt_decay", "E_adapt")  # fmt: skip
+    if cfg.name == "c2c":
+        fields = ("theta", "U_reset", "beta", "U_rest", "R", "sign", "decay", "surr_scale", "n_ref", "adapt",
+                  "adapt_decay")  # fmt: skip
     p = ref_dyn.Physiology(**{f: getattr(cpu.p, f) for f in fields}, spike_mode=cpu.p.spike_mode)
     v, g, kw = cpu.state()
 
@@ -697,7 +726,7 @@ def main_single(args, rank, world, local):
         step(x, target)
     torch.cuda.synchronize()
     factorised = cfg.name == "c3"
-    plan = None if factorised else engine.get_plan(cfg.drive, cfg.p, cfg.B, cfg.n_in, device)
+    plan = None if factorised else plan_of(cfg, device)
 
     # ---- synaptic events: counted on the device over one untimed step (the counter's
     # atomics stay out of the timed region) ----
@@ -742,7 +771,7 @@ def main_single(args, rank, world, local):
     kernel_ms = {k: sum(s.elapsed_time(e) for s, e in v) / len(v) for k, v in timer.items()}
     with torch.no_grad():
         v0, g0, kw0 = cfg.state()
-        run = engine.simulate(v0, g0, x, cfg.drive, cfg.p, **kw0)
+        run = simulate_of(cfg)(v0, g0, x, cfg.drive, cfg.p, **kw0)
     if factorised:
         kname = "wt_lowrank_forward"
         fwd_bytes = factorised_bytes(cfg, x.shape[1])

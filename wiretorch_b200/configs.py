@@ -46,9 +46,13 @@ class Config:
         """``(v, g, kw)`` at rest: voltages at reset, conductances zero (and the gating
         state of a gated network at its rest values)."""
         dev = self.drive.scale.device
-        S = self.p.E_syn.shape[0]
+        current = hasattr(self.p, "sign")  # current-based: the currents (B, N, S)
+        S = (self.p.sign if current else self.p.E_syn).shape[0]
         v = self.p.U_reset.expand(self.B, self.N).clone()
-        g = torch.zeros((self.B, 2, S, self.N), device=dev).permute(0, 3, 1, 2)
+        if current:
+            g = torch.zeros((self.B, S, self.N), device=dev).permute(0, 2, 1)
+        else:
+            g = torch.zeros((self.B, 2, S, self.N), device=dev).permute(0, 3, 1, 2)
         kw = {"refractory": torch.zeros((self.B, self.N), dtype=torch.int32, device=dev)}
         if self.p.adapt is not None:
             kw["adaptation"] = torch.zeros((self.B, self.N), device=dev)
@@ -70,7 +74,8 @@ class Config:
         T = self.T if T is None else T
         dev = self.drive.scale.device
         gen = torch.Generator(device=dev).manual_seed(seed)
-        p = (self.rates_in * float(self.p.dt) / 1000.0).to(dev)
+        dt = float(self.p.dt) if hasattr(self.p, "dt") else self.extra["dt"]  # (current-based: in extra)
+        p = (self.rates_in * dt / 1000.0).to(dev)
         return (torch.rand((self.B, T, self.n_in), generator=gen, device=dev) < p).float()
 
 
@@ -220,6 +225,43 @@ def c2(B=64, T=500, seed=0, device="cuda", n_in=2000, p_in=0.05, w_mu=-1.0, w_mu
     cfg.extra["log_sf_shape"] = (S, n_types)
     cfg.extra["target_rates"] = torch.from_numpy(
         rng.uniform(1.0, 30.0, (B, N)).astype(np.float32)).to(dev)  # fmt: skip
+    return cfg
+
+
+def c2_current(B=64, T=500, seed=0, device="cuda", w_scale=0.15, N=20000, p_max=0.05, **kw):
+    """The current-based family on C2's network: the same 40-type connectome, weights
+    (times ``w_scale``, as current jumps) and Poisson input as ``c2``, with current-based
+    neurons in the family's natural units (``current/dynamics.py``; reset 0, threshold 1,
+    U_rest 0, R 1, tau_m 20 ms, refractory 2 ms, surrogate scale 10); each cell type's
+    synapse type signed by the type (+1 excitatory, -1 inhibitory; the input +1) and
+    decaying with its C2 time constant (5 or 10 ms). Forward only in the benchmark. At the
+    chosen ``w_scale`` the network fires at 5-10 Hz."""
+    from wiretorch_b200.types import CurrentPhysiology
+
+    base = c2(B=B, T=T, seed=seed, device=device, N=N, p_max=p_max, **kw)
+    dev = base.drive.scale.device
+    d = base.drive
+
+    def scaled(W):
+        return type(W)(W.row_ptr, W.cols, W.values * w_scale, W.n_targets)
+
+    drive = Drive(made=d.made, scale=d.scale, recurrent=[(r, scaled(W)) for r, W in d.recurrent],
+                  feedforward=[(r, scaled(W)) for r, W in d.feedforward])  # fmt: skip
+    S = d.made.shape[1]
+    n_types = base.n_types
+    n_e_types = sum(1 for a in range(n_types) if float(base.p.E_syn[a]) == 0.0)
+    sign = torch.tensor([1.0 if a < n_e_types else -1.0 for a in range(n_types)] + [1.0], device=dev)
+    tau_s = torch.tensor([5.0 if a < n_e_types else 10.0 for a in range(n_types)] + [5.0], device=dev)
+    dt = 0.1
+    ones = torch.ones(base.N, device=dev)
+    p = CurrentPhysiology(
+        theta=ones.clone(), U_reset=torch.zeros(base.N, device=dev), beta=ones * math.exp(-dt / 20.0),
+        U_rest=torch.zeros(base.N, device=dev), R=ones.clone(), sign=sign, decay=torch.exp(-dt / tau_s),
+        surr_scale=torch.tensor(10.0, device=dev), n_ref=torch.full((base.N,), 20, dtype=torch.int32, device=dev),
+    )  # fmt: skip
+    assert S == sign.numel()
+    cfg = Config("c2c", drive, p, B, T, base.N, base.n_in, base.rates_in, base.types, n_types, base.out_degree)
+    cfg.extra["dt"] = dt
     return cfg
 
 
