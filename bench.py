@@ -211,6 +211,7 @@ def build(args, rank, device):
         return cfg, cfg.inputs(T=args.chunk, seed=1 + rank)  # one chunk of input, reused
     elif args.config == "c2c":
         cfg = configs.c2_current(B=args.batch or 64, T=500, seed=0, device=device)
+        engine.POOL_SYNAPSES = True  # 41 synapse types with 2 distinct (decay, sign) pairs
     else:
         cfg = configs.c1(B=args.batch or 8, T=1000, seed=0, device=device)
     x = cfg.inputs(seed=1 + rank)
@@ -229,7 +230,7 @@ def plan_of(cfg, device):
     from wiretorch_b200 import current, engine
 
     if cfg.name == "c2c":
-        return engine.get_plan(cfg.drive, current._fields(cfg.p), cfg.B, cfg.n_in, device, pool=False)
+        return engine.get_plan(cfg.drive, current._fields(cfg.p), cfg.B, cfg.n_in, device)
     return engine.get_plan(cfg.drive, cfg.p, cfg.B, cfg.n_in, device)
 
 

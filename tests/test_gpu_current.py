@@ -26,7 +26,7 @@ import pytest
 import torch
 
 import golden_io
-from wiretorch_b200 import current
+from wiretorch_b200 import current, engine
 
 pytestmark = pytest.mark.gpu
 
@@ -104,6 +104,26 @@ def test_free_run_is_spike_exact(name):
     np.testing.assert_allclose(run.tracked["v"].cpu().numpy(), d["out.v_track"], rtol=V_RTOL, atol=V_ATOL)
     if "rec.spikes" in d:  # the reference suite's own recording
         assert (spikes == d["rec.spikes"]).all()
+
+
+@pytest.mark.parametrize("name", CASES)
+def test_pooled_free_run_is_spike_exact(name):
+    """Synapse types of one decay and sign pooled into a channel (as the benchmark runs):
+    the same raster, and the final currents summed over each pool."""
+    drive, p, d, meta = golden_io.load(name, "cuda")
+    engine.POOL_SYNAPSES = True
+    try:
+        run = _run(drive, p, meta, d["in.x"], d["in.v"], d["in.g"], _kw(d, "in."))
+        plan = engine.get_plan(drive, current._fields(p), d["in.x"].shape[0], d["in.x"].shape[2], "cuda")
+    finally:
+        engine.POOL_SYNAPSES = False
+    spikes = run.output.cpu().numpy() > 0.5
+    differs = (spikes != d["out.spikes"]).any(axis=(0, 2))
+    assert not differs.any(), f"first divergence at step {int(np.argmax(differs))}"
+    np.testing.assert_allclose(run.tracked["v"].cpu().numpy(), d["out.v_track"], rtol=V_RTOL, atol=V_ATOL)
+    got, want = run.syn.cpu().numpy(), d["out.g"]
+    for members in plan.ch.member:
+        np.testing.assert_allclose(got[..., members[0]], want[..., members].sum(-1), rtol=I_RTOL, atol=I_ATOL)
 
 
 def test_tracked_currents_and_chunking():

@@ -19,6 +19,10 @@ conductance step reads them a step later). The synaptic input is summed in fixed
 over all pathways (order-independent), where the reference adds pathway after pathway in
 float32.
 
+With ``engine.POOL_SYNAPSES`` (``WIRETORCH_POOL_SYNAPSES=1``), synapse types of the same
+decay and sign share a channel, as in the conductance family: the returned currents then
+hold each pool's sum at its first member type.
+
 The kernel reads the current-based parameters in the conductance fields of ``WtNet``
 (``U_rest`` as ``E_L``, ``R`` as ``C_m``, the types' signs as ``E_syn``; each type a single
 exponential). Gradients flow to the scales, the weights and the input (and, with
@@ -114,7 +118,7 @@ def simulate(
     B, T, n_in = x.shape
     device = x.device
     f = _fields(p)
-    plan = engine.get_plan(drive, f, B, n_in, device, pool=False)
+    plan = engine.get_plan(drive, f, B, n_in, device)  # pooled as engine.POOL_SYNAPSES says
     # the kernel's state (B, 2, S, N) seen as the conductance layout (B, N, 2, S): the
     # currents are the decay component, the rise component zero
     S = plan.ch.Sp
@@ -128,6 +132,7 @@ def simulate(
         run.syn = run.syn[:, :, 1]
         if run.tracked is not None:
             run.tracked["I"] = run.tracked.pop("g")[..., 1, :]
+            run.tracked.pop("I_leak", None)
         return run
     _plan.fold(plan, drive.scale)
     v_k, g_k, counter, g_a, gating_k = engine._prepare_state(plan, v, g, refractory, gating, adaptation, f)
@@ -137,13 +142,13 @@ def simulate(
                                  probabilities=probabilities, track=track, track_b=track_b)  # fmt: skip
     tracked = None
     if track:
-        tracked = {"v": out["track_v"], "I": out["track_g"][..., 1, :]}
+        tracked = {"v": out["track_v"], "I": engine._external_tracked_g(plan, out["track_g"])[..., 1, :]}
         if "track_a" in out:
             tracked["a"] = out["track_a"]
     return Run(
         output=out["spikes"],
         v=v_k,
-        syn=g_k[:, 1].permute(0, 2, 1),
+        syn=engine._external_g(plan, g_k)[:, :, 1],
         probabilities=out.get("prob"),
         tracked=tracked,
         refractory=counter if refractory is not None or p.n_ref is not None else None,

@@ -117,7 +117,10 @@ def _channels(made: torch.Tensor, p, pool: bool) -> Channels:
         mgc = p.mg_c.detach().cpu().float() if p.mg_c is not None else torch.zeros(S)
         mga = p.mg_a.detach().cpu().float() if p.mg_a is not None else torch.zeros(S)
         for s in range(S):
-            poolable = bool(torch.isinf(clip[s])) and float(jr[s]) == -float(jd[s])
+            # a double exponential (jump_r = -jump_d), or a single one (no rise: the
+            # current-based family's currents)
+            single = float(dr[s]) == 0.0 and float(jr[s]) == 0.0
+            poolable = bool(torch.isinf(clip[s])) and (float(jr[s]) == -float(jd[s]) or single)
             key = (
                 (float(dr[s]), float(dd[s]), float(E[s]), float(mgc[s]), float(mga[s]))
                 if poolable
