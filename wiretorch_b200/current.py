@@ -121,7 +121,7 @@ def simulate(
     plan = engine.get_plan(drive, f, B, n_in, device)  # pooled as engine.POOL_SYNAPSES says
     # the kernel's state (B, 2, S, N) seen as the conductance layout (B, N, 2, S): the
     # currents are the decay component, the rise component zero
-    S = plan.ch.Sp
+    S = plan.ch.S  # synapse types (pooled into plan.ch.Sp channels by _internal_g)
     g = torch.zeros((B, v.shape[1], 2, S), device=device)
     g[:, :, 1] = I.detach().to(device, torch.float32)
     if grad:
