@@ -33,3 +33,25 @@ def test_oracle_free_run_matches_reference(name, threads):
         np.testing.assert_allclose(out["prob"], d["out.prob"], rtol=0, atol=1e-5)
     if "rec.spikes" in d:
         assert (out["spikes"] == d["rec.spikes"]).all()
+
+
+def test_c2c_configuration_at_a_tenth():
+    """The current-based C2 configuration (``configs.c2_current``) at a tenth of its
+    neurons with the same in-degrees: each cell type's synapse type carries the type's
+    sign and time constant, the state is the currents (B, N, S), and the oracle's
+    current-based step fires it in the benchmark's range (a few Hz, not silent, not
+    saturated)."""
+    from wiretorch_b200 import configs
+
+    cfg = configs.c2_current(B=2, T=500, device="cpu", N=2000, p_max=0.5)
+    v, I, kw = cfg.state()
+    S = cfg.drive.made.shape[1]
+    assert I.shape == (2, 2000, S) and v.shape == (2, 2000)
+    assert set(cfg.p.sign.tolist()) == {1.0, -1.0} and float(cfg.p.sign[-1]) == 1.0
+    exc = cfg.p.sign > 0
+    np.testing.assert_allclose(cfg.p.decay[exc].numpy(), np.exp(-0.1 / 5.0), rtol=1e-6)
+    np.testing.assert_allclose(cfg.p.decay[~exc].numpy(), np.exp(-0.1 / 10.0), rtol=1e-6)
+    net = oracle.Network(cfg.drive, cfg.p, cfg.B, cfg.n_in)
+    out = net.simulate(cfg.inputs(seed=1), v, I, **kw, track=False)
+    rate = out["spikes"].mean() / 1e-4
+    assert 1.0 < rate < 30.0, rate
