@@ -276,7 +276,7 @@ static_assert(WT_CHUNK_EDGES <= 128, "a chunk's edges take at most four per lane
 // pass, the Mg block, presynaptic gating, adaptation and one rank of a neuron partition
 // known at compile time; everything else (escape noise, probabilities, tracking, saved
 // input) in the generic variant, tested at run time.
-constexpr int kRef = 1, kSave = 2, kGeneric = 4, kMg = 8, kGate = 16, kAdapt = 32, kPart = 64;
+constexpr int kRef = 1, kSave = 2, kGeneric = 4, kMg = 8, kGate = 16, kAdapt = 32, kPart = 64, kCur = 128;
 
 // Warps per block of the forward kernel (one block per SM): 24 for the specialised
 // kernels of up to four channels (80 registers a thread, as good as no spill), WT_GATE_WARPS
@@ -344,7 +344,7 @@ __global__ void __launch_bounds__(warps_of<S, FEAT>() * 32, 1) forward_kernel(co
     // current-based neurons: a step's input enters the currents the same step's membrane
     // update uses, so every warp scatters first and a grid barrier completes X_t before
     // the items read it (the conductance step uses the input a step later)
-    const bool CUR = GEN && (flags & WT_F_CURRENT);
+    const bool CUR = GEN ? (flags & WT_F_CURRENT) != 0 : (FEAT & kCur) != 0;
 
     const int B = net.B, N = net.N, n_in = net.n_in, C = net.C, T = run.T, Np = geo.Np;
     const int Nsrc = net.N_src > 0 ? net.N_src : N;  // neuron sources (all ranks' when partitioned)
@@ -1352,10 +1352,11 @@ static cudaError_t launch_sf(const WtNet &net, const WtForward &run, const WtWor
 // and saving as given; no other feature); everything else runs the generic kernel.
 template <int S>
 static cudaError_t launch_s(const WtNet &net, const WtForward &run, const WtWorkspace &ws, cudaStream_t st) {
-    const int generic = WT_F_SAMPLE | WT_F_PROB | WT_F_TRACK | WT_F_SAVE_INPUT | WT_F_CURRENT;
+    const int generic = WT_F_SAMPLE | WT_F_PROB | WT_F_TRACK | WT_F_SAVE_INPUT;
     const int feat = ((run.flags & WT_F_REFRACTORY) ? kRef : 0) | ((run.flags & WT_F_SAVE) ? kSave : 0) |
                      ((run.flags & WT_F_MG_BLOCK) ? kMg : 0) | ((run.flags & WT_F_GATED) ? kGate : 0) |
-                     ((run.flags & WT_F_ADAPT) ? kAdapt : 0) | ((run.flags & WT_F_PARTITION) ? kPart : 0);
+                     ((run.flags & WT_F_ADAPT) ? kAdapt : 0) | ((run.flags & WT_F_PARTITION) ? kPart : 0) |
+                     ((run.flags & WT_F_CURRENT) ? kCur : 0);
     // the Mg block, gating and adaptation are specialised for forward runs with a
     // refractory period (the large simulations' cases: Mg block and gating in any
     // combination, or adaptation alone), and so are the ranks of a neuron partition;
@@ -1364,6 +1365,13 @@ static cudaError_t launch_s(const WtNet &net, const WtForward &run, const WtWork
     if (S > 4 || (run.flags & generic) || (extra && (feat & (kRef | kSave)) != kRef) ||
         ((extra & kAdapt) && (extra & ~kPart) != kAdapt))
         return launch_sf<S, kGeneric>(net, run, ws, st);
+    if (feat & kCur) {  // current-based neurons: forward runs with a refractory period
+        switch (feat) {
+            case kRef | kCur: return launch_sf<S, kRef | kCur>(net, run, ws, st);
+            case kRef | kSave | kCur: return launch_sf<S, kRef | kSave | kCur>(net, run, ws, st);
+            default: return launch_sf<S, kGeneric>(net, run, ws, st);
+        }
+    }
     if (feat & kPart) {
         switch (feat) {
             case kRef | kPart: return launch_sf<S, kRef | kPart>(net, run, ws, st);
