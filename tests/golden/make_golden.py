@@ -36,7 +36,8 @@ Three more kinds of case:
   and the recurrent one with a refractory period, short-term plasticity and adaptation)
   run through ``network_simulators/current/dynamics.py`` ``simulate``, with the
   reference suite's recordings (``tests/fixtures/current_*.npz``) where there are, and the
-  gradients of a fixed readout with respect to the scale, the weights and the input.
+  gradients of a fixed readout with respect to the scale, the weights, the input and the
+  learnable physiology.
 * ``loss_filter`` / ``loss_van_rossum``: the reference's ``double_exponential``
   (``training_utils/filtering.py:28-73``, its CPU Toeplitz path) and
   ``VanRossumRateLoss`` over three chunks with the filter state carried, with the
@@ -530,10 +531,13 @@ def current_scenarios(networks):
     }  # fmt: skip
 
 
+CURRENT_PHYS_GRADS = ("theta", "U_reset", "beta", "U_rest", "R", "decay", "adapt", "adapt_decay")
+
+
 def current_gradients(dynamics, model, x, probabilities):
     """Gradients of ``sum(spikes R) (+ sum(prob R2))`` over ``GRAD_STEPS`` steps of a
-    current-based network with respect to its scale, weights and input (its physiology
-    fixed), through the recurrent spikes when the network's drive says so (the
+    current-based network with respect to its scale, weights, input and learnable
+    physiology, through the recurrent spikes when the network's drive says so (the
     current-based networks' default)."""
     drive, p = model._drive(), model._physiology()
     v, I, kw = engine_inputs(model)
@@ -550,10 +554,16 @@ def current_gradients(dynamics, model, x, probabilities):
 
     drive.recurrent = [(r, leaf(W)) for r, W in drive.recurrent]
     drive.feedforward = [(r, leaf(W)) for r, W in drive.feedforward]
-    for name in ("theta", "U_reset", "beta", "U_rest", "R", "sign", "decay", "surr_scale", "adapt", "adapt_decay"):
+    for name in ("sign", "surr_scale"):
         value = getattr(p, name)
         if isinstance(value, torch.Tensor):
             setattr(p, name, value.detach())
+    for name in CURRENT_PHYS_GRADS:  # the learnable physiology, made leaves
+        value = getattr(p, name)
+        if isinstance(value, torch.Tensor):
+            value = value.detach().clone().requires_grad_(True)
+            setattr(p, name, value)
+            leaves[f"phys.{name}"] = value
     run = dynamics.simulate(v, I, x, drive, p, probabilities=probabilities, **kw)
     loss = (run.output * readout(READOUT_SEED, run.output.shape)).sum()
     if probabilities:

@@ -11,8 +11,9 @@
   recorded spike raster.
 * **Gradients**: of the reference suite's fixed random readout of the spikes (plus the
   probabilities where the network outputs them) over the first 100 steps, with respect
-  to the scales, the weights and the input, each within 1e-3 of its largest entry;
-  through the recurrent spikes where the network's drive asks (the family's default).
+  to the scales, the weights, the input and the learnable physiology, each within 1e-3 of
+  its largest entry; through the recurrent spikes where the network's drive asks (the
+  family's default).
 
 Voltages are in the family's natural units (reset 0, threshold 1): 1e-5 is a hundred-
 thousandth of the reset-to-threshold gap; the relative 1e-6 (eight float32 ulps) covers
@@ -139,10 +140,10 @@ def test_tracked_currents_and_chunking():
     assert torch.equal(second.v, whole.v)
 
 
-def test_learnt_physiology_is_refused():
+def test_learnt_signs_are_refused():
     drive, p, d, meta = golden_io.load("current_feedforward", "cuda")
-    p.theta = p.theta.clone().requires_grad_(True)
-    with pytest.raises(NotImplementedError, match="physiology"):
+    p.sign = p.sign.clone().float().requires_grad_(True)
+    with pytest.raises(NotImplementedError, match="signs"):
         current.simulate(_t(d["in.v"]), _t(d["in.g"]), _t(d["in.x"]), drive, p)
 
 
@@ -160,10 +161,19 @@ def _leaf(t):
     return t.detach().clone().requires_grad_(True)
 
 
-def _engine_gradients(name, recurrent=None):
+PHYS = ("theta", "U_reset", "beta", "U_rest", "R", "decay", "adapt", "adapt_decay")
+
+
+def _engine_gradients(name, recurrent=None, physiology=False):
     drive, p, d, meta = golden_io.load(name, "cuda")
     if recurrent is not None:
         drive.recurrent_gradients = recurrent
+    phys = {}
+    if physiology:  # the learnable physiology as leaves
+        for key in PHYS:
+            if getattr(p, key) is not None:
+                phys[key] = _leaf(getattr(p, key))
+                setattr(p, key, phys[key])
     T = meta["grad_steps"]
     x = _leaf(_t(d["in.x"][:, :T]))
     drive.scale = _leaf(drive.scale)
@@ -183,6 +193,8 @@ def _engine_gradients(name, recurrent=None):
         loss = loss + (run.probabilities * _readout(meta["readout_seed"] + 2, run.output.shape)).sum()
     loss.backward()
     grads = {"x": x.grad, "scale": drive.scale.grad}
+    for key, t in phys.items():
+        grads[f"phys.{key}"] = t.grad
     seen = []
     for W in [W for _, W in drive.recurrent] + [W for _, W in drive.feedforward]:
         if all(W is not s for s in seen):
@@ -218,6 +230,18 @@ def test_gradients_match_reference(name):
     np.testing.assert_array_equal(spikes.detach().cpu().numpy() > 0.5, d["out.spikes"][:, :T])
     np.testing.assert_allclose(loss, float(d["grad.loss"]), rtol=1e-4, atol=1e-4)
     worst = _worst(grads, d, masks)
+    assert all(w <= TOL for w in worst.values()), worst
+
+
+@pytest.mark.parametrize("name", CASES)
+def test_physiology_gradients_match_reference(name):
+    """With every learnable parameter of the physiology a leaf (threshold, reset, U_rest,
+    R, the leak's and the synapses' decays, the adaptation's rise and decay): all
+    gradients within 1e-3 of their largest entry."""
+    loss, spikes, grads, d, masks = _engine_gradients(name, physiology=True)
+    np.testing.assert_allclose(loss, float(d["grad.loss"]), rtol=1e-4, atol=1e-4)
+    worst = _worst(grads, d, masks)
+    assert any(k.startswith("phys.") for k in worst)
     assert all(w <= TOL for w in worst.values()), worst
 
 

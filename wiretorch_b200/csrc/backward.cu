@@ -51,6 +51,7 @@ __global__ void __launch_bounds__(kBlock, (PHYS || S > 2) ? 1 : 3) backward_kern
     const float g_L = Cm * rate, inv_C = 1.0f / Cm;
     const float a_decay = ADAPT ? net.adapt_decay[n] : 0.0f;
     const float E_a = (ADAPT && !CUR) ? net.E_adapt[n] : 0.0f;
+    const float adapt_n = (ADAPT && CUR) ? net.adapt[n] : 0.0f;
     int in_c[S];
 #pragma unroll
     for (int c = 0; c < S; c++) in_c[c] = net.input_of[c];
@@ -150,7 +151,7 @@ __global__ void __launch_bounds__(kBlock, (PHYS || S > 2) ? 1 : 3) backward_kern
                 }
             }
         }
-        if (SYN && (wants & (WT_W_DECAY | WT_W_JUMP))) {
+        if (SYN && !CUR && (wants & (WT_W_DECAY | WT_W_JUMP))) {
             const float *Xt = bw.X_saved + ((size_t)b * T + t) * C * N + n;
 #pragma unroll
             for (int c = 0; c < S; c++) {
@@ -173,6 +174,34 @@ __global__ void __launch_bounds__(kBlock, (PHYS || S > 2) ? 1 : 3) backward_kern
             // with the membrane of step t already added (so that Q_t above is complete,
             // and the recurrent carry, which reads Q_t from the same state, sees it too).
             const float gx = dv * (1.0f - r);
+            // physiology gradients of step t, from the adjoints entering it (saved: the
+            // currents after the step's input, G, and the adaptation current entering it)
+            if (PHYS) {
+                float Isyn = 0.0f;
+#pragma unroll
+                for (int c = 0; c < S; c++) Isyn = Isyn + G[c] * net.E_syn[c];
+                if (ADAPT) Isyn = Isyn - (cur.ga * a_decay + adapt_n * s);  // - I_a{t+1}
+                const float drive = E_L + Cm * Isyn;  // U_rest + R (sum_j sign_j I_j - I_a)
+                if (wants & WT_W_BETA) acc_beta += gx * (v - drive);
+                if (wants & WT_W_E_L) acc_E_L += gx * (1.0f - beta);
+                if (wants & WT_W_C_M) acc_C_m += gx * (1.0f - beta) * Isyn;
+                if (wants & WT_W_RESET) acc_reset += dv * r;
+                if (ADAPT && (wants & WT_W_ADAPT)) acc_adapt += la * s;
+                if (ADAPT && (wants & WT_W_ADAPT_DECAY)) acc_adapt_decay += la * cur.ga;
+            }
+            if (SYN && (wants & WT_W_DECAY)) {  // I_{t+1} = decay I_t + X_t
+#pragma unroll
+                for (int c = 0; c < S; c++) {
+                    float It;
+                    if (t == 0)
+                        It = bw.g_init[((size_t)b * 2 * S + S + c) * N + n];
+                    else if (t - 1 >= t_lo)
+                        It = q[0].G[c];
+                    else
+                        It = __ldg(G_b + ((size_t)(t - 1) * S + c) * N);
+                    acc_dd[c] += ld[c] * It;
+                }
+            }
             if (ADAPT) la = la * a_decay;  // I_a{t+1} = a_decay I_a{t} + adapt s_t (s detached)
             const float xv = v - theta;
             const float gs = cur.gs + R_b;
@@ -189,6 +218,7 @@ __global__ void __launch_bounds__(kBlock, (PHYS || S > 2) ? 1 : 3) backward_kern
                 g_x += cur.gp * k * p * (1.0f - p);
             }
             if (REF) g_x *= 1.0f - held;
+            acc_theta -= g_x;
             dv = gx * beta + g_x;
 #pragma unroll
             for (int c = 0; c < S; c++) {

@@ -189,8 +189,11 @@ int wt_backward(const WtNet *net, const WtBackward *bw, void *stream) {
     if ((f & WT_F_REFRACTORY) && !bw->held_bits) return fail(WT_ERR_ARGS, "missing refractory bits%s");
     if ((f & WT_F_ADAPT) && (!bw->a_saved || !net->adapt_decay || (!net->E_adapt && !(f & WT_F_CURRENT))))
         return fail(WT_ERR_ARGS, "missing adaptation%s");
-    if ((f & WT_F_CURRENT) && (bw->wants || (f & WT_F_MG_BLOCK)))
-        return fail(WT_ERR_UNSUPPORTED, "current-based neurons: no physiology gradients%s");
+    if ((f & WT_F_CURRENT) && ((bw->wants & (WT_W_E_SYN | WT_W_JUMP | WT_W_E_ADAPT)) || (f & WT_F_MG_BLOCK)))
+        return fail(WT_ERR_UNSUPPORTED, "current-based neurons: no sign, jump or E_adapt gradients%s");
+    if ((f & WT_F_CURRENT) && (f & WT_F_ADAPT) && !net->adapt) return fail(WT_ERR_ARGS, "missing adaptation%s");
+    if ((f & WT_F_CURRENT) && (bw->wants & WT_W_DECAY) && !bw->g_init)
+        return fail(WT_ERR_ARGS, "decay gradients need the currents entering the run%s");
     if ((w & (WT_W_DECAY | WT_W_JUMP)) && !bw->X_saved) return fail(WT_ERR_ARGS, "missing saved input%s");
     if ((w & WT_W_DECAY) && !bw->g_init) return fail(WT_ERR_ARGS, "missing initial conductances%s");
     float *const outs[11] = {bw->g_theta, bw->g_reset, bw->g_E_L, bw->g_C_m, bw->g_beta, bw->g_E_syn,

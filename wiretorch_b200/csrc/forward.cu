@@ -1022,11 +1022,12 @@ __global__ void __launch_bounds__(warps_of<S, FEAT>() * 32, 1) forward_kernel(co
                 s = spike_of(v, k.theta, cnt, u01, sflags, ksur, held);
                 const float rr = fmaxf(s, held);
                 float Gt[S];
-                float I_leak = 0.0f, v_next;
+                float I_leak = 0.0f, v_next, ga_in = ga;
                 if (CUR) {
                     // current-based membrane (current/dynamics.py:116-125, 180-183), float32,
                     // in its order: the adaptation current rises by the spike first, then
                     // v' = (beta v + (1 - beta)(U_rest + R (sum_j sign_j I_j - I_a)))(1 - r) + U r
+                    ga_in = ga;  // I_a{t}, saved for the backward pass
                     if (ADAPT) ga = ga * k.a_decay + k.adapt * s;
                     float Isyn = 0.0f;
 #pragma unroll
@@ -1062,9 +1063,11 @@ __global__ void __launch_bounds__(warps_of<S, FEAT>() * 32, 1) forward_kernel(co
                 if (SAVE) {
                     run.v_saved[out] = v;
                     float *Gs = run.G_saved + (q.bTN + tN) * S + n;
+                    // (current-based: the currents after the step's input, and the
+                    // adaptation current entering the step)
 #pragma unroll
-                    for (int c = 0; c < S; c++) Gs[(size_t)c * N] = gr[c] + gd[c];
-                    if (ADAPT) run.a_saved[out] = ga;
+                    for (int c = 0; c < S; c++) Gs[(size_t)c * N] = CUR ? gd[c] : gr[c] + gd[c];
+                    if (ADAPT) run.a_saved[out] = CUR ? ga_in : ga;
                 }
                 if (REF) {
                     const int c1 = cnt - 1;

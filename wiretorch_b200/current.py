@@ -27,8 +27,10 @@ The kernel reads the current-based parameters in the conductance fields of ``WtN
 (``U_rest`` as ``E_L``, ``R`` as ``C_m``, the types' signs as ``E_syn``; each type a single
 exponential). Gradients flow to the scales, the weights and the input (and, with
 ``Drive.recurrent_gradients``, the current-based networks' default, through the recurrent
-spikes): the backward kernel's current-based adjoint, then the engine's edge gradients. A
-learnt physiology has no gradient here (such a call raises).
+spikes): the backward kernel's current-based adjoint, then the engine's edge gradients;
+and to a learnt physiology (``theta``, ``U_reset``, ``U_rest``, ``R``, ``beta``, the
+synaptic ``decay``, ``adapt``, ``adapt_decay``), from per-(trial, neuron) sums the
+same reverse scan accumulates.
 """
 
 from __future__ import annotations
@@ -70,24 +72,29 @@ _FIELDS: dict = {}
 
 
 def _fields(p) -> _Fields:
+    """The fields of ``p``; the per-neuron tensors are ``p``'s own, so that gradients
+    reach them, and the decays are stacked under autograd when they are learnt (then the
+    fields are built afresh for every call, the stack being part of its graph)."""
+    learnt = torch.is_grad_enabled() and p.decay.requires_grad
     key = id(p)
     hit = _FIELDS.get(key)
-    if hit is not None and hit[0] is p:
+    if not learnt and hit is not None and hit[0] is p:
         return hit[1]
     S = p.sign.shape[0]
     dev = p.sign.device
     zeros = torch.zeros(S, device=dev)
     f = _Fields(
         theta=p.theta, U_reset=p.U_reset, E_L=p.U_rest, C_m=p.R, beta=p.beta,
-        E_syn=p.sign.float(), g_clip=torch.full((S,), float("inf"), device=dev),
-        decay=torch.stack([zeros, p.decay.detach().float()]),
+        E_syn=p.sign.detach().float(), g_clip=torch.full((S,), float("inf"), device=dev),
+        decay=torch.stack([zeros, p.decay.float() if learnt else p.decay.detach().float()]),
         jump=torch.stack([zeros, torch.ones(S, device=dev)]),
         surr_scale=p.surr_scale, spike_mode=p.spike_mode, n_ref=p.n_ref,
         adapt=p.adapt, adapt_decay=p.adapt_decay,
     )  # fmt: skip
-    if len(_FIELDS) > 64:
-        _FIELDS.clear()
-    _FIELDS[key] = (p, f)
+    if not learnt:
+        if len(_FIELDS) > 64:
+            _FIELDS.clear()
+        _FIELDS[key] = (p, f)
     return f
 
 
@@ -108,12 +115,12 @@ def simulate(
     if not x.is_cuda:
         raise RuntimeError("wiretorch_b200 runs on CUDA tensors only (no CPU path)")
     weights = [W for _, W in drive.recurrent] + [W for _, W in drive.feedforward]
-    if torch.is_grad_enabled() and any(
-        isinstance(getattr(p, n, None), torch.Tensor) and getattr(p, n).requires_grad for n in PHYSIOLOGY
-    ):
-        raise NotImplementedError("current-based networks: learnt physiology has no gradient on this engine")
+    learnt = [n for n in PHYSIOLOGY if isinstance(getattr(p, n, None), torch.Tensor) and getattr(p, n).requires_grad]
+    if torch.is_grad_enabled() and getattr(p.sign, "requires_grad", False):
+        raise NotImplementedError("current-based networks: the synapse types' signs are not learnable")
     grad = torch.is_grad_enabled() and (
         drive.scale.requires_grad or x.requires_grad or any(getattr(W, "requires_grad", False) for W in weights)
+        or bool(learnt)
     )
     B, T, n_in = x.shape
     device = x.device
