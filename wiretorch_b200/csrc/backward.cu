@@ -33,7 +33,9 @@ constexpr int kAhead = 3;
 
 // PHYS: some physiology gradient is wanted (else the scan carries only dL/dv, dL/dg and
 // Q); SYN: some synapse parameter's.
-template <int S, bool PHYS, bool SYN>
+// CUR: current-based neurons (WT_F_CURRENT), compiled apart so that the conductance
+// kernels carry none of its code.
+template <int S, bool PHYS, bool SYN, bool CUR>
 __global__ void __launch_bounds__(kBlock, (PHYS || S > 2) ? 1 : 3) backward_kernel(const WtNet net, const WtBackward bw) {
     const int N = net.N, C = net.C, T = bw.T;
     const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
@@ -42,7 +44,6 @@ __global__ void __launch_bounds__(kBlock, (PHYS || S > 2) ? 1 : 3) backward_kern
     const int flags = bw.flags, wants = PHYS ? bw.wants : 0;
     const bool REF = flags & WT_F_REFRACTORY, MG = flags & WT_F_MG_BLOCK, ADAPT = flags & WT_F_ADAPT;
     const bool SAMPLE = flags & WT_F_SAMPLE, PROB = flags & WT_F_PROB;
-    const bool CUR = flags & WT_F_CURRENT;
     const int words = (N + 31) >> 5;
     const float dt = net.dt, k = net.surr_scale;
 
@@ -168,7 +169,7 @@ __global__ void __launch_bounds__(kBlock, (PHYS || S > 2) ? 1 : 3) backward_kern
                 }
             }
         }
-        if (CUR) {
+        if constexpr (CUR) {
             // Current-based step (current/dynamics.py:116-125, 166-183): the adjoint state
             // entering step t is dL/dv_{t+1} and the adjoints of I_{t+1} and I_a{t+1}
             // with the membrane of step t already added (so that Q_t above is complete,
@@ -754,12 +755,21 @@ template <int S>
 cudaError_t launch_bwd_s(const WtNet &net, const WtBackward &bw, cudaStream_t st) {
     const long long items = (long long)net.B * net.N;
     const int blocks = (int)((items + kBlock - 1) / kBlock);
-    if (bw.wants & (WT_W_E_SYN | WT_W_DECAY | WT_W_JUMP))
-        backward_kernel<S, true, true><<<blocks, kBlock, 0, st>>>(net, bw);
-    else if (bw.wants)
-        backward_kernel<S, true, false><<<blocks, kBlock, 0, st>>>(net, bw);
-    else
-        backward_kernel<S, false, false><<<blocks, kBlock, 0, st>>>(net, bw);
+    const bool syn = bw.wants & (WT_W_E_SYN | WT_W_DECAY | WT_W_JUMP);
+    if (bw.flags & WT_F_CURRENT) {
+        if (syn)
+            backward_kernel<S, true, true, true><<<blocks, kBlock, 0, st>>>(net, bw);
+        else if (bw.wants)
+            backward_kernel<S, true, false, true><<<blocks, kBlock, 0, st>>>(net, bw);
+        else
+            backward_kernel<S, false, false, true><<<blocks, kBlock, 0, st>>>(net, bw);
+    } else if (syn) {
+        backward_kernel<S, true, true, false><<<blocks, kBlock, 0, st>>>(net, bw);
+    } else if (bw.wants) {
+        backward_kernel<S, true, false, false><<<blocks, kBlock, 0, st>>>(net, bw);
+    } else {
+        backward_kernel<S, false, false, false><<<blocks, kBlock, 0, st>>>(net, bw);
+    }
     return cudaGetLastError();
 }
 
