@@ -250,3 +250,24 @@ def test_recurrent_carry_matters():
     miss the reference's by far more than the tolerance."""
     _, _, grads, d, masks = _engine_gradients("current_recurrent", recurrent=False)
     assert max(_worst(grads, d, masks, weights=False).values()) > 10 * TOL
+
+
+def test_specialised_kernels_match_the_generic_one():
+    """Current-based runs with a refractory period take kernels with the mode compiled in
+    (forward, and forward saving for the backward pass); tracking sends the same run
+    through the generic kernel. All three give identical spikes and state, bit for bit."""
+    drive, p, d, meta = golden_io.load("current_recurrent", "cuda")
+    p.n_ref = torch.full_like(p.theta, 20, dtype=torch.int32)
+    kw = {"refractory": torch.zeros(p.theta.shape[0], dtype=torch.int32, device="cuda").expand(2, -1).contiguous()}
+    x, v, I = _t(d["in.x"]), _t(d["in.v"]), _t(d["in.g"])
+    with torch.no_grad():
+        fast = current.simulate(v, I, x, drive, p, **kw)
+        generic = current.simulate(v, I, x, drive, p, **kw, track=True)
+    drive.scale = drive.scale.clone().requires_grad_(True)  # saving for the backward pass
+    saving = current.simulate(v, I, x, drive, p, **kw)
+    saving.output.sum().backward()
+    assert float(fast.output.sum()) > 20
+    for run in (generic, saving):
+        for name in ("output", "v", "syn", "refractory"):
+            assert torch.equal(getattr(fast, name).detach(), getattr(run, name).detach()), name
+    assert drive.scale.grad is not None and torch.isfinite(drive.scale.grad).all()
