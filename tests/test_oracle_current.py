@@ -55,3 +55,25 @@ def test_c2c_configuration_at_a_tenth():
     out = net.simulate(cfg.inputs(seed=1), v, I, **kw, track=False)
     rate = out["spikes"].mean() / 1e-4
     assert 1.0 < rate < 30.0, rate
+
+
+def test_field_mapping_follows_the_physiology():
+    """The current-based physiology as the kernel's fields: U_rest as E_L, R as C_m, the
+    signs as E_syn, each type a decay component with a unit jump; cached per physiology
+    and its tensors, so that a field replaced on the same object is seen."""
+    import torch
+
+    from wiretorch_b200 import current
+    from wiretorch_b200.types import CurrentPhysiology
+
+    N = 4
+    p = CurrentPhysiology(theta=torch.ones(N), U_reset=torch.zeros(N), beta=torch.full((N,), 0.9),
+                          U_rest=torch.full((N,), 0.1), R=torch.full((N,), 2.0), sign=torch.tensor([1.0, -1.0]),
+                          decay=torch.tensor([0.9, 0.8]), surr_scale=torch.tensor(5.0))  # fmt: skip
+    f = current._fields(p)
+    assert f.E_L is p.U_rest and f.C_m is p.R and f.beta is p.beta and f.current
+    assert torch.equal(f.E_syn, p.sign) and torch.equal(f.decay[1], p.decay) and not f.decay[0].any()
+    assert torch.equal(f.jump, torch.tensor([[0.0, 0.0], [1.0, 1.0]]))
+    assert current._fields(p) is f
+    p.theta = torch.full((N,), 2.0)
+    assert current._fields(p).theta is p.theta

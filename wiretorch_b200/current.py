@@ -69,6 +69,8 @@ class _Fields:
 
 
 _FIELDS: dict = {}
+_SOURCE_FIELDS = ("theta", "U_reset", "U_rest", "R", "beta", "sign", "decay", "surr_scale", "n_ref", "adapt",
+                  "adapt_decay")  # fmt: skip
 
 
 def _fields(p) -> _Fields:
@@ -76,9 +78,11 @@ def _fields(p) -> _Fields:
     reach them, and the decays are stacked under autograd when they are learnt (then the
     fields are built afresh for every call, the stack being part of its graph)."""
     learnt = torch.is_grad_enabled() and p.decay.requires_grad
-    key = id(p)
+    # cached per physiology object and its very tensors (a field replaced is a new entry)
+    parts = tuple(getattr(p, n) for n in _SOURCE_FIELDS)
+    key = (id(p), *map(id, parts))
     hit = _FIELDS.get(key)
-    if not learnt and hit is not None and hit[0] is p:
+    if not learnt and hit is not None and all(a is b for a, b in zip(hit[0], (p, *parts))):
         return hit[1]
     S = p.sign.shape[0]
     dev = p.sign.device
@@ -94,7 +98,7 @@ def _fields(p) -> _Fields:
     if not learnt:
         if len(_FIELDS) > 64:
             _FIELDS.clear()
-        _FIELDS[key] = (p, f)
+        _FIELDS[key] = ((p, *parts), f)
     return f
 
 
