@@ -5,8 +5,8 @@
 
 For N > 1 run one process per GPU (``torch.distributed.run``); ranks talk over NCCL.
 
-Workload (``--config c5``, the default: the largest configuration): BASELINE
-configuration 5 — 1,000,000 conductance-LIF neurons with ~1B edges from a
+Workload (``--config c5``, the default: the largest configuration): benchmark
+configuration C5 — 1,000,000 conductance-LIF neurons with ~1B edges from a
 distance-dependent model, AMPA + NMDA (Mg block) + GABA_A, short-term depression,
 refractoriness, 4 trials, T=5,000 steps of 0.1 ms, forward, run as engine calls of 1,000
 steps with the state carried. One step is one such 5,000-step simulation. At N = 1 it
@@ -20,7 +20,8 @@ learnt per-type-pair scales, 64 trials per GPU, T=500: forward through the engin
 against filtered target rates), backpropagation through time to the 41x40 scales, the
 gradients' all-reduce across ranks and an SGD update (gradient norm clipped at 1); every
 rank simulates its own 64 trials (trial-batch sharding, weak scaling). ``--config c1 /
-c3 / c4``: the other configurations, forward.
+c3 / c4``: the other configurations, forward. ``--config c2c``: the current-based family
+(``wiretorch_b200.current``) on configuration 2's network, forward.
 
 ``value``: neuron-steps per second of the whole job (trials x neurons x time steps of
 the work all ranks did / the slowest rank's device time). ``synaptic_events_per_s``:
@@ -28,13 +29,14 @@ edges traversed by recurrent spikes per second (counted on the device over one e
 untimed step and multiplied by the steps timed), input events separately.
 ``roofline``: the dominant kernel's algorithmic bytes per launch / its CUDA-event
 duration against the measured HBM copy bandwidth. ``e2e``: the same step through the
-public API fed from pinned host memory (the spike input as bytes, and the target rates
-for c2), each step's (or engine call's) input copied on a second stream while the
+public API fed from pinned host memory (the spike input as bits, unpacked on the
+device by ``wiretorch_b200.chunks``, and the target rates for c2), each step's (or engine call's) input copied on a second stream while the
 previous one computes, and its result (spike count, or loss and learnt parameters)
 read back. ``cpu_baseline``: the oracle (the C restatement of the reference's time
 loop) on a bounded sample of the same network on the host cores. ``--impl reference``
-times that CPU implementation alone (and, for c1 / c2 where the reference's package is
-installed under ``baseline/_ref``, the reference's own ``dynamics.simulate``).
+times that CPU implementation alone (and, for c1 / c2 / c2c where the reference's
+package is installed under ``baseline/_ref``, the reference's own ``dynamics.simulate``
+of the family).
 """
 
 from __future__ import annotations

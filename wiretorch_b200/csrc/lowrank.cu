@@ -1,5 +1,5 @@
 // The factorised (low-rank) recurrent drive on the tensor cores. A pathway k whose weights
-// are W_k = U_k V^T (rank r <= 64; the BASELINE's factorised configuration, a linear
+// are W_k = U_k V^T (rank r <= 64; the benchmark's factorised configuration C3, a linear
 // low-rank product, where wiretorch's LowRankProjection, projections.py:167-216, assembles
 // a dense W every forward, network.py:731-752) drives neuron n of trial b with
 //
