@@ -2,8 +2,9 @@
 // spike i of a row in bit i % 8 (least significant first) of byte i / 8. The runners'
 // data path moves spikes between host and device in this form (an eighth of a bool
 // tensor's bytes, a thirty-second of a float's) and these kernels convert on the device:
-// one thread per packed byte, its eight spikes read or written with vector accesses when
-// the rows keep them aligned. Both are bound by the HBM bytes of the unpacked side.
+// one thread per packed byte (per half byte when unpacking to float), its spikes read or
+// written with vector accesses when the rows keep them aligned. Both are bound by the HBM
+// bytes of the unpacked side.
 #include "common.cuh"
 
 namespace wt {
@@ -42,6 +43,27 @@ __global__ void unpack_kernel(const uint8_t *__restrict__ bits, T *__restrict__ 
             }
         } else {
             for (int k = 0; k < m; k++) o[k] = (T)((byte >> k) & 1u);
+        }
+    }
+}
+
+// bits -> float spikes, a thread per half byte: its four spikes one 16-byte store when the
+// rows keep them aligned, so that a warp's stores cover 512 contiguous bytes
+__global__ void unpack_f32_kernel(const uint8_t *__restrict__ bits, float *__restrict__ out, long long rows, int n,
+                                  bool vec) {
+    const int nb = (n + 7) >> 3, nq = (n + 3) >> 2;  // bytes and half bytes of a row
+    const long long total = rows * nq;
+    for (long long i = grid_index(); i < total; i += grid_threads()) {
+        const long long row = i / nq;
+        const int jq = (int)(i - row * nq);
+        const unsigned q = (bits[row * nb + (jq >> 1)] >> ((jq & 1) * 4)) & 15u;
+        float *o = out + row * n + (long long)jq * 4;
+        const int m = min(4, n - jq * 4);
+        if (vec && m == 4) {
+            *reinterpret_cast<float4 *>(o) =
+                make_float4((float)(q & 1u), (float)((q >> 1) & 1u), (float)((q >> 2) & 1u), (float)((q >> 3) & 1u));
+        } else {
+            for (int k = 0; k < m; k++) o[k] = (float)((q >> k) & 1u);
         }
     }
 }
@@ -98,9 +120,9 @@ int grid_for(long long total) {
     return (int)(want < 1 ? 1 : want > cap ? cap : want);
 }
 
-// Whether each byte's eight spikes sit at one aligned vector: a float row of a multiple
-// of 4 spikes from a 16-byte-aligned base (two 16-byte accesses), a uint8 row of a
-// multiple of 8 from an 8-byte-aligned base (one 8-byte access).
+// Whether the spikes sit at aligned vectors: a float row of a multiple of 4 spikes from a
+// 16-byte-aligned base (16-byte accesses), a uint8 row of a multiple of 8 from an
+// 8-byte-aligned base (one 8-byte access per byte of bits).
 bool vector_rows(const WtSpikeBits &a) {
     const uintptr_t base = (uintptr_t)a.spikes;
     return a.kind == WT_SPIKES_F32 ? (a.n % 4 == 0 && base % 16 == 0) : (a.n % 8 == 0 && base % 8 == 0);
@@ -111,12 +133,12 @@ bool vector_rows(const WtSpikeBits &a) {
 cudaError_t launch_unpack_spikes(const WtSpikeBits &a, cudaStream_t st) {
     const long long total = a.rows * (long long)((a.n + 7) / 8);
     if (total == 0) return cudaSuccess;
-    const int grid = grid_for(total);
     const bool vec = vector_rows(a);
     if (a.kind == WT_SPIKES_F32)
-        unpack_kernel<float><<<grid, 256, 0, st>>>(a.bits, (float *)a.spikes, a.rows, a.n, vec);
+        unpack_f32_kernel<<<grid_for(a.rows * (long long)((a.n + 3) / 4)), 256, 0, st>>>(a.bits, (float *)a.spikes,
+                                                                                        a.rows, a.n, vec);
     else
-        unpack_kernel<uint8_t><<<grid, 256, 0, st>>>(a.bits, (uint8_t *)a.spikes, a.rows, a.n, vec);
+        unpack_kernel<uint8_t><<<grid_for(total), 256, 0, st>>>(a.bits, (uint8_t *)a.spikes, a.rows, a.n, vec);
     return cudaGetLastError();
 }
 
