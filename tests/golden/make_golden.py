@@ -38,6 +38,11 @@ Three more kinds of case:
   reference suite's recordings (``tests/fixtures/current_*.npz``) where there are, and the
   gradients of a fixed readout with respect to the scale, the weights, the input and the
   learnable physiology.
+* ``curstats_recurrent`` / ``curstats_feedforward``: the current-based networks of the
+  reference's statistics test (``STATS_NETWORKS["current_*"]``, 2,000 and 1,000 neurons),
+  their inputs, the rates (and feedforward spikes) recorded in
+  ``tests/fixtures/statistics_current.npz``, and a run of the reference's current-based
+  dynamics here.
 * ``loss_filter`` / ``loss_van_rossum``: the reference's ``double_exponential``
   (``training_utils/filtering.py:28-73``, its CPU Toeplitz path) and
   ``VanRossumRateLoss`` over three chunks with the filter state carried, with the
@@ -462,6 +467,59 @@ def make_statistics_case(name, reference, networks, dynamics):
           f"{(HERE / f'{name}.npz').stat().st_size / 1e6:.2f} MB")
 
 
+def make_current_statistics_case(name, reference, networks):
+    """``curstats_<net>``: the current-based network of the reference's
+    ``STATS_NETWORKS["current_<net>"]`` with both recorded inputs, the rates the
+    reference recorded for it (``statistics_current.npz``, from its PyTorch
+    current-based dynamics) and a run of the same dynamics here on the first input."""
+    from wiretorch.network_simulators.current import dynamics as current_dynamics
+
+    sys.path.insert(0, str(reference / "tests" / "fixtures"))
+    import generate
+
+    net = "current_" + name.removeprefix("curstats_")
+    builder, kwargs, n_steps = generate.STATS_NETWORKS[net]
+    seeds = generate.STATS_INPUT_SEEDS
+    builts = [builder(generate.STATS_BATCH, networks.SEED, n_steps=n_steps, input_seed=s, **kwargs) for s in seeds]
+    model = builts[0].model
+    drive, p = model._drive(), model._physiology()
+    v, I, kw = engine_inputs(model)
+    sparse = {}
+
+    def sp(W):
+        if id(W) not in sparse:
+            sparse[id(W)] = sparse_of(W)
+        return sparse[id(W)]
+
+    from wiretorch_b200.types import Drive as WtDrive
+
+    saved = WtDrive(made=drive.made, scale=drive.scale, recurrent=[(r, sp(W)) for r, W in drive.recurrent],
+                    feedforward=[(r, sp(W)) for r, W in drive.feedforward], gates=list(drive.gates or []),
+                    recurrent_gradients=bool(drive.recurrent_gradients))  # fmt: skip
+    xs = [torch.from_numpy(b.input_spikes).float() for b in builts]
+    spikes, _, _, _, _ = reference_free_run(current_dynamics, drive, p, xs[0], v, I, kw, 250)
+    with np.load(reference / "tests" / "fixtures" / "statistics_current.npz") as rec:
+        recorded = {f"rates_{s}": rec[f"{net}.rates.{s}"] for s in seeds}
+        recorded.update({f"population_rate_{s}": rec[f"{net}.population_rate.{s}"] for s in seeds})
+        if f"{net}.spikes.bits" in rec.files:
+            shape = tuple(rec[f"{net}.spikes.shape"])
+            recorded["spikes"] = np.unpackbits(rec[f"{net}.spikes.bits"], axis=-1, count=shape[-1]).astype(bool)
+    types = builts[0].structure["types"]
+    inputs = {"v": v, "g": I, **kw, "types": torch.from_numpy(np.asarray(types))}
+    for s, x in zip(seeds, xs):
+        inputs[f"x_{s}"] = x
+    meta = dict(case=name, batch=generate.STATS_BATCH, steps=n_steps, burn_in=generate.STATS_BURN_IN,
+                chunk=250, seeds=list(seeds), x_bits=True, n_in=int(xs[0].shape[2]), family="current",
+                dt=float(networks.DT),
+                origin=f"reference tests/fixtures/generate.py STATS_NETWORKS[{net!r}] and statistics_current.npz")  # fmt: skip
+    golden_io.save(HERE / f"{name}.npz", drive=saved, p=p, inputs=inputs,
+                   outputs={"spikes": spikes[:, generate.STATS_BURN_IN :]}, grads={}, recorded=recorded,
+                   meta=meta)  # fmt: skip
+    rates = spikes[:, generate.STATS_BURN_IN :].float().mean((0, 1)) * 1000.0 / float(networks.DT)
+    print(f"{name}: CPU reference {float(rates.mean()):.2f} Hz, recorded {recorded[f'rates_{seeds[0]}'].mean():.2f} Hz, "
+          f"{(HERE / f'{name}.npz').stat().st_size / 1e6:.2f} MB")
+
+
 # ---------------------------------------------------------------------------------------
 # The loss filter and the van Rossum rate loss
 # ---------------------------------------------------------------------------------------
@@ -618,10 +676,13 @@ def main():
     configs_ = config_builders()
     stats = ["statistics_recurrent", "statistics_feedforward"]
     current = current_scenarios(networks)
-    todo = args.names or [*cases, "recurrent_gradients", *configs_, *stats, "loss", *current]
+    curstats = ["curstats_recurrent", "curstats_feedforward"]
+    todo = args.names or [*cases, "recurrent_gradients", *configs_, *stats, "loss", *current, *curstats]
     for name in todo:
         if name in current:
             make_current_case(name, current[name], reference)
+        elif name in curstats:
+            make_current_statistics_case(name, reference, networks)
         elif name in configs_:
             make_config_case(name, *configs_[name], dynamics)
         elif name in stats:

@@ -170,12 +170,17 @@ def load(name: str, device="cpu"):
     return drive, p, data, meta
 
 
-KINDS = ("config_", "statistics_", "loss_", "current_")
+KINDS = ("config_", "statistics_", "loss_", "current_", "curstats_")
 
 
 def cases() -> list[str]:
     """The scenario cases (one engine call of a reference test network each)."""
     return sorted(p.stem for p in GOLDEN.glob("*.npz") if not p.stem.startswith(KINDS))
+
+
+def curstats_cases() -> list[str]:
+    """The reference's at-scale statistics networks of the current-based family."""
+    return sorted(p.stem for p in GOLDEN.glob("curstats_*.npz"))
 
 
 def current_cases() -> list[str]:

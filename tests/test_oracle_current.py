@@ -77,3 +77,56 @@ def test_field_mapping_follows_the_physiology():
     assert current._fields(p) is f
     p.theta = torch.full((N,), 2.0)
     assert current._fields(p).theta is p.theta
+
+
+# ---- at the reference's statistics scale (2,000 and 1,000 neurons, 3,000 / 2,000 steps) ----
+
+
+def _curstats_run(name):
+    """The oracle's free run of a ``curstats_*`` case's first input in 250-step calls (the
+    state carried), after the burn-in; and the case."""
+    drive, p, d, meta = golden_io.load(name)
+    A = meta["seeds"][0]
+    x = d[f"in.x_{A}"]
+    oracle.set_threads(4)
+    try:
+        net = oracle.Network(drive, p, x.shape[0], x.shape[2])
+        v, g = d["in.v"], d["in.g"]
+        kw = {k: d[f"in.{k}"] for k in ("refractory", "gating", "adaptation") if f"in.{k}" in d}
+        spikes = []
+        for start in range(0, x.shape[1], meta["chunk"]):
+            out = net.simulate(x[:, start : start + meta["chunk"]], v, g, **kw, track=False)
+            spikes.append(out["spikes"])
+            v, g = out["v"], out["g"]
+            kw = {k: (out[k] if out[k] is not None else kw[k]) for k in kw}
+    finally:
+        oracle.set_threads(1)
+    return np.concatenate(spikes, 1)[:, meta["burn_in"] :], d, meta
+
+
+def test_oracle_current_statistics_recurrent():
+    """The current-based recurrent network of the reference's statistics test: per-type
+    population rates within the reference's own tolerance (twice the spread between its
+    two recorded inputs, at least 2%) of its recording, and the raster of the reference's
+    CPU run of the same input reproduced spike for spike (4 trials x 2,000 neurons x 2,500
+    steps after the burn-in)."""
+    spikes, d, meta = _curstats_run("curstats_recurrent")
+    types = d["in.types"]
+    A, B = meta["seeds"]
+    means = golden_io.population_rates(spikes, types, meta["dt"])
+    rec_a, rec_b = d[f"rec.rates_{A}"], d[f"rec.rates_{B}"]
+    ref = np.array([rec_a[types == t].mean() for t in np.unique(types)])
+    ref_b = np.array([rec_b[types == t].mean() for t in np.unique(types)])
+    allowed = np.maximum(2 * np.abs(ref_b - ref), 0.02 * ref)
+    assert np.all(np.abs(means - ref) <= allowed), (means, ref, allowed)
+    cpu_means = golden_io.population_rates(d["out.spikes"], types, meta["dt"])
+    assert np.all(np.abs(means - cpu_means) <= allowed)
+    assert (spikes == d["out.spikes"]).all()
+
+
+def test_oracle_current_statistics_feedforward():
+    """The current-based feedforward network: the reference's recorded raster, and its CPU
+    run here, reproduced spike for spike (4 trials x 1,000 neurons x 1,500 steps)."""
+    spikes, d, meta = _curstats_run("curstats_feedforward")
+    assert (spikes == d["rec.spikes"]).all()
+    assert (spikes == d["out.spikes"]).all()
