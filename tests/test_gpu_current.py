@@ -271,3 +271,32 @@ def test_specialised_kernels_match_the_generic_one():
         for name in ("output", "v", "syn", "refractory"):
             assert torch.equal(getattr(fast, name).detach(), getattr(run, name).detach()), name
     assert drive.scale.grad is not None and torch.isfinite(drive.scale.grad).all()
+
+
+@pytest.mark.parametrize("name", golden_io.curstats_cases())
+def test_statistics_scale_rates_match_reference(name):
+    """The reference's current-based statistics networks (2,000 and 1,000 neurons, 2,500 /
+    1,500 steps after the burn-in, 250-step calls with the state carried): per-type
+    population rates within the reference's own tolerance (twice the spread between its
+    two recorded inputs, at least 2%) of its recording and of its CPU run."""
+    drive, p, d, meta = golden_io.load(name, "cuda")
+    A, B = meta["seeds"]
+    x = _t(d[f"in.x_{A}"])
+    v, I = _t(d["in.v"]), _t(d["in.g"])
+    kw = {k: _t(d[f"in.{k}"]) for k in ("refractory", "gating", "adaptation") if f"in.{k}" in d}
+    out = []
+    with torch.no_grad():
+        for start in range(0, x.shape[1], meta["chunk"]):
+            run = current.simulate(v, I, x[:, start : start + meta["chunk"]], drive, p, **kw)
+            out.append(run.output)
+            v, I = run.v, run.syn
+            kw = {k: getattr(run, k) for k in kw}
+    spikes = torch.cat(out, 1)[:, meta["burn_in"] :].cpu().numpy() > 0.5
+    types = d["in.types"]
+    means = golden_io.population_rates(spikes, types, meta["dt"])
+    ref = np.array([d[f"rec.rates_{A}"][types == t].mean() for t in np.unique(types)])
+    ref_b = np.array([d[f"rec.rates_{B}"][types == t].mean() for t in np.unique(types)])
+    allowed = np.maximum(2 * np.abs(ref_b - ref), 0.02 * ref)
+    assert np.all(np.abs(means - ref) <= allowed), (means, ref, allowed)
+    cpu = golden_io.population_rates(d["out.spikes"], types, meta["dt"])
+    assert np.all(np.abs(means - cpu) <= allowed), (means, cpu, allowed)
