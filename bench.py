@@ -461,9 +461,10 @@ def _to_cpu(cfg):
 def run_reference(args, rank, world):
     """``--impl reference``: the CPU implementation of the path on the host cores, rank 0
     only: the oracle (the C restatement of the reference's time loop, forward only), each
-    step a bounded sample of the configuration's trials and steps; for c1 / c2 also the
-    reference's own ``dynamics.simulate`` when its package is installed under
-    ``baseline/_ref`` (a bounded sample too)."""
+    step a bounded sample of the configuration's trials and steps; for c1 / c2 / c2c also
+    the reference's own ``dynamics.simulate`` when its package is installed under
+    ``baseline/_ref`` (a bounded sample too; for c2 also its training step, forward +
+    BPTT + loss, at a reduced number of steps)."""
     if rank != 0:
         return
     device = "cuda" if torch.cuda.is_available() else "cpu"
@@ -550,9 +551,53 @@ def reference_dynamics_baseline(args, cfg):
     el = timed(T)
     T = int(min(cfg.T, max(T, T * 15.0 / max(el, 1e-3))))
     el = timed(T)
-    return {"value": cfg.B * cfg.N * T / el, "unit": "neuron-steps/s", "cores": threads,
-            "kind": "reference", "sample": f"{cfg.B} trials x {T} steps of the {cfg.name} network, forward only, "
-                                            f"dense weights ({el:.1f} s)"}  # fmt: skip
+    out = {"value": cfg.B * cfg.N * T / el, "unit": "neuron-steps/s", "cores": threads,
+           "kind": "reference", "sample": f"{cfg.B} trials x {T} steps of the {cfg.name} network, forward only, "
+                                           f"dense weights ({el:.1f} s)"}  # fmt: skip
+    if cfg.name == "c2":  # the benchmarked workload itself: forward + BPTT + loss, at reduced T
+        try:
+            from wiretorch.training_utils import losses as ref_losses
+        except Exception as e:  # noqa: BLE001
+            out["training"] = {"unavailable": f"importing the reference's losses failed: {type(e).__name__}: {e}"}
+        else:
+            out["training"] = _reference_training(ref_dyn, ref_losses, drive, p, cfg, cpu, v, g, kw, threads)
+    return out
+
+
+def _reference_training(ref_dyn, ref_losses, drive, p, cfg, cpu, v, g, kw, threads, seconds=15.0):
+    """The reference's own C2 training step on the host cores at a reduced number of
+    steps: its ``dynamics.simulate`` with autograd (dense weights), its
+    ``VanRossumRateLoss`` (``training_utils/losses.py:140-194``) against the target rates,
+    and the backward pass to the learnt per-type-pair log scales (the optimiser's step
+    is negligible beside them)."""
+    import copy
+
+    B, N = cfg.B, cfg.N
+    types = cpu.types.cpu()
+    target = cpu.extra["target_rates"] * (DT / 1000.0)
+
+    def timed(T):
+        x = cfg.inputs(T=T, seed=99).cpu()
+        log_sf = torch.zeros(cfg.extra["log_sf_shape"], requires_grad=True)
+        d = copy.copy(drive)
+        loss_fn = ref_losses.VanRossumRateLoss(DT, 20.0, DT, T)
+        t0 = time.perf_counter()
+        d.scale = torch.exp(log_sf)[:, types]
+        run = ref_dyn.simulate(v, g, x, d, p, **kw)
+        loss = loss_fn(target[:, None, :].expand(B, T, N), output_spikes=run.output)
+        loss.backward()
+        return time.perf_counter() - t0
+
+    # (from rest the spikes depend on the scales from the third step on: a conductance step
+    # uses the input a step later)
+    timed(3)  # warm-up
+    T = 4
+    el = timed(T)
+    T = int(min(cfg.T, max(T, T * seconds / max(el, 1e-3))))
+    el = timed(T)
+    return {"value": B * N * T / el, "unit": "neuron-steps/s", "cores": threads, "kind": "reference",
+            "sample": f"{B} trials x {T} steps of the c2 network, forward + BPTT + van Rossum rate loss, dense "
+                      f"weights, autograd ({el:.1f} s)"}  # fmt: skip
 
 
 def config_of(args, cfg, world):
